@@ -1,0 +1,467 @@
+"""Benchmark of the per-layer decode step of the hot/cold KV path.
+
+Workload (BASELINE configs[1] geometry): Llama-3.1-8B attention shapes (32 query /
+8 KV heads, head_dim 128, fp16), 32 layers, batch 1, an 8192-token prompt per
+layer compressed to a budget of 512 with the evicted tokens in the HBM cold
+store, retrieval of the top 64 every 16 steps, held until replaced. The
+pre-RoPE q/k/v of every layer and step are seeded N(0,1) draws resident in HBM
+(no weights or dataset exist here; the hot path's cost does not depend on the
+values). Default eviction policy: SnapKV scoring (window 32, max-pool 7), which
+evicts one token into the cold store every decode step, so each step runs
+attention + eviction + (every 16th step) cold top-k and re-RoPE inject.
+
+One step = one decode step through all layers. Every timed step is captured as
+a CUDA graph right before it is replayed (capture is outside the timed region),
+L2 is flushed before each replay, and each replay is bracketed by CUDA events
+on the launching stream. value = device time / layer-steps (us per layer-step,
+lower is better), max over ranks at N > 1 (each rank runs its own replica).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode-step µs/layer (attn+evict+cold top-k) at 8k ctx; HBM GB/s vs peak"
+UNIT = "us/layer-step"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=32)
+    p.add_argument("--warmup", type=int, default=16)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--policy", default="snapkv", choices=["snapkv", "hotcold"])
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--prompt", type=int, default=8192)
+    p.add_argument("--budget", type=int, default=512)
+    p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--cpu-steps", type=int, default=16)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def config(a):
+    recent = 32 if a.policy == "snapkv" else 128
+    ratio = 0.0 if a.policy == "snapkv" else max(0.05, 0.75 - recent / a.budget)  # run_baselines.py:86-87
+    return dict(Hq=32, Hk=8, D=128, theta=500000.0, layers=a.layers, prompt=a.prompt, budget=a.budget,
+                policy=a.policy, recent=recent, topk_ratio=ratio, pool_kernel=7, ccap=32768, faiss_dim=128,
+                window_size=16, query_pool_size=4, lookahead_k=64, hold=True, dtype="float16")
+
+
+def workload_config(c, extra=None):
+    d = {"workload": "llama3.1-8b-geometry hot/cold decode step, 32 layers, 8k prompt, budget 512",
+         "layers": c["layers"], "prompt_tokens": c["prompt"], "budget": c["budget"], "policy": c["policy"],
+         "recent": c["recent"], "lookahead_k": c["lookahead_k"], "retrieval_every": c["window_size"],
+         "hold_retrieved": c["hold"], "cold_ring": c["ccap"], "batch": 1, "heads": "32q/8kv", "head_dim": 128,
+         "l2": "flushed (256 MiB write) before every timed step"}
+    if extra:
+        d.update(extra)
+    return d
+
+
+# ------------------------------------------------------------------------------------------
+# clocks
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str | None):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.gpu_id is not None:
+            cmd += ["-i", self.gpu_id]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r.split(", ") for r in self.lines if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "traffic.md")
+    try:
+        for line in open(path):
+            if line.startswith(f"traffic[{kernel}]"):
+                return int(float(line.split("=", 1)[1].split()[0]))
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------
+class Workload:
+    """32 layers of prompt + decode inputs in HBM and the controller holding their state."""
+
+    def __init__(self, c, steps, seed, device):
+        import torch
+        from transformers import LlamaConfig
+        from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding, apply_rotary_pos_emb
+
+        from hotcold_kv_cache_b200 import KVController
+        self.torch = torch
+        self.c, self.dev = c, device
+        L, T, Hq, Hk, D = c["layers"], c["prompt"], c["Hq"], c["Hk"], c["D"]
+        dt = torch.float16
+        g = torch.Generator(device=device).manual_seed(seed)
+        cfg = LlamaConfig(hidden_size=Hq * D, num_attention_heads=Hq, num_key_value_heads=Hk, head_dim=D,
+                          num_hidden_layers=L, rope_theta=c["theta"], vocab_size=16, intermediate_size=16,
+                          max_position_embeddings=1 << 17)
+        self.rot = LlamaRotaryEmbedding(cfg).to(device)
+        self.ctrl = KVController(max_capacity_prompt=c["budget"], topk_ratio=c["topk_ratio"],
+                                 recent_size=c["recent"], cpu_buffer_size=c["ccap"], faiss_dim=c["faiss_dim"],
+                                 window_size=c["window_size"], query_pool_size=c["query_pool_size"],
+                                 lookahead_k=c["lookahead_k"], hold_retrieved=c["hold"],
+                                 retrieve_after_prefill=False, policy=c["policy"], pool_kernel=c["pool_kernel"],
+                                 profile_overlap=False)
+        self.ctrl.set_rotary(self.rot.inv_freq, self.rot.attention_scaling)
+        pos = torch.arange(T, device=device)[None]
+        cos, sin = self.rot(torch.empty(1, dtype=dt, device=device), pos)
+        for li in range(L):
+            q = torch.randn((1, Hq, T, D), generator=g, device=device, dtype=dt)
+            k = torch.randn((1, Hk, T, D), generator=g, device=device, dtype=dt)
+            v = torch.randn((1, Hk, T, D), generator=g, device=device, dtype=dt)
+            if li == 0:
+                self.ctrl._lazy_init(k, n_layers=L)
+            qp, kp = apply_rotary_pos_emb(q, k, cos, sin)
+            self.ctrl.prefill_layer(li, q, qp, k, kp, v, pos)
+            del q, k, v, qp, kp
+        self.n = steps
+        self.dq = torch.randn((steps, L, 1, Hq, D), generator=g, device=device, dtype=dt)
+        self.dk = torch.randn((steps, L, 1, Hk, D), generator=g, device=device, dtype=dt)
+        self.dv = torch.randn((steps, L, 1, Hk, D), generator=g, device=device, dtype=dt)
+        p = torch.arange(T, T + steps, device=device)
+        cs, sn = self.rot(torch.empty(1, dtype=dt, device=device), p[None])
+        self.cos, self.sin = cs[0].contiguous(), sn[0].contiguous()   # (steps, D)
+        self.pos = p.view(steps, 1).contiguous()
+        self.out = torch.empty((L, 1, Hq, D), dtype=dt, device=device)
+        # size the shared scratch for every op now, so that no allocation happens in a capture
+        from hotcold_kv_cache_b200._lib import byref, size
+        a0 = self.ctrl.arenas[0]
+        need = max(size("hc_attend_scratch_bytes", byref(a0.L)), size("hc_retrieve_scratch_bytes", byref(a0.L)),
+                   size("hc_compress_scratch_bytes", byref(a0.L), a0.max_cap, 1))
+        self.ctrl.workspace.get(need)
+        torch.cuda.synchronize(device)
+
+    def step(self, i):
+        """Decode step i through all layers (the public per-layer API). Each layer's output
+        stays in its arena's output buffer."""
+        c = self.c
+        for li in range(c["layers"]):
+            self.ctrl.decode_layer(li, self.dq[i, li], self.dk[i, li], self.dv[i, li], self.cos[i:i + 1],
+                                   self.sin[i:i + 1], self.pos[i])
+
+
+def kernel_counts(ctrl, before):
+    """Kernels launched by the ops between two dbg snapshots (fixed per op)."""
+    d = {k: ctrl.dbg[k] - before[k] for k in ctrl.dbg}
+    L_steps = d["triton_decode_calls"]
+    # append 1 + attend 1 per layer-step; compression: score + select (+ copy kernel above 32 tokens);
+    # retrieval: query + scan + pick + splice
+    return 2 * L_steps + 2 * d["compress_calls"] + 4 * d["retrieval_launched"]
+
+
+def run_ours(a, rank, world):
+    import torch
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    c = config(a)
+    K, W = a.steps, a.warmup
+    total_steps = W + K
+    wl = Workload(c, total_steps + K, a.seed + rank, dev)
+    ctrl = wl.ctrl
+    # warm-up: eager steps (grow the workspace, fill the query pool, land a retrieval)
+    for i in range(W):
+        wl.step(i)
+    torch.cuda.synchronize(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(dev)
+    times = []
+    dbg0 = dict(ctrl.dbg)
+    gpu_id = None
+    try:
+        gpu_id = torch.cuda.get_device_properties(dev).pci_bus_id if hasattr(
+            torch.cuda.get_device_properties(dev), "pci_bus_id") else str(dev.index)
+    except Exception:
+        gpu_id = None
+    clocks = ClockSampler(gpu_id if rank == 0 else None)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    if rank == 0:
+        clocks.start()
+    for i in range(W, total_steps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                wl.step(i)
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream(dev)
+        e0.record(cur)
+        g.replay()
+        e1.record(cur)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+        del g
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    clk = clocks.stop() if rank == 0 else None
+    launches = kernel_counts(ctrl, dbg0)
+    step_ms = float(sum(times) / len(times))
+    tot = torch.tensor([sum(times)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.MAX)
+    max_total_ms = float(tot.item())
+    layer_steps_all = world * K * c["layers"]
+    value = max_total_ms * 1e3 / layer_steps_all
+    status = ctrl.device_status()
+    if status:
+        raise RuntimeError(f"device status word set: {status}")
+
+    # ---- per-op device time of one layer-step, isolated behind a GPU sleep ----------------
+    ops = per_op_times(wl, total_steps, dev)
+
+    # ---- end to end through the public API with host buffers ------------------------------
+    e2e = run_e2e(wl, total_steps + 0, min(K, 8), dev)
+
+    peak, peak_kind = measured_peaks()
+    att = ops["attend"]
+    roof = {"bound": "hbm", "kernel": "attn_kernel (hc_attend)", "achieved": round(att["gbs"], 1),
+            "peak": peak, "unit": "GB/s", "frac": round(att["gbs"] / peak, 4),
+            "traffic": profiled_traffic("attend"), "peak_source": f"{peak_kind} hbm_gbs",
+            "bytes_per_launch": att["bytes"], "us_per_launch": round(att["us"], 3)}
+    res = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+           "ms_per_step": round(step_ms, 4), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+           "dtype": "f16", "data": "synthetic N(0,1) pre-RoPE q/k/v, seeded; no weights or dataset",
+           "config": workload_config(c, {"parallelism": f"replicas{world}"}),
+           "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "clocks": clk,
+           "ops_us_per_layer_step": {k: round(v["us"], 3) for k, v in ops.items()},
+           "hbm_gbs_per_layer_step": round(ops["_step_bytes"] / (value * 1e-6) / 1e9, 1)}
+    return res
+
+
+def per_op_times(wl, start_step, dev, reps=3):
+    """Device time of each op of one layer-step: a GPU sleep first, so the op's launches are
+    queued before the GPU reaches them and host latency stays out of the interval."""
+    import torch
+    from hotcold_kv_cache_b200 import arena as arena_mod  # noqa: F401
+    ctrl, c = wl.ctrl, wl.c
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    acc = {"append": [], "compress": [], "retrieve": [], "attend": []}
+    nbytes_att = []
+    i = start_step
+    for r in range(reps):
+        for li in range(c["layers"]):
+            a = ctrl.arenas[li]
+            q, k, v = wl.dq[i, li], wl.dk[i, li], wl.dv[i, li]
+            cs, sn, p = wl.cos[i:i + 1], wl.sin[i:i + 1], wl.pos[i]
+
+            def timed(fn):
+                flush.zero_()
+                torch.cuda._sleep(200000)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                out = fn()
+                e1.record()
+                e1.synchronize()
+                return e0.elapsed_time(e1) * 1e3, out
+
+            t_app, qp = timed(lambda: a.append(q, k, v, cs, sn, p))
+            n_pool, extra, extra_n = ctrl._pool(li)
+            t_ret, _ = timed(lambda: a.retrieve(n_pool=max(n_pool, 1), extra_sum=extra, extra_n=extra_n))
+            t_cmp, _ = timed(lambda: a.compress_decode(qp.view(1, a.Hq, 1, a.D)))
+            t_att, _ = timed(lambda: a.attend(qp, p, True))
+            acc["append"].append(t_app)
+            acc["retrieve"].append(t_ret)
+            acc["compress"].append(t_cmp)
+            acc["attend"].append(t_att)
+            n_tok = int(a.n_hot[0]) + a.r_max
+            nbytes_att.append(n_tok * a.Hk * a.D * 2 * 2 + 2 * a.Hq * a.D * 2)
+        i += 1
+    Hk, D, R = c["Hk"], c["D"], c["lookahead_k"]
+    a = ctrl.arenas[0]
+    n_cold = int(a.cold_count[0])
+    bytes_ = {
+        "attend": float(np.mean(nbytes_att)),
+        "append": (c["Hq"] * D * 2) * 2 + Hk * D * 2 * 4,
+        "compress": (int(a.n_hot[0]) + 1) * Hk * D * 2 + Hk * D * 2 * 2 + c["faiss_dim"] * 4,
+        "retrieve": n_cold * c["faiss_dim"] * 4 + R * Hk * D * 2 * 4,
+    }
+    out = {}
+    for k, v in acc.items():
+        us = float(np.median(v))
+        out[k] = {"us": us, "bytes": bytes_[k], "gbs": bytes_[k] / (us * 1e-6) / 1e9}
+    out["_step_bytes"] = bytes_["attend"] + bytes_["append"] + bytes_["compress"] + bytes_["retrieve"] / c[
+        "window_size"]
+    return out
+
+
+def run_e2e(wl, start, n, dev):
+    """Per step: pinned host -> device copy of every layer's q/k/v, the public per-layer
+    decode call for all layers, device -> host read of every layer's attention output."""
+    import torch
+    c = wl.c
+    L = c["layers"]
+    hq = wl.dq[start:start + n].cpu().pin_memory()
+    hk = wl.dk[start:start + n].cpu().pin_memory()
+    hv = wl.dv[start:start + n].cpu().pin_memory()
+    hout = torch.empty((L, 1, c["Hq"], c["D"]), dtype=torch.float16).pin_memory()
+    dq, dk, dv = torch.empty_like(wl.dq[0]), torch.empty_like(wl.dk[0]), torch.empty_like(wl.dv[0])
+    times = []
+    for j in range(n):
+        i = start + j
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dq.copy_(hq[j], non_blocking=True)
+        dk.copy_(hk[j], non_blocking=True)
+        dv.copy_(hv[j], non_blocking=True)
+        for li in range(L):
+            o = wl.ctrl.decode_layer(li, dq[li], dk[li], dv[li], wl.cos[i:i + 1], wl.sin[i:i + 1], wl.pos[i])
+            wl.out[li].copy_(o)
+        hout.copy_(wl.out, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = float(np.mean(times))
+    h2d = (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2
+    return {"value": round(ms * 1e3 / L, 3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(hout.numel() * 2), "api": "KVController.decode_layer, eager, per layer",
+            "steps": n}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU arm: the oracle port of the reference path on one layer
+# ------------------------------------------------------------------------------------------
+def cpu_port(c, n_steps, seed):
+    """Time the CPU restatement of the reference per-layer decode step (torch-free numpy port)
+    on ONE layer of the workload: prompt compressed into hot + cold tiers (untimed), then
+    n_steps decode steps timed with perf_counter. Returns (us per layer-step, threads)."""
+    from hotcold_kv_cache_b200 import synth
+    from oracle import hotcold_oracle as O
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = 1
+    inp = synth.layer_inputs(seed, 1, c["Hq"], c["Hk"], c["D"], c["prompt"], n_steps, c["dtype"])
+    layer = O.OracleLayer(Hq=c["Hq"], Hk=c["Hk"], D=c["D"], dtype=c["dtype"],
+                          inv_freq=synth.rope_inv_freq(c["D"], c["theta"]),
+                          policy=O.Policy(c["policy"], cap=c["budget"], recent=c["recent"],
+                                          topk_ratio=c["topk_ratio"], pool_kernel=c["pool_kernel"]),
+                          cpu_buffer_size=c["ccap"], faiss_dim=c["faiss_dim"], window_size=c["window_size"],
+                          query_pool_size=c["query_pool_size"], lookahead_k=c["lookahead_k"],
+                          hold_retrieved=c["hold"], retrieve_after_prefill=False)
+    layer.prefill(inp["q_pre"], inp["k_pre"], inp["v"])
+    layer.start_decode(c["prompt"])
+    ts = []
+    for i in range(n_steps):
+        t0 = time.perf_counter()
+        layer.decode(inp["dq"][i], inp["dk"][i], inp["dv"][i], step=i + 1)
+        ts.append(time.perf_counter() - t0)
+    return float(np.mean(ts)) * 1e6, threads
+
+
+def cpu_baseline_obj(c, n_steps, seed):
+    us, thr = cpu_port(c, n_steps, seed)
+    return {"value": round(us, 1), "unit": UNIT, "cores": thr, "kind": "port",
+            "sample": f"1 of {c['layers']} layers, {n_steps} decode steps (one retrieval per 16), "
+                      f"numpy restatement in oracle/, faiss replaced by exact flat inner product"}
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        c = config(a)
+        us, thr = cpu_port(c, max(a.cpu_steps, 1), a.seed)
+        out = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": UNIT, "n_gpus": a.gpus,
+               "steps": a.cpu_steps, "warmup": 0, "ms_per_step": round(us * c["layers"] / 1e3, 3),
+               "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+               "data": "synthetic N(0,1) pre-RoPE q/k/v, seeded",
+               "config": workload_config(c, {"parallelism": "cpu"}),
+               "cpu_baseline": {"value": round(us, 1), "unit": UNIT, "cores": thr, "kind": "port",
+                                "sample": f"1 of {c['layers']} layers, {a.cpu_steps} decode steps"},
+               "e2e": {"value": round(us, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(out))
+        return 0
+    if world > 1:
+        import datetime
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    res = run_ours(a, rank, world)
+    if rank == 0 and not a.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_obj(config(a), a.cpu_steps, a.seed)
+    if world > 1:
+        import torch
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,376 @@
+"""HBM state of one attention layer and the C-ABI calls over it.
+
+A LayerArena holds, for n_seq sequences, the hot slab (budget + 1 physical
+slots with a logical-order table and a free-slot stack), the held segment of
+retrieved tokens, the cold ring (payload + float32 index vectors), the query
+pool and the device-resident counters, plus the descriptor array the kernels
+read. All buffers are allocated once; every op afterwards is an asynchronous
+launch on the current stream with no host synchronisation, so a decode step
+can be captured in a CUDA graph.
+
+The host keeps mirrors of the counters (hot length, cold count). They follow
+from the schedule alone (compression plans depend only on lengths and
+budgets), so the host never reads them back.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import byref, call, ptr, size
+
+
+class Workspace:
+    """Grow-only scratch buffer shared by the ops of one stream."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.buf = torch.empty(0, dtype=torch.uint8, device=self.device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf.numel() < nbytes:
+            self.buf = torch.empty(int(nbytes * 1.25) + 4096, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+def plan_keep(policy: str, budget: int, recent: int, topk_ratio: float, S: int):
+    """(prefix_len, n_top) of a compression of S hot tokens, or None when S <= budget.
+    hot/cold: cache.py:44-53; SnapKV: scoring.py:117-120 with the trigger of cache.py:44."""
+    if S <= budget:
+        return None
+    if policy == "hotcold":
+        rec = min(recent, budget, S)
+        prefix = S - rec
+        if prefix <= 0:
+            return None
+        ntop = max(1, min(int(budget * topk_ratio), prefix))
+        return prefix, ntop
+    window = min(recent, S)
+    prefix = S - window
+    return prefix, max(0, min(budget - window, prefix))
+
+
+class LayerArena:
+    def __init__(self, *, n_seq: int, Hq: int, Hk: int, D: int, F: int, dtype, device, budgets, r_max: int,
+                 ccap, p_max: int, policy: str, recent: int, topk_ratio: float, pool_kernel: int = 7,
+                 pooling: str = "maxpool", normalize: bool = True, inv_freq: torch.Tensor, rope_scaling: float = 1.0,
+                 workspace: Workspace | None = None, hot_cap_hint: int | None = None):
+        """hot_cap_hint: initial physical hot slots when below budget + 1 (the slab grows on
+        demand up to budget + 1, so a huge budget does not preallocate)."""
+        _lib.load()
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            raise RuntimeError("the hot/cold path runs on CUDA devices only")
+        self.device, self.dtype = dev, dtype
+        self.n_seq, self.Hq, self.Hk, self.D, self.F = n_seq, Hq, Hk, D, F
+        budgets = [int(b) for b in (budgets if hasattr(budgets, "__len__") else [budgets] * n_seq)]
+        ccaps = [int(c) for c in (ccap if hasattr(ccap, "__len__") else [ccap] * n_seq)]
+        assert len(budgets) == n_seq and len(ccaps) == n_seq
+        self.budgets, self.ccaps = budgets, ccaps
+        self.policy, self.recent, self.topk_ratio = policy, int(recent), float(topk_ratio)
+        self.r_max, self.p_max = int(r_max), int(p_max)
+        caps = [b + 1 if hot_cap_hint is None else min(b + 1, max(int(hot_cap_hint), 1)) for b in budgets]
+        self.caps = caps
+        mc, R, C, P = max(caps), max(self.r_max, 1), max(max(ccaps), 1), max(self.p_max, 1)
+        self.max_cap, self.max_ccap = mc, C
+        z = dict(device=dev)
+        self.hot_k = torch.empty((n_seq, Hk, mc, D), dtype=dtype, **z)
+        self.hot_v = torch.empty((n_seq, Hk, mc, D), dtype=dtype, **z)
+        self.hot_kpre = torch.empty((n_seq, Hk, mc, D), dtype=dtype, **z)
+        self.hot_pos = torch.zeros((n_seq, mc), dtype=torch.int64, **z)
+        self.hot_ord = torch.zeros((n_seq, mc), dtype=torch.int32, **z)
+        self.hot_free = torch.zeros((n_seq, mc), dtype=torch.int32, **z)
+        self.held_k = torch.zeros((n_seq, Hk, R, D), dtype=dtype, **z)
+        self.held_v = torch.zeros((n_seq, Hk, R, D), dtype=dtype, **z)
+        self.held_pos = torch.zeros((n_seq, R), dtype=torch.int64, **z)
+        self.held_valid = torch.zeros((n_seq, R), dtype=torch.uint8, **z)
+        self.held_src = torch.full((n_seq, R), -1, dtype=torch.int32, **z)
+        self.cold_vec = torch.empty((n_seq, C, F), dtype=torch.float32, **z)
+        self.cold_kpre = torch.empty((n_seq, C, Hk, D), dtype=dtype, **z)
+        self.cold_v = torch.empty((n_seq, C, Hk, D), dtype=dtype, **z)
+        self.cold_pos = torch.zeros((n_seq, C), dtype=torch.int64, **z)
+        self.qwin = torch.zeros((n_seq, P, D), dtype=dtype, **z)
+        self.st = torch.zeros((n_seq, 16), dtype=torch.int32, **z)
+        self.counters = torch.zeros((n_seq * Hk,), dtype=torch.int32, **z)
+        self.inv_freq = inv_freq.detach().to(device=dev, dtype=torch.float32).contiguous()
+        self.q_post = torch.empty((n_seq, Hq, D), dtype=dtype, **z)
+        self.out = torch.empty((n_seq, Hq, D), dtype=dtype, **z)
+        self.ws = workspace or Workspace(dev)
+
+        self.pool_kernel, self.pooling, self.normalize, self.rope_scaling = pool_kernel, pooling, normalize, rope_scaling
+        self._build_descriptors()
+        # host mirrors
+        self.n_hot = np.zeros(n_seq, np.int64)
+        self.cold_count = np.zeros(n_seq, np.int64)
+
+    def _build_descriptors(self):
+        n_seq, caps, budgets, ccaps = self.n_seq, self.caps, self.budgets, self.ccaps
+        mc, C = self.max_cap, self.max_ccap
+        descs = (_lib.HcSeqDesc * n_seq)()
+        for s in range(n_seq):
+            d = descs[s]
+            d.hot_k = self.hot_k[s].data_ptr()
+            d.hot_v = self.hot_v[s].data_ptr()
+            d.hot_kpre = self.hot_kpre[s].data_ptr()
+            d.hot_pos = self.hot_pos[s].data_ptr()
+            d.hot_ord = self.hot_ord[s].data_ptr()
+            d.hot_free = self.hot_free[s].data_ptr()
+            d.held_k = self.held_k[s].data_ptr()
+            d.held_v = self.held_v[s].data_ptr()
+            d.held_pos = self.held_pos[s].data_ptr()
+            d.held_valid = self.held_valid[s].data_ptr()
+            d.held_src = self.held_src[s].data_ptr()
+            d.cold_vec = self.cold_vec[s].data_ptr()
+            d.cold_kpre = self.cold_kpre[s].data_ptr()
+            d.cold_v = self.cold_v[s].data_ptr()
+            d.cold_pos = self.cold_pos[s].data_ptr()
+            d.qwin = self.qwin[s].data_ptr()
+            d.st = self.st[s].data_ptr()
+            d.cap, d.budget, d.r_max, d.ccap, d.p_max = caps[s], budgets[s], self.r_max, ccaps[s], self.p_max
+        raw = bytes(ctypes.string_at(ctypes.addressof(descs), ctypes.sizeof(descs)))
+        self.desc = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
+        L = _lib.HcLayer()
+        L.desc = self.desc.data_ptr()
+        L.inv_freq = self.inv_freq.data_ptr()
+        L.counters = self.counters.data_ptr()
+        L.topk_ratio = self.topk_ratio
+        L.n_seq, L.Hq, L.Hk, L.D, L.F = n_seq, self.Hq, self.Hk, self.D, self.F
+        L.dtype = _lib.dtype_code(self.dtype)
+        L.policy = _lib.HC_POLICY_HOTCOLD if self.policy == "hotcold" else _lib.HC_POLICY_SNAPKV
+        L.recent = self.recent
+        L.pool_kernel = int(self.pool_kernel)
+        L.pooling = _lib.HC_POOL_MAX if self.pooling == "maxpool" else _lib.HC_POOL_AVG
+        L.normalize = 1 if self.normalize else 0
+        L.max_cap, L.max_r, L.max_ccap = mc, self.r_max, C
+        L.scale = 1.0 / math.sqrt(self.D)
+        L.rope_scaling = float(self.rope_scaling)
+        self.L = L
+
+    def ensure_hot_capacity(self, need):
+        """Grow the physical hot slab so that sequence s can hold need[s] tokens (capped at
+        budget + 1). Contents, logical order and free slots carry over; runs only when the
+        slab is too small, never in a steady decode loop."""
+        need = np.broadcast_to(np.asarray(need, np.int64), (self.n_seq,))
+        new_caps = [min(self.budgets[s] + 1, max(self.caps[s], int(need[s]))) for s in range(self.n_seq)]
+        if new_caps == self.caps:
+            return
+        grown = [max(c, min(self.budgets[s] + 1, 2 * self.caps[s])) if c > self.caps[s] else c
+                 for s, c in enumerate(new_caps)]
+        mc_old, mc = self.max_cap, max(grown)
+        if mc > mc_old:
+            def grow(t, dim, fill=None):
+                shape = list(t.shape)
+                shape[dim] = mc
+                n = torch.empty(shape, dtype=t.dtype, device=t.device) if fill is None else \
+                    torch.full(shape, fill, dtype=t.dtype, device=t.device)
+                n.narrow(dim, 0, mc_old).copy_(t)
+                return n
+            # per-sequence regions are [Hk][cap][D] with the sequence's own cap: re-lay them
+            for name in ("hot_k", "hot_v", "hot_kpre"):
+                old = getattr(self, name)
+                new = torch.empty((self.n_seq, self.Hk, mc, self.D), dtype=old.dtype, device=old.device)
+                for s in range(self.n_seq):
+                    c = self.caps[s]
+                    src = old[s].reshape(-1)[: self.Hk * c * self.D].view(self.Hk, c, self.D)
+                    new[s].reshape(-1)[: self.Hk * grown[s] * self.D].view(self.Hk, grown[s], self.D)[:, :c] \
+                        .copy_(src)
+                setattr(self, name, new)
+            self.hot_pos = grow(self.hot_pos, 1, 0)
+            self.hot_ord = grow(self.hot_ord, 1, 0)
+            self.hot_free = grow(self.hot_free, 1, 0)
+        else:
+            for name in ("hot_k", "hot_v", "hot_kpre"):
+                t = getattr(self, name)
+                for s in range(self.n_seq):
+                    c, g = self.caps[s], grown[s]
+                    if g != c:
+                        buf = t[s].reshape(-1)
+                        tmp = buf[: self.Hk * c * self.D].view(self.Hk, c, self.D).clone()
+                        buf[: self.Hk * g * self.D].view(self.Hk, g, self.D)[:, :c].copy_(tmp)
+        for s in range(self.n_seq):
+            c, g = self.caps[s], grown[s]
+            if g > c:
+                nf = c - int(self.n_hot[s])
+                self.hot_free[s, nf: nf + g - c] = torch.arange(g - 1, c - 1, -1, dtype=torch.int32,
+                                                                device=self.device)
+                self.st[s, 1] += g - c
+        self.caps = grown
+        self.max_cap = mc
+        self._build_descriptors()
+
+    # ------------------------------------------------------------------ helpers
+    def _stream(self):
+        return _lib.stream_of(self.device)
+
+    def _row_major(self, t: torch.Tensor, rows: int) -> tuple[torch.Tensor, int]:
+        """(n_seq, rows, D) view with contiguous rows; returns (tensor, seq stride)."""
+        t = t.reshape(self.n_seq, rows, self.D) if t.dim() != 3 else t
+        if t.stride(2) != 1 or t.stride(1) != self.D:
+            t = t.contiguous()
+        return t, t.stride(0)
+
+    def plan(self, s: int, S: int):
+        return plan_keep(self.policy, self.budgets[s], self.recent, self.topk_ratio, S)
+
+    # ------------------------------------------------------------------ ops
+    def store_prompt(self, k_post, v, k_pre, pos):
+        """Prompt of T <= budget tokens into the slab (cache.py:145-148). Tensors (n_seq,Hk,T,D)."""
+        T = k_post.shape[2]
+        call("hc_store_prompt", byref(self.L), T, ptr(k_post), ptr(v), ptr(k_pre), *self._strides(k_post, v, k_pre),
+             ptr(pos.contiguous()), self._stream())
+        self.n_hot[:] = T
+
+    def _strides(self, k, v, kp):
+        st = k.stride()
+        if v.stride() != st or kp.stride() != st or st[3] != 1:
+            raise ValueError("k_post, v and k_pre must share strides with unit stride over head_dim")
+        return st[0], st[1], st[2]
+
+    def compress_prompt(self, q_obs, k_post, v, k_pre, pos):
+        """Prompt of T tokens into an empty slab: sequences with T > budget score, keep and
+        evict into the cold ring (cache.py:37-128 on the prompt); the others keep the whole
+        prompt. Tensors (n_seq,Hk,T,D), q_obs (n_seq,Hq,tq,D). Returns evicted counts."""
+        T = k_post.shape[2]
+        self.ensure_hot_capacity([min(T, b) + 1 for b in self.budgets])
+        tq = q_obs.shape[2]
+        qs = q_obs.stride()
+        nbytes = size("hc_compress_scratch_bytes", byref(self.L), T, tq)
+        ws = self.ws.get(nbytes)
+        pos = pos.contiguous()
+        call("hc_compress_ex", byref(self.L), ptr(q_obs), qs[0], qs[1], qs[2], tq, T, ptr(k_post), ptr(v), ptr(k_pre),
+             *self._strides(k_post, v, k_pre), ptr(pos), ptr(ws), ws.numel(), 1 << 30, self._stream())
+        ev = np.zeros(self.n_seq, np.int64)
+        for s in range(self.n_seq):
+            p = self.plan(s, T)
+            if p is None:
+                self.n_hot[s] = T
+                continue
+            prefix, ntop = p
+            ev[s] = prefix - ntop
+            self.n_hot[s] = T - ev[s]
+            self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + ev[s])
+        return ev
+
+    def append(self, q_pre, k_pre, v, cos, sin, pos):
+        """Decode-step RoPE + append + query-pool push. q_pre (n_seq,Hq,D), k_pre/v (n_seq,Hk,D),
+        cos/sin (n_seq,D) or None, pos (n_seq,) int64. Returns q_post (n_seq,Hq,D)."""
+        if (self.n_hot + 1 > np.asarray(self.caps)).any():
+            self.ensure_hot_capacity(self.n_hot + 1)
+        q, qss = self._row_major(q_pre, self.Hq)
+        k, kss = self._row_major(k_pre, self.Hk)
+        vv, vss = self._row_major(v, self.Hk)
+        if vss != kss:
+            k, vv = k.contiguous(), vv.contiguous()
+            kss = k.stride(0)
+        if cos is not None:
+            cos = cos.reshape(self.n_seq, self.D).contiguous()
+            sin = sin.reshape(self.n_seq, self.D).contiguous()
+        call("hc_append", byref(self.L), ptr(q), qss, ptr(k), ptr(vv), kss, ptr(cos), ptr(sin), ptr(pos),
+             ptr(self.q_post), self._stream())
+        self.n_hot += 1
+        return self.q_post
+
+    def append_rotated(self, k_post, k_pre, v, pos):
+        if (self.n_hot + 1 > np.asarray(self.caps)).any():
+            self.ensure_hot_capacity(self.n_hot + 1)
+        k, kss = self._row_major(k_post, self.Hk)
+        kp = k_pre.reshape(self.n_seq, self.Hk, self.D).contiguous()
+        vv = v.reshape(self.n_seq, self.Hk, self.D).contiguous()
+        k = k.contiguous()
+        call("hc_append_rotated", byref(self.L), ptr(k), ptr(kp), ptr(vv), k.stride(0), ptr(pos), self._stream())
+        self.n_hot += 1
+
+    def compress_decode(self, q_obs):
+        """Compression of the slab when a sequence holds more than its budget. q_obs
+        (n_seq,Hq,tq,D). Returns evicted counts per sequence (all zero when no sequence
+        compresses; nothing is launched then)."""
+        ev = np.zeros(self.n_seq, np.int64)
+        active = False
+        for s in range(self.n_seq):
+            p = self.plan(s, int(self.n_hot[s]))
+            if p is not None:
+                active = True
+                ev[s] = p[0] - p[1]
+        if not active:
+            return ev
+        tq = q_obs.shape[2]
+        qs = q_obs.stride()
+        nbytes = size("hc_compress_scratch_bytes", byref(self.L), self.max_cap, tq)
+        ws = self.ws.get(nbytes)
+        call("hc_compress_ex", byref(self.L), ptr(q_obs), qs[0], qs[1], qs[2], tq, 0, None, None, None, 0, 0, 0, None,
+             ptr(ws), ws.numel(), int(ev.max()), self._stream())
+        self.n_hot -= ev
+        for s in range(self.n_seq):
+            self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + ev[s])
+        return ev
+
+    def retrieve(self, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0, qvec=None):
+        """Search + gather + re-RoPE into the held segment."""
+        nbytes = size("hc_retrieve_scratch_bytes", byref(self.L))
+        ws = self.ws.get(nbytes)
+        qd = (0, 0, 0)
+        P = 0
+        if q_dense is not None:
+            qd = q_dense.stride()[:3]
+            P = q_dense.shape[2]
+        mc = int(self.cold_count.max())
+        call("hc_retrieve_ex", byref(self.L), ptr(q_dense), qd[0], qd[1], qd[2], P, int(n_pool), ptr(extra_sum),
+             int(extra_n), ptr(qvec), ptr(ws), ws.numel(), mc, self._stream())
+
+    def prompt_query_sum(self, q_dense):
+        out = torch.empty((self.n_seq, self.D), dtype=torch.float32, device=self.device)
+        qs = q_dense.stride()
+        call("hc_prompt_query_sum", byref(self.L), ptr(q_dense), qs[0], qs[1], qs[2], q_dense.shape[2], ptr(out),
+             self._stream())
+        return out
+
+    def attend(self, q_post, cur_pos, use_held: bool, overflow_nan: bool = True):
+        nbytes = size("hc_attend_scratch_bytes", byref(self.L))
+        ws = self.ws.get(nbytes)
+        q = q_post if q_post.is_contiguous() else q_post.contiguous()
+        call("hc_attend", byref(self.L), ptr(q), ptr(cur_pos), 1 if use_held else 0, ptr(self.out),
+             1 if overflow_nan else 0, ptr(ws), ws.numel(), self._stream())
+        return self.out
+
+    def cold_append(self, k_pre, v, pos, evicted_idx):
+        """Evicted tokens (n_seq,Hk,Te,D) into the cold ring (controller.py:190-238)."""
+        Te = k_pre.shape[2]
+        st = k_pre.stride()
+        if v.stride() != st:
+            v = v.contiguous()
+            k_pre = k_pre.contiguous()
+            st = k_pre.stride()
+        idx = evicted_idx.to(device=self.device, dtype=torch.int64).contiguous()
+        call("hc_cold_append", byref(self.L), ptr(k_pre), ptr(v), st[0], st[1], st[2],
+             ptr(pos.to(device=self.device, dtype=torch.int64).contiguous()), ptr(idx), Te, self._stream())
+        m = (evicted_idx >= 0).sum(dim=1).cpu().numpy()
+        for s in range(self.n_seq):
+            self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + int(m[s]))
+        return m
+
+    # ------------------------------------------------------------------ views (API, not the hot path)
+    def logical_order(self, s: int) -> torch.Tensor:
+        return self.hot_ord[s, : int(self.n_hot[s])].long()
+
+    def hot_view(self, which: str) -> torch.Tensor:
+        """(n_seq, Hk, S, D) of the hot tier in logical order (all sequences of equal length)."""
+        src = {"k": self.hot_k, "v": self.hot_v, "kpre": self.hot_kpre}[which]
+        return torch.stack([src[s].index_select(1, self.logical_order(s)) for s in range(self.n_seq)], 0)
+
+    def hot_positions(self) -> torch.Tensor:
+        return torch.stack([self.hot_pos[s].index_select(0, self.logical_order(s)) for s in range(self.n_seq)], 0)
+
+    def cold_order(self, s: int) -> torch.Tensor:
+        """Physical ring slots of sequence s, oldest first (device tensor)."""
+        st = self.st[s].cpu()
+        head, count = int(st[2]), int(st[3])
+        return (torch.arange(count, device=self.device) + head) % self.ccaps[s]
+
+    def device_state(self) -> np.ndarray:
+        """Counters as the kernels see them (synchronises)."""
+        return self.st.cpu().numpy()

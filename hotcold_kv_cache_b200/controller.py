@@ -1,0 +1,434 @@
+"""KVController: the cold store, the retrieval schedule and the held set.
+
+Same constructor, members and counters as the reference KVController
+(controller.py:14-442 of src/hotcold_kv). What changes is where things live:
+the cold tier is an HBM ring per (layer, sequence) with float32 index vectors
+instead of host deques plus a CPU FAISS index, the search is a CUDA scan +
+exact top-k instead of a daemon thread, and retrieved tokens go straight into
+a held segment in HBM instead of a pinned buffer and a side-stream copy.
+
+Schedule. A retrieval that fires at a decode step (every `window_size` forward
+calls, controller.py:314-342) is attended at that same step; the prompt-end
+retrieval (patch.py:231-233) is attended at decode step 1. The reference's
+asynchronous thread makes that step nondeterministic; this is the
+deterministic order its synchronous path would give. Nothing here blocks the
+host: every op is an asynchronous launch on the current stream.
+"""
+
+from __future__ import annotations
+
+from collections import deque
+from typing import List, Optional
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from .arena import LayerArena, Workspace
+from .datatypes import EvictedKV, RetrievedKV, _canon_br_2d, _canon_kv_4d
+
+DBG_KEYS = (
+    "compress_calls", "evicted_tokens", "faiss_add",
+    "retrieval_launched", "retrieval_launched_prefill", "retrieval_ready_cpu", "retrieval_skipped_no_cold",
+    "retrieval_ready_empty",
+    "prefetch_launched", "prefetch_ready", "prefetch_skipped_empty",
+    "injection_used", "injection_new", "injection_skipped_no_valid",
+    "prefetch_copy_ms_sum", "prefetch_copy_ms_count", "prefetch_not_ready_checks", "main_waited_for_prefetch",
+    "triton_decode_calls", "triton_prefill_fallback",
+)
+
+
+class _RingView:
+    """Read-only view of one cold ring in age order (the reference's cpu_*_ring deques)."""
+
+    def __init__(self, ctrl: "KVController", li: int, b: int, field: str):
+        self.c, self.li, self.b, self.field = ctrl, li, b, field
+
+    def __len__(self):
+        return int(self.c.arenas[self.li].cold_count[self.b])
+
+    def __getitem__(self, i):
+        a = self.c.arenas[self.li]
+        n = len(self)
+        if i < 0:
+            i += n
+        if not 0 <= i < n:
+            raise IndexError(i)
+        slot = int(a.cold_order(self.b)[i])
+        if self.field == "kpre":
+            return a.cold_kpre[self.b, slot]
+        if self.field == "v":
+            return a.cold_v[self.b, slot]
+        return int(a.cold_pos[self.b, slot])
+
+
+class _IndexView:
+    """The reference's per-(layer, sequence) FAISS index, reduced to ntotal."""
+
+    def __init__(self, ctrl, li, b):
+        self.c, self.li, self.b = ctrl, li, b
+
+    @property
+    def ntotal(self):
+        return int(self.c.arenas[self.li].cold_count[self.b])
+
+
+class KVController:
+    def __init__(
+        self,
+        max_capacity_prompt: int = 128,
+        topk_ratio: float = 0.15,
+        recent_size: int = 32,
+        cpu_buffer_size: int = 8192,
+        faiss_dim: int = 64,
+        normalize_for_ip: bool = True,
+        window_size: int = 16,
+        query_pool_size: int = 4,
+        lookahead_k: int = 32,
+        hold_retrieved: bool = False,
+        retrieve_after_prefill: bool = False,
+        enable_asserts: bool = True,
+        profile_overlap: bool = True,
+        force_wait_for_prefetch_diagnostic: bool = False,
+        *,
+        policy: str = "hotcold",
+        pool_kernel: int = 7,
+        pooling: str = "maxpool",
+        overflow_nan: bool = True,
+    ):
+        """Reference arguments (controller.py:15-34) plus:
+        policy: "hotcold" (cache.py:37-128) or "snapkv" (SnapKV score, scoring.py:50-132,
+            with recent_size as the observation/recent window);
+        pool_kernel, pooling: SnapKV pooling (scoring.py:40-47);
+        overflow_nan: reproduce the reference kernel's NaN on fp32 exp overflow."""
+        if policy not in ("hotcold", "snapkv"):
+            raise ValueError(f"unknown policy {policy!r}")
+        if pooling not in ("maxpool", "avgpool"):
+            raise ValueError(f"unknown pooling {pooling!r}")
+        self.max_capacity_prompt = int(max_capacity_prompt)
+        self.topk_ratio = float(topk_ratio)
+        self.recent_size = int(recent_size)
+        self.cpu_buffer_size = int(cpu_buffer_size)
+        self.faiss_dim = int(faiss_dim)
+        self.normalize_for_ip = bool(normalize_for_ip)
+        self.window_size = int(window_size)
+        self.query_pool_size = int(query_pool_size)
+        self.lookahead_k = int(lookahead_k)
+        self.hold_retrieved = bool(hold_retrieved)
+        self.retrieve_after_prefill = bool(retrieve_after_prefill)
+        self.enable_asserts = bool(enable_asserts)
+        self.profile_overlap = bool(profile_overlap)
+        self.force_wait_for_prefetch_diagnostic = bool(force_wait_for_prefetch_diagnostic)
+        self.policy, self.pool_kernel, self.pooling = policy, int(pool_kernel), pooling
+        self.overflow_nan = bool(overflow_nan)
+
+        self._inited = False
+        self.B = self.Hk = self.D = self.n_layers = None
+        self.step_count: List[int] = []
+        self.arenas: List[Optional[LayerArena]] = []
+        self._qpool: List[deque] = []
+        self._prompt_qsum: List[Optional[torch.Tensor]] = []
+        self._staged: List[bool] = []
+        self._held_active: List[bool] = []
+        self._retrieval_ready_cpu: List[Optional[tuple]] = []
+        self.last_injected_len = 0
+        self.workspace: Optional[Workspace] = None
+        self.rotary = None  # (inv_freq tensor, attention_scaling); else the active rotary module
+        self.dbg = {k: (0.0 if k == "prefetch_copy_ms_sum" else 0) for k in DBG_KEYS}
+
+    # ------------------------------------------------------------------ setup
+    def _lazy_init(self, k_pre: torch.Tensor, n_layers: int):
+        """controller.py:124-158: geometry and per-layer state; device buffers follow on the
+        first forward of each layer."""
+        if self._inited:
+            return
+        B, Hk, _, D = k_pre.shape
+        self.B, self.Hk, self.D, self.n_layers = int(B), int(Hk), int(D), int(n_layers)
+        L = self.n_layers
+        self.step_count = [0] * L
+        self.arenas = [None] * L
+        self._qpool = [deque(maxlen=max(self.query_pool_size, 1)) for _ in range(L)]
+        self._prompt_qsum = [None] * L
+        self._staged = [False] * L
+        self._held_active = [False] * L
+        self._retrieval_ready_cpu = [None] * L
+        self.workspace = Workspace(k_pre.device)
+        self._inited = True
+
+    def set_rotary(self, inv_freq: torch.Tensor, attention_scaling: float = 1.0):
+        """Rotary parameters for re-rotating retrieved keys (instead of the active module)."""
+        self.rotary = (inv_freq, float(attention_scaling))
+
+    def _rotary_params(self):
+        if self.rotary is not None:
+            return self.rotary
+        from . import patch
+        rot = patch.ACTIVE_ROTARY_EMB
+        if rot is None:
+            raise RuntimeError("ACTIVE_ROTARY_EMB is None. Call set_active_rotary_emb(model.model.rotary_emb).")
+        return rot.inv_freq, float(getattr(rot, "attention_scaling", 1.0))
+
+    def arena(self, layer_idx: int, Hq: int, dtype, device) -> LayerArena:
+        li = int(layer_idx)
+        a = self.arenas[li]
+        if a is None:
+            inv_freq, sc = self._rotary_params()
+            a = LayerArena(n_seq=self.B, Hq=int(Hq), Hk=self.Hk, D=self.D, F=self.faiss_dim, dtype=dtype,
+                           device=device, budgets=self.max_capacity_prompt, r_max=max(self.lookahead_k, 0),
+                           ccap=self.cpu_buffer_size, p_max=max(self.query_pool_size, 1), policy=self.policy,
+                           recent=self.recent_size, topk_ratio=self.topk_ratio, pool_kernel=self.pool_kernel,
+                           pooling=self.pooling, normalize=self.normalize_for_ip, inv_freq=inv_freq,
+                           rope_scaling=sc, workspace=self.workspace,
+                           hot_cap_hint=None if self.max_capacity_prompt < (1 << 16) else 4096)
+            self.arenas[li] = a
+        return a
+
+    # ------------------------------------------------------------------ cold store
+    def cold_size(self, layer_idx: int) -> int:
+        if not self._inited or self.arenas[int(layer_idx)] is None:
+            return 0
+        return int(self.arenas[int(layer_idx)].cold_count.sum())
+
+    def _count_eviction(self, ev: np.ndarray):
+        if int(ev.max(initial=0)) > 0:
+            self.dbg["compress_calls"] += 1
+            self.dbg["evicted_tokens"] += int(ev.sum())
+            self.dbg["faiss_add"] += int(np.minimum(ev, self.cpu_buffer_size).sum())
+
+    def add_evicted_to_cold_store(self, layer_idx: int, ev: EvictedKV):
+        """controller.py:190-238: append evicted tokens (host or device tensors) to the
+        layer's cold rings; tokens whose evicted_idx is negative are skipped."""
+        if not self._inited:
+            raise RuntimeError("KVController not initialized")
+        li = int(layer_idx)
+        a = self.arenas[li]
+        if a is None:
+            dev = ev.k_pre_cpu.device if ev.k_pre_cpu.is_cuda else self.workspace.device
+            a = self.arena(li, self.Hk, ev.k_pre_cpu.dtype if ev.k_pre_cpu.is_floating_point() else torch.float32,
+                           dev)
+        kp = ev.k_pre_cpu.to(device=a.device, dtype=a.dtype)
+        vv = ev.v_cpu.to(device=a.device, dtype=a.dtype)
+        m = a.cold_append(kp, vv, ev.pos_cpu, ev.evicted_idx)
+        self.dbg["faiss_add"] += int(np.minimum(m, self.cpu_buffer_size).sum())
+
+    @property
+    def cpu_kpre_ring(self):
+        return [[_RingView(self, li, b, "kpre") for b in range(self.B)] for li in range(self.n_layers or 0)]
+
+    @property
+    def cpu_v_ring(self):
+        return [[_RingView(self, li, b, "v") for b in range(self.B)] for li in range(self.n_layers or 0)]
+
+    @property
+    def cpu_pos_ring(self):
+        return [[_RingView(self, li, b, "pos") for b in range(self.B)] for li in range(self.n_layers or 0)]
+
+    @property
+    def index(self):
+        return [[_IndexView(self, li, b) for b in range(self.B)] for li in range(self.n_layers or 0)]
+
+    # ------------------------------------------------------------------ vectors (host helpers)
+    def _pad_or_crop(self, x: torch.Tensor, dim: int) -> torch.Tensor:
+        if x.shape[-1] > dim:
+            return x[..., :dim]
+        if x.shape[-1] < dim:
+            return F.pad(x, (0, dim - x.shape[-1]))
+        return x
+
+    def _normalize(self, x: torch.Tensor, dim: int = -1) -> torch.Tensor:
+        return F.normalize(x, dim=dim) if self.normalize_for_ip else x
+
+    def _k_token_to_vec_np(self, kpre_token: torch.Tensor) -> np.ndarray:
+        """controller.py:178-182 (host helper): head-mean, pad/crop, normalise."""
+        v = kpre_token.detach().float().cpu().mean(dim=0)
+        v = self._normalize(self._pad_or_crop(v, self.faiss_dim), dim=0)
+        return v.numpy().astype("float32", copy=False)
+
+    def _q_to_vecs_np(self, q_pre: torch.Tensor) -> np.ndarray:
+        """controller.py:184-188 (host helper)."""
+        q = q_pre.detach().mean(dim=1).mean(dim=1)
+        q = self._normalize(self._pad_or_crop(q, self.faiss_dim), dim=-1)
+        return q.float().cpu().numpy().astype("float32", copy=False)
+
+    # ------------------------------------------------------------------ query pool and retrieval
+    def update_query_window(self, layer_idx: int, q_pre: torch.Tensor):
+        """controller.py:240-241: push a (B,Hq,T,D) pre-RoPE query into the pool. The decode
+        path pushes inside its append kernel; this entry serves direct callers."""
+        li = int(layer_idx)
+        a = self.arena(li, q_pre.shape[1], q_pre.dtype, q_pre.device)
+        T = int(q_pre.shape[2])
+        if T == 1:
+            m = q_pre.detach().mean(dim=1)[:, 0]  # (B,D), model dtype
+            head = a.st[:, 6].long()
+            a.qwin[torch.arange(a.n_seq, device=a.device), head] = m.to(a.dtype)
+            a.st[:, 6] = ((head + 1) % a.p_max).to(torch.int32)
+            self._qpool[li].append(1)
+        else:
+            self._prompt_qsum[li] = a.prompt_query_sum(q_pre)
+            self._qpool[li].append(("prompt", T))
+
+    def _pool(self, li: int):
+        n_pool, extra_n = 0, 0
+        for e in self._qpool[li]:
+            if isinstance(e, tuple):
+                extra_n = e[1]
+            else:
+                n_pool += 1
+        return n_pool, (self._prompt_qsum[li] if extra_n else None), extra_n
+
+    def _retrieve(self, li: int, **kw):
+        self.arenas[li].retrieve(**kw)
+        self.dbg["retrieval_ready_cpu"] += 1   # some sequence has a non-empty ring: hits are valid
+        self.dbg["prefetch_launched"] += 1
+        self._staged[li] = True
+
+    def launch_retrieval_now(self, layer_idx: int, q_pre: torch.Tensor):
+        """controller.py:295-312: one retrieval from the given pre-RoPE queries
+        (B,Hq,P,D), used at the end of the prompt."""
+        if self.lookahead_k <= 0 or not self._inited:
+            return
+        li = int(layer_idx)
+        if self.cold_size(li) == 0:
+            self.dbg["retrieval_skipped_no_cold"] += 1
+            return
+        self._retrieve(li, q_dense=q_pre)
+        self.dbg["retrieval_launched"] += 1
+        self.dbg["retrieval_launched_prefill"] += 1
+
+    def maybe_launch_async_retrieval(self, layer_idx: int):
+        """controller.py:314-342: count the forward call; every window_size calls search
+        the cold store with the pooled queries."""
+        if self.lookahead_k <= 0:
+            return
+        li = int(layer_idx)
+        self.step_count[li] += 1
+        if self.step_count[li] % self.window_size != 0:
+            return
+        if not self._inited:
+            return
+        if self.cold_size(li) == 0:
+            self.dbg["retrieval_skipped_no_cold"] += 1
+            return
+        n_pool, extra, extra_n = self._pool(li)
+        if n_pool == 0 and extra_n == 0:
+            return
+        self._retrieve(li, n_pool=n_pool, extra_sum=extra, extra_n=extra_n)
+        self.dbg["retrieval_launched"] += 1
+
+    def maybe_prefetch_to_gpu(self, layer_idx: int, device=None, dtype=None):
+        """controller.py:344-380. The cold tier already lives in HBM and retrieval writes the
+        held segment directly, so there is nothing to copy."""
+        return None
+
+    def _retrieval_worker(self, layer_idx: int, q_vecs):
+        """controller.py:250-293 with given query vectors (B, faiss_dim): search, gather and
+        re-rotate into the held segment; the gathered pre-RoPE pack is also kept in
+        _retrieval_ready_cpu[layer_idx] as (k_pre, v, pos, valid) device tensors."""
+        li = int(layer_idx)
+        a = self.arenas[li]
+        if a is None:
+            return
+        qv = torch.as_tensor(np.asarray(q_vecs, dtype=np.float32)).to(a.device).reshape(a.n_seq, self.faiss_dim)
+        if self.cold_size(li) == 0:
+            self._retrieval_ready_cpu[li] = None
+            self.dbg["retrieval_ready_empty"] += 1
+            return
+        a.retrieve(qvec=qv.contiguous())
+        self._retrieval_ready_cpu[li] = self._held_pack(li)
+        self._staged[li] = True
+        self.dbg["retrieval_ready_cpu"] += 1
+
+    def _held_pack(self, li: int):
+        a = self.arenas[li]
+        R = a.r_max
+        src = a.held_src[:, :R].long()
+        valid = a.held_valid[:, :R].bool()
+        idx = src.clamp(min=0)
+        kpre = torch.stack([a.cold_kpre[b].index_select(0, idx[b]) for b in range(a.n_seq)], 0)  # (B,R,Hk,D)
+        vv = torch.stack([a.cold_v[b].index_select(0, idx[b]) for b in range(a.n_seq)], 0)
+        m = valid[:, :, None, None]
+        kpre = torch.where(m, kpre, torch.zeros_like(kpre)).permute(0, 2, 1, 3).contiguous()
+        vv = torch.where(m, vv, torch.zeros_like(vv)).permute(0, 2, 1, 3).contiguous()
+        return kpre, vv, a.held_pos[:, :R].clone(), valid
+
+    def poll_staged_gpu(self, layer_idx: int) -> RetrievedKV:
+        """controller.py:382-442: the retrieved set staged since the last poll, if any."""
+        li = int(layer_idx)
+        if not self._inited or not self._staged[li]:
+            return RetrievedKV(k_pre=torch.empty(0), v=torch.empty(0), pos=torch.empty(0, dtype=torch.long),
+                               valid=torch.empty(0, dtype=torch.bool), ready=False)
+        self._staged[li] = False
+        self.dbg["prefetch_ready"] += 1
+        kpre, vv, pos, valid = self._held_pack(li)
+        return RetrievedKV(k_pre=kpre, v=vv, pos=pos, valid=valid, ready=True)
+
+    @property
+    def held_mem(self):
+        """Per layer: (k_post, v, pos, valid) of the held set while it is attended, else None
+        (patch.py:252-261)."""
+        out = []
+        for li in range(self.n_layers or 0):
+            a = self.arenas[li]
+            if a is None or not self._held_active[li]:
+                out.append(None)
+            else:
+                R = a.r_max
+                out.append((a.held_k[:, :, :R], a.held_v[:, :, :R], a.held_pos[:, :R], a.held_valid[:, :R].bool()))
+        return out
+
+    # ------------------------------------------------------------------ the per-layer hot path
+    def prefill_layer(self, layer_idx: int, q_pre, q_post, k_pre, k_post, v, positions):
+        """The prompt forward of one layer (patch.py:159-233): query pool, schedule,
+        compression of the prompt into the hot slab with eviction into the cold ring,
+        and the prompt-end retrieval. Tensors (B,H,T,D); positions (B,T) int64."""
+        li = int(layer_idx)
+        a = self.arena(li, q_pre.shape[1], k_post.dtype, k_post.device)
+        T = int(k_post.shape[2])
+        if self.query_pool_size >= self.window_size:
+            self.update_query_window(li, q_pre)
+        self.maybe_launch_async_retrieval(li)
+        r = self.recent_size
+        q_obs = q_post if T <= r else q_post[:, :, -r:, :]
+        ev = a.compress_prompt(q_obs, k_post, v, k_pre, positions.to(k_post.device, torch.int64))
+        self._count_eviction(ev)
+        self.dbg["triton_prefill_fallback"] += 1
+        if self.retrieve_after_prefill:
+            self.launch_retrieval_now(li, q_pre[:, :, -self.query_pool_size:, :])
+
+    def decode_layer(self, layer_idx: int, q_pre, k_pre, v, cos, sin, pos):
+        """One decode step of one layer (patch.py:151-315): RoPE + append + query-pool push,
+        scheduled retrieval into the held segment, compression with eviction, and
+        attention over [held | hot]. q_pre (B,Hq,D), k_pre/v (B,Hk,D), cos/sin (B,D) in the
+        model dtype or None, pos (B,) int64 on the device. Returns (B,Hq,D)."""
+        li = int(layer_idx)
+        a = self.arena(li, q_pre.shape[1], k_pre.dtype, k_pre.device)
+        q_post = a.append(q_pre, k_pre, v, cos, sin, pos)
+        self._qpool[li].append(1)
+        self.maybe_launch_async_retrieval(li)
+        ev = a.compress_decode(q_post.view(a.n_seq, a.Hq, 1, a.D))
+        self._count_eviction(ev)
+        use_held = False
+        if self._staged[li]:
+            self._staged[li] = False
+            self.dbg["prefetch_ready"] += 1
+            use_held = True
+            if self.hold_retrieved:
+                self._held_active[li] = True
+                self.dbg["injection_new"] += 1
+        elif self.hold_retrieved and self._held_active[li]:
+            use_held = True
+        if not self.hold_retrieved:
+            self._held_active[li] = use_held
+        self.last_injected_len = a.r_max if use_held else 0
+        if use_held:
+            self.dbg["injection_used"] += 1
+        self.dbg["triton_decode_calls"] += 1
+        return a.attend(q_post, pos, use_held, self.overflow_nan)
+
+    def device_status(self) -> int:
+        """OR of the device status words of every layer (synchronises): HC_DEV_* bits."""
+        bits = 0
+        for a in self.arenas:
+            if a is not None:
+                bits |= int(np.bitwise_or.reduce(a.st[:, 8].cpu().numpy()))
+        return bits

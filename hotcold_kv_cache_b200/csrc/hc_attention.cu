@@ -1,0 +1,474 @@
+// Split-K decode attention (flash-decode) for the hot/cold path.
+//
+// Replaces the reference's Triton kernel evict_fwd_kernel (kernels.py:9-74), which
+// runs one program per (batch, query head) over all keys and so reads each KV head
+// once per query head of its GQA group. Here one CTA owns (sequence, KV head, chunk
+// of CH tokens): its G = Hq/Hk query heads share a single read of the chunk's K and V
+// rows, which arrive in shared memory by cp.async.bulk (one 16-byte aligned row copy
+// per token, completing on an mbarrier). Scores use 8 lanes per token with 128-bit
+// shared loads; each CTA writes a partial (max, sum, output) per query head and the
+// last CTA of a (sequence, KV head) to finish merges the partials (counter in global
+// memory, reset by that CTA).
+//
+// Token list of a sequence in slab mode: [held segment (held_len slots) | hot tokens in
+// logical order through hot_ord]. Held slot j is attended iff held_valid[j] and
+// held_pos[j] <= cur_pos (patch.py:287-289). Dense mode reads (B,Hk,S,D) tensors with a
+// (B,S) mask, the drop-in for triton_evict_attention_forward (kernels.py:77-137).
+//
+// Softmax: the reference exponentiates raw scores (kernels.py:146); it equals the stable
+// form computed here except when a logit overflows fp32 exp, where the reference returns
+// NaN — reproduced when overflow_nan is set. No unmasked token gives 0/0 = NaN in both.
+
+#include "hc_internal.cuh"
+
+namespace hc {
+
+
+constexpr int kAttnThreads = 128;
+
+template <int DT, int D, int G, int CH>
+struct AttnSmem {
+  using T = typename Elem<DT>::T;
+  static constexpr size_t kOff = 0;
+  static constexpr size_t vOff = kOff + sizeof(T) * CH * D;
+  static constexpr size_t qOff = vOff + sizeof(T) * CH * D;
+  static constexpr size_t sOff = qOff + sizeof(float) * G * D;
+  static constexpr size_t mlOff = sOff + sizeof(float) * G * CH;
+  static constexpr size_t validOff = mlOff + sizeof(float) * 2 * G;
+  static constexpr size_t barOff = (validOff + sizeof(int) * CH + 15) & ~size_t(15);
+  static constexpr size_t miscOff = barOff + 16;
+  static constexpr size_t bytes = miscOff + 16;
+};
+
+template <int DT, int D, int G, int CH, bool DENSE>
+__global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  using SM = AttnSmem<DT, D, G, CH>;
+  constexpr int ROWB = D * sizeof(T);
+  constexpr int VEC = 16 / sizeof(T);   // elements per 16-byte load
+  constexpr int NJ = D / (8 * VEC);     // 16-byte loads per lane per row (8 lanes per row)
+  static_assert(NJ >= 1, "head dim too small");
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  T* sK = reinterpret_cast<T*>(smem + SM::kOff);
+  T* sV = reinterpret_cast<T*>(smem + SM::vOff);
+  float* sQ = reinterpret_cast<float*>(smem + SM::qOff);
+  float* sS = reinterpret_cast<float*>(smem + SM::sOff);
+  float* sML = reinterpret_cast<float*>(smem + SM::mlOff);
+  int* sValid = reinterpret_cast<int*>(smem + SM::validOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::barOff);
+  int* sMisc = reinterpret_cast<int*>(smem + SM::miscOff);
+
+  const int c = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  pdl_wait();
+
+  // ---- token range of this chunk -------------------------------------------------------
+  int n_held = 0, n_tok;
+  hc_seq_desc d;
+  hc_seq_state* st = nullptr;
+  if constexpr (DENSE) {
+    n_tok = a.S;
+  } else {
+    d = a.desc[s];
+    st = d.st;
+    n_held = a.use_held ? max(0, min(st->held_len, d.r_max)) : 0;
+    n_tok = n_held + max(0, min(st->n_hot, d.cap));
+  }
+  const int n_chunks = (n_tok + CH - 1) / CH;
+  if (c >= n_chunks) return;
+  const int t0 = c * CH;
+  const int nt = min(CH, n_tok - t0);
+
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  // query heads of this KV head -> shared (float)
+  const T* qg = reinterpret_cast<const T*>(a.q) + ((size_t)s * a.Hq + (size_t)h * G) * D;
+  for (int i = tid; i < G * D; i += kAttnThreads) sQ[i] = E::to_f(qg[i]);
+  __syncthreads();
+
+  // ---- resolve rows and issue the bulk copies -------------------------------------------
+  const T* krow = nullptr;
+  const T* vrow = nullptr;
+  bool copy = false;
+  if (tid < nt) {
+    const int t = t0 + tid;
+    int valid = 1;
+    if constexpr (DENSE) {
+      const size_t off = (((size_t)s * a.Hk + h) * a.S + t) * D;
+      krow = reinterpret_cast<const T*>(a.k) + off;
+      vrow = reinterpret_cast<const T*>(a.v) + off;
+      valid = a.mask[(size_t)s * a.S + t] != 0;
+      copy = true;
+    } else if (t < n_held) {
+      const size_t off = ((size_t)h * d.r_max + t) * D;
+      krow = reinterpret_cast<const T*>(d.held_k) + off;
+      vrow = reinterpret_cast<const T*>(d.held_v) + off;
+      valid = d.held_valid[t] != 0 && d.held_pos[t] <= a.cur_pos[s];
+      copy = true;
+    } else {
+      const int slot = d.hot_ord[t - n_held];
+      if (slot >= 0 && slot < d.cap) {
+        const size_t off = ((size_t)h * d.cap + slot) * D;
+        krow = reinterpret_cast<const T*>(d.hot_k) + off;
+        vrow = reinterpret_cast<const T*>(d.hot_v) + off;
+        copy = true;
+      } else {
+        valid = 0;
+        set_status(st, HC_DEV_INDEX);
+      }
+    }
+    sValid[tid] = valid;
+  }
+  const int n_copy = __syncthreads_count(copy);
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], (uint32_t)(n_copy * ROWB));
+    mbar_arrive_expect_tx(&bars[1], (uint32_t)(n_copy * ROWB));
+  }
+  if (copy) {
+    bulk_g2s(sK + (size_t)tid * D, krow, ROWB, &bars[0]);
+    bulk_g2s(sV + (size_t)tid * D, vrow, ROWB, &bars[1]);
+  } else if (tid < nt) {
+    for (int i = 0; i < D; ++i) {
+      sK[(size_t)tid * D + i] = E::from_f(0.f);
+      sV[(size_t)tid * D + i] = E::from_f(0.f);
+    }
+  }
+  // q fragments in registers: lane `sub` owns d = j*8*VEC + sub*VEC + e
+  const int sub = lane & 7, tk = lane >> 3;
+  float qr[G][NJ * VEC];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) qr[g][j * VEC + e] = sQ[g * D + j * 8 * VEC + sub * VEC + e];
+
+  if (!__syncthreads_and(mbar_wait(&bars[0], 0))) {
+    if (tid == 0) set_status(st, HC_DEV_TIMEOUT);
+    mbar_wait(&bars[1], 0);  // bounded: give copies in flight a last chance to land
+    mbar_wait(&bars[0], 0);
+    return;
+  }
+
+  // ---- scores: 4 tokens per warp per pass, 8 lanes per token ----------------------------
+  for (int base = warp * 4; base < nt; base += 16) {
+    const int t = base + tk;
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.f;
+    if (t < nt) {
+      const T* row = sK + (size_t)t * D;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        uint4 u = *reinterpret_cast<const uint4*>(row + j * 8 * VEC + sub * VEC);
+        float kf[VEC];
+        unpack16<DT>(u, kf);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[g] = fmaf(qr[g][j * VEC + e], kf[e], acc[g]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 4);
+      acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 2);
+      acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
+    }
+    if (sub == 0 && t < nt) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) sS[g * CH + t] = sValid[t] ? acc[g] * a.scale : kNegInf;
+    }
+  }
+  __syncthreads();
+
+  // ---- chunk softmax statistics, probabilities in place ---------------------------------
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    float m = kNegInf;
+    for (int t = lane; t < nt; t += 32) m = fmaxf(m, sS[g * CH + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      const float x = sS[g * CH + t];
+      const float p = (x == kNegInf) ? 0.f : __expf(x - m);
+      sS[g * CH + t] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      sML[g] = m;
+      sML[G + g] = l;
+    }
+  }
+  if (!__syncthreads_and(mbar_wait(&bars[1], 0))) {
+    if (tid == 0) set_status(st, HC_DEV_TIMEOUT);
+    mbar_wait(&bars[1], 0);
+    return;
+  }
+
+  // ---- P.V: thread d owns output column d for every query head ----------------------------
+  float o[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) o[g] = 0.f;
+  if (tid < D) {
+    for (int t = 0; t < nt; ++t) {
+      const float vv = E::to_f(sV[(size_t)t * D + tid]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) o[g] = fmaf(sS[g * CH + t], vv, o[g]);
+    }
+  }
+
+  const size_t head0 = (size_t)s * a.Hq + (size_t)h * G;
+  T* outp = reinterpret_cast<T*>(a.out);
+  if (n_chunks == 1) {
+    if (tid < D) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float r = o[g] / sML[G + g];
+        if (a.overflow_nan && sML[g] >= kExpOverflow) r = __int_as_float(0x7fc00000);
+        outp[(head0 + g) * D + tid] = E::from_f(r);
+      }
+    }
+    if (a.ml && tid < G) {
+      a.ml[(head0 + tid) * 2] = sML[tid];
+      a.ml[(head0 + tid) * 2 + 1] = sML[G + tid];
+    }
+    pdl_launch_dependents();
+    return;
+  }
+
+  // ---- partials, then the last CTA of this (sequence, KV head) merges them ---------------
+  constexpr int PSTRIDE = G * D + 2 * G;
+  float* pbase = a.part + ((size_t)s * a.Hk + h) * (size_t)a.max_chunks * PSTRIDE;
+  float* mine = pbase + (size_t)c * PSTRIDE;
+  if (tid < D) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) mine[g * D + tid] = o[g];
+  }
+  if (tid < 2 * G) mine[G * D + tid] = sML[tid];
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(&a.counters[(size_t)s * a.Hk + h], 1);
+    sMisc[0] = (prev == n_chunks - 1);
+  }
+  __syncthreads();
+  if (!sMisc[0]) return;
+  __threadfence();
+  if (tid == 0) a.counters[(size_t)s * a.Hk + h] = 0;
+
+  if (tid < D) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float M = kNegInf;
+      for (int cc = 0; cc < n_chunks; ++cc) M = fmaxf(M, pbase[(size_t)cc * PSTRIDE + G * D + g]);
+      float L = 0.f, O = 0.f;
+      for (int cc = 0; cc < n_chunks; ++cc) {
+        const float* pc = pbase + (size_t)cc * PSTRIDE;
+        const float w = __expf(pc[G * D + g] - M);
+        L = fmaf(pc[G * D + G + g], w, L);
+        O = fmaf(pc[g * D + tid], w, O);
+      }
+      float r = O / L;
+      if (a.overflow_nan && M >= kExpOverflow) r = __int_as_float(0x7fc00000);
+      outp[(head0 + g) * D + tid] = E::from_f(r);
+      if (a.ml && tid == 0) {
+        a.ml[(head0 + g) * 2] = M;
+        a.ml[(head0 + g) * 2 + 1] = L;
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// Second output of the dense drop-in (kernels.py:103,134-137): per token the mean over query
+// heads of softmax probability times sum_d |v_d| / D, rounded to the input dtype; masked
+// tokens contribute exactly 0 (the reference's exp(-1e35)).
+template <int DT, int D, int G>
+__global__ void __launch_bounds__(128) evict_loss_kernel(const void* q_, const void* k_, const void* v_,
+                                                         const uint8_t* mask, const float* ml, float* loss,
+                                                         int Hq, int Hk, int S, float scale) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  const int b = blockIdx.y;
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= S) return;
+  const T* q = reinterpret_cast<const T*>(q_) + (size_t)b * Hq * D;
+  float acc = 0.f;
+  const bool m = mask[(size_t)b * S + t] != 0;
+  for (int h = 0; h < Hk; ++h) {
+    const T* kr = reinterpret_cast<const T*>(k_) + (((size_t)b * Hk + h) * S + t) * D;
+    const T* vr = reinterpret_cast<const T*>(v_) + (((size_t)b * Hk + h) * S + t) * D;
+    float av = 0.f;
+    for (int dd = lane; dd < D; dd += 32) av += fabsf(E::to_f(vr[dd]));
+    av = warp_sum(av) / (float)D;
+    for (int g = 0; g < G; ++g) {
+      const int hq = h * G + g;
+      float dot = 0.f;
+      for (int dd = lane; dd < D; dd += 32) dot = fmaf(E::to_f(q[(size_t)hq * D + dd]), E::to_f(kr[dd]), dot);
+      dot = warp_sum(dot) * scale;
+      const float M = ml[((size_t)b * Hq + hq) * 2], L = ml[((size_t)b * Hq + hq) * 2 + 1];
+      const float p = m ? __expf(dot - M) / L : 0.f;
+      acc += p * av;
+    }
+  }
+  if (lane == 0) loss[(size_t)b * S + t] = E::round(acc / (float)Hq);
+}
+
+__global__ void __launch_bounds__(1024) argmin_kernel(const float* loss, int S, int64_t* out) {
+  const int b = blockIdx.x;
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  float best = __int_as_float(0x7f800000);
+  int bi = 0x7fffffff;
+  for (int t = threadIdx.x; t < S; t += blockDim.x) {
+    const float x = loss[(size_t)b * S + t];
+    if (x < best || (x == best && t < bi)) {
+      best = x;
+      bi = t;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob < best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] < best || (sv[w] == best && si[w] < bi)) {
+        best = sv[w];
+        bi = si[w];
+      }
+    out[b] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// host launchers
+// ------------------------------------------------------------------------------------------
+template <int DT, int D, int G, int CH, bool DENSE>
+cudaError_t launch_attn_t(const AttnArgs& a, int n_seq, cudaStream_t stream) {
+  using SM = AttnSmem<DT, D, G, CH>;
+  auto kern = attn_kernel<DT, D, G, CH, DENSE>;
+  cudaError_t e = ensure_smem(kern, SM::bytes);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.max_chunks, a.Hk, n_seq);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = SM::bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <int DT, int D, int CH, bool DENSE>
+cudaError_t launch_attn_g(const AttnArgs& a, int G, int n_seq, cudaStream_t stream) {
+  switch (G) {
+    case 1: return launch_attn_t<DT, D, 1, CH, DENSE>(a, n_seq, stream);
+    case 2: return launch_attn_t<DT, D, 2, CH, DENSE>(a, n_seq, stream);
+    case 4: return launch_attn_t<DT, D, 4, CH, DENSE>(a, n_seq, stream);
+    case 8: return launch_attn_t<DT, D, 8, CH, DENSE>(a, n_seq, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int DT, bool DENSE>
+cudaError_t launch_attn_d(const AttnArgs& a, int D, int G, int CH, int n_seq, cudaStream_t stream) {
+  if (D == 128) {
+    if (CH == 32) return launch_attn_g<DT, 128, 32, DENSE>(a, G, n_seq, stream);
+    return launch_attn_g<DT, 128, 64, DENSE>(a, G, n_seq, stream);
+  }
+  if (D == 64) {
+    if (CH == 32) return launch_attn_g<DT, 64, 32, DENSE>(a, G, n_seq, stream);
+    return launch_attn_g<DT, 64, 64, DENSE>(a, G, n_seq, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// Chunk length: 32 tokens when the whole batch would otherwise fill fewer than ~2 waves
+// of 148 SMs, else 64.
+int attn_chunk(int n_seq, int Hk, int max_tokens) {
+  const long ctas64 = (long)n_seq * Hk * ((max_tokens + 63) / 64);
+  return ctas64 < 296 ? 32 : 64;
+}
+
+cudaError_t launch_attention(const AttnArgs& a0, int dtype, int D, int G, int n_seq, int max_tokens, bool dense,
+                             cudaStream_t stream) {
+  AttnArgs a = a0;
+  const int CH = attn_chunk(n_seq, a.Hk, max_tokens);
+  a.max_chunks = (max_tokens + CH - 1) / CH;
+  if (a.max_chunks < 1) a.max_chunks = 1;
+  if (dense) {
+    switch (dtype) {
+      case HC_F32: return launch_attn_d<HC_F32, true>(a, D, G, CH, n_seq, stream);
+      case HC_F16: return launch_attn_d<HC_F16, true>(a, D, G, CH, n_seq, stream);
+      case HC_BF16: return launch_attn_d<HC_BF16, true>(a, D, G, CH, n_seq, stream);
+    }
+  } else {
+    switch (dtype) {
+      case HC_F32: return launch_attn_d<HC_F32, false>(a, D, G, CH, n_seq, stream);
+      case HC_F16: return launch_attn_d<HC_F16, false>(a, D, G, CH, n_seq, stream);
+      case HC_BF16: return launch_attn_d<HC_BF16, false>(a, D, G, CH, n_seq, stream);
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+size_t attention_part_bytes(int n_seq, int Hq, int Hk, int D, int max_tokens) {
+  const int G = Hq / Hk;
+  const size_t chunks = (size_t)(max_tokens + 31) / 32 + 1;
+  return (size_t)n_seq * Hk * chunks * (size_t)(G * D + 2 * G) * sizeof(float);
+}
+
+template <int DT, int D, int G>
+cudaError_t launch_loss_t(const void* q, const void* k, const void* v, const uint8_t* mask, const float* ml,
+                          float* loss, int B, int Hq, int Hk, int S, float scale, cudaStream_t stream) {
+  evict_loss_kernel<DT, D, G><<<dim3((S + 3) / 4, B), 128, 0, stream>>>(q, k, v, mask, ml, loss, Hq, Hk, S, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_evict_idx(int dtype, const void* q, const void* k, const void* v, const uint8_t* mask,
+                             const float* ml, float* loss, int64_t* out, int B, int Hq, int Hk, int S, int D,
+                             float scale, cudaStream_t stream) {
+  const int G = Hq / Hk;
+  cudaError_t e = cudaErrorInvalidValue;
+#define HC_LOSS_CASE(DTV)                                                                          \
+  if (dtype == DTV) {                                                                              \
+    if (D == 128 && G == 1) e = launch_loss_t<DTV, 128, 1>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream); \
+    if (D == 128 && G == 2) e = launch_loss_t<DTV, 128, 2>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream); \
+    if (D == 128 && G == 4) e = launch_loss_t<DTV, 128, 4>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream); \
+    if (D == 128 && G == 8) e = launch_loss_t<DTV, 128, 8>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream); \
+    if (D == 64 && G == 1) e = launch_loss_t<DTV, 64, 1>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream);   \
+    if (D == 64 && G == 2) e = launch_loss_t<DTV, 64, 2>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream);   \
+    if (D == 64 && G == 4) e = launch_loss_t<DTV, 64, 4>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream);   \
+    if (D == 64 && G == 8) e = launch_loss_t<DTV, 64, 8>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream);   \
+  }
+  HC_LOSS_CASE(HC_F32)
+  HC_LOSS_CASE(HC_F16)
+  HC_LOSS_CASE(HC_BF16)
+#undef HC_LOSS_CASE
+  if (e != cudaSuccess) return e;
+  argmin_kernel<<<B, 1024, 0, stream>>>(loss, S, out);
+  return cudaGetLastError();
+}
+
+}  // namespace hc

@@ -1,0 +1,242 @@
+// Shared device helpers for the hot/cold decode kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/hotcold_b200.h"
+
+namespace hc {
+
+constexpr float kNegInf = -__builtin_huge_valf();
+// Logits at or above this value overflow float32 exp (ln(FLT_MAX) rounded up).
+constexpr float kExpOverflow = 88.72283935546875f;
+// Upper bound on mbarrier polls before a wait gives up and reports HC_DEV_TIMEOUT; each poll
+// suspends for at most kPollSuspendNs, so a wait ends within about a second.
+constexpr int kMaxPolls = 1 << 20;
+constexpr uint32_t kPollSuspendNs = 1000;
+
+// ----------------------------------------------------------------------------------------
+// element types
+// ----------------------------------------------------------------------------------------
+template <int DT> struct Elem;
+template <> struct Elem<HC_F32> {
+  using T = float;
+  static __device__ __forceinline__ float load(const T* p) { return *p; }
+  static __device__ __forceinline__ float to_f(T x) { return x; }
+  static __device__ __forceinline__ T from_f(float x) { return x; }
+  static __device__ __forceinline__ float round(float x) { return x; }
+};
+template <> struct Elem<HC_F16> {
+  using T = __half;
+  static __device__ __forceinline__ float load(const T* p) { return __half2float(*p); }
+  static __device__ __forceinline__ float to_f(T x) { return __half2float(x); }
+  static __device__ __forceinline__ T from_f(float x) { return __float2half_rn(x); }
+  static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+};
+template <> struct Elem<HC_BF16> {
+  using T = __nv_bfloat16;
+  static __device__ __forceinline__ float load(const T* p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ float to_f(T x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ T from_f(float x) { return __float2bfloat16_rn(x); }
+  static __device__ __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+};
+
+// Unpack a 16-byte vector of elements into floats.
+template <int DT>
+__device__ __forceinline__ void unpack16(const uint4& u, float* f) {
+  if constexpr (DT == HC_F32) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  } else {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (DT == HC_F16) {
+        __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+        float2 t = __half22float2(h);
+        f[2 * i] = t.x; f[2 * i + 1] = t.y;
+      } else {
+        __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+        float2 t = __bfloat1622float2(h);
+        f[2 * i] = t.x; f[2 * i + 1] = t.y;
+      }
+    }
+  }
+}
+
+// RoPE on one element pair, rounded like HF's apply_rotary_pos_emb in the model dtype:
+// out = round(round(x*c) + round(rot*s)), each product and the sum a separate op.
+template <int DT>
+__device__ __forceinline__ float rope_elem(float x, float rot, float c, float s) {
+  using E = Elem<DT>;
+  float a = E::round(__fmul_rn(x, c));
+  float b = E::round(__fmul_rn(rot, s));
+  return E::round(__fadd_rn(a, b));
+}
+
+// cos/sin of HF's LlamaRotaryEmbedding at one position for frequency index i:
+// float32 angle inv_freq[i]*float(pos), float32 cos/sin, times attention_scaling,
+// rounded to the model dtype.
+template <int DT>
+__device__ __forceinline__ void rope_cs(float inv_freq, int64_t pos, float scaling, float& c, float& s) {
+  float ang = __fmul_rn(inv_freq, (float)pos);
+  c = Elem<DT>::round(__fmul_rn(cosf(ang), scaling));
+  s = Elem<DT>::round(__fmul_rn(sinf(ang), scaling));
+}
+
+// ----------------------------------------------------------------------------------------
+// warp / block reductions
+// ----------------------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Exclusive prefix sum of one int per thread over the block; returns the block total.
+// `sh` needs blockDim.x/32 + 1 ints. All threads must call.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* sh, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) sh[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? sh[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) sh[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  int before = (warp > 0 ? sh[warp - 1] : 0) + x - v;
+  total = sh[nw - 1];
+  __syncthreads();
+  return before;
+}
+
+// Monotone map float -> uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t fkey(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ----------------------------------------------------------------------------------------
+// TMA bulk copies (cp.async.bulk, non-tensor) completing on an mbarrier
+// ----------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// One bulk global->shared copy of `bytes` (multiple of 16, both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kPollSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on phase `parity`. Returns false after kMaxPolls polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (int i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+__device__ __forceinline__ void set_status(hc_seq_state* st, int bits) {
+  if (st) atomicOr(&st->status, bits);
+}
+
+// ----------------------------------------------------------------------------------------
+// Programmatic dependent launch: let the next kernel in the stream start its prologue,
+// and wait for the previous one before touching its outputs.
+// ----------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ----------------------------------------------------------------------------------------
+// host: launch with programmatic stream serialization, dtype x head-dim dispatch
+// ----------------------------------------------------------------------------------------
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Raise a kernel's dynamic shared memory limit once per device.
+template <typename K>
+inline cudaError_t ensure_smem(K kern, size_t bytes) {
+  static unsigned long long done = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) done |= bit;
+  return e;
+}
+
+#define HC_DISPATCH_DT_D(dtype, D, FN, ...)                                     \
+  do {                                                                          \
+    if ((dtype) == HC_F32 && (D) == 128) return FN<HC_F32, 128>(__VA_ARGS__);   \
+    if ((dtype) == HC_F16 && (D) == 128) return FN<HC_F16, 128>(__VA_ARGS__);   \
+    if ((dtype) == HC_BF16 && (D) == 128) return FN<HC_BF16, 128>(__VA_ARGS__); \
+    if ((dtype) == HC_F32 && (D) == 64) return FN<HC_F32, 64>(__VA_ARGS__);     \
+    if ((dtype) == HC_F16 && (D) == 64) return FN<HC_F16, 64>(__VA_ARGS__);     \
+    if ((dtype) == HC_BF16 && (D) == 64) return FN<HC_BF16, 64>(__VA_ARGS__);   \
+    return cudaErrorInvalidValue;                                               \
+  } while (0)
+
+}  // namespace hc

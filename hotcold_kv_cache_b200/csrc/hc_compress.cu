@@ -1,0 +1,758 @@
+// Hot-tier compression with eviction into the cold ring.
+//
+// Reference flow (HotColdLayer._compress_if_needed, cache.py:37-128): score every hot
+// token, keep the top-n_top of the prefix plus the recent tail, gather the kept tokens,
+// copy the evicted ones to pinned host memory, and hand them to the cold store, which
+// builds one index vector per token in a Python loop (controller.py:190-238). Under
+// HC_POLICY_SNAPKV the score is SnapKV's importance (scoring.py:50-79) averaged over KV
+// heads and the keep set follows keep_index (scoring.py:110-132).
+//
+// Here the whole flow stays in HBM:
+//   score_kernel   (seq, KV head, token chunk): bulk-copies the chunk's post-RoPE keys to
+//                  shared memory and scores them against the GQA-mean observation queries;
+//                  hot/cold: one logit sum per token; SnapKV: one logit per (row, token)
+//                  plus the chunk's softmax partials per row.
+//   stats/token    (large inputs only) SnapKV softmax statistics per row, then per-token
+//                  importance, pooling and the mean over KV heads.
+//   select_kernel  (one CTA per sequence): exact top-k of the prefix (ties to the lower
+//                  index), order-preserving compaction of the logical order, free-slot
+//                  push, ring plan; small evictions are copied inline.
+//   evict_kernel   (large evictions / prompt): payload copies into the cold ring with the
+//                  index vector (mean over KV heads of the pre-RoPE key, pad/crop,
+//                  L2-normalise; controller.py:178-182) and, for a prompt, the kept
+//                  tokens into the slab.
+// Scores are float32 throughout (the reference rounds its GPU logits to the model dtype).
+
+#include "hc_topk.cuh"
+
+namespace hc {
+
+constexpr int kScoreCH = 64;        // tokens per score CTA
+constexpr int kInlineEvict = 32;    // evictions copied by the select CTA itself
+constexpr int kSmallSelect = 1 << 20;  // Hk*tq*S up to which select computes token scores
+
+struct Plan {
+  int S, prefix, ntop, nobs, active;
+};
+
+// cache.py:44-53 (hot/cold) or scoring.py:117-120 with the trigger of cache.py:44 (SnapKV).
+__device__ __forceinline__ Plan make_plan(const hc_layer& L, int budget, int S) {
+  Plan p{S, 0, 0, 0, 0};
+  if (S <= budget) return p;
+  if (L.policy == HC_POLICY_HOTCOLD) {
+    const int recent = min(min(L.recent, budget), S);
+    const int prefix = S - recent;
+    if (prefix <= 0) return p;
+    int ntop = (int)((double)budget * L.topk_ratio);
+    ntop = max(1, min(ntop, prefix));
+    p = Plan{S, prefix, ntop, recent, 1};
+  } else {
+    const int window = min(L.recent, S);
+    const int prefix = S - window;
+    const int ntop = max(0, min(budget - window, prefix));
+    p = Plan{S, prefix, ntop, window, 1};
+  }
+  return p;
+}
+
+struct CompressArgs {
+  hc_layer L;
+  const void* q_obs;
+  int64_t qs_seq, qs_head, qs_tok;
+  int tq;        // query rows provided
+  int S_dense;   // prompt length (dense mode)
+  int S_max;     // row stride of the per-token scratch arrays
+  int max_chunks;
+  const void* src_k;
+  const void* src_v;
+  const void* src_kpre;
+  int64_t ss_seq, ss_head, ss_tok;
+  const int64_t* src_pos;
+  // scratch
+  int* hdr;        // [n_seq][16]: S, prefix, ntop, nobs, active, n_keep_copy, n_evict, tq_used
+  float* logits;   // [n_seq][Hk][tqmax][S_max]   (hot/cold: [n_seq][Hk][S_max])
+  float* part;     // [n_seq][Hk][tqmax][max_chunks][2]
+  float* stats;    // [n_seq][Hk][tqmax][2]
+  float* imp;      // [n_seq][Hk][S_max]
+  float* tok;      // [n_seq][S_max]
+  uint8_t* sel;    // [n_seq][S_max]
+  int* keep_src;   // [n_seq][S_max]
+  int* ev_src;     // [n_seq][S_max]
+  int* ev_dst;     // [n_seq][S_max]
+  int tqmax;
+};
+
+template <bool DENSE>
+__device__ __forceinline__ int seq_len(const CompressArgs& a, const hc_seq_desc& d) {
+  if constexpr (DENSE) return a.S_dense;
+  return d.st->n_hot;
+}
+
+// ------------------------------------------------------------------------------------------
+// score
+// ------------------------------------------------------------------------------------------
+template <int DT, int D, bool DENSE>
+__global__ void __launch_bounds__(128) score_kernel(CompressArgs a) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  constexpr int CH = kScoreCH;
+  constexpr int ROWB = D * sizeof(T);
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int NJ = D / (8 * VEC);
+  extern __shared__ __align__(128) unsigned char smem[];
+  T* sK = reinterpret_cast<T*>(smem);
+  float* sQ = reinterpret_cast<float*>(smem + sizeof(T) * CH * D);      // [tqmax + 1][D]
+  float* sL = sQ + (size_t)(a.tqmax + 1) * D;                             // [tqmax][CH]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sL + (size_t)a.tqmax * CH + 4);
+
+  const int c = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const hc_layer& L = a.L;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
+  if (!pl.active) return;
+  const int S = pl.S;
+  if (c * CH >= S) return;
+  const int t0 = c * CH, nt = min(CH, S - t0);
+  const int tqu = min(pl.nobs, a.tq);
+  const int G = L.Hq / L.Hk;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // key rows of this chunk (an out-of-range slot is reported and read as zeros)
+  const T* row = nullptr;
+  if (tid < nt) {
+    const int t = t0 + tid;
+    if constexpr (DENSE) {
+      row = reinterpret_cast<const T*>(a.src_k) + (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)t * a.ss_tok;
+    } else {
+      const int slot = d.hot_ord[t];
+      if (slot >= 0 && slot < d.cap) row = reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + slot) * D;
+      else set_status(d.st, HC_DEV_INDEX);
+    }
+  }
+  const int n_copy = __syncthreads_count(row != nullptr);
+  if (tid == 0) mbar_arrive_expect_tx(bar, (uint32_t)(n_copy * ROWB));
+  if (row) bulk_g2s(sK + (size_t)tid * D, row, ROWB, bar);
+  else if (tid < nt)
+    for (int i = 0; i < D; ++i) sK[(size_t)tid * D + i] = E::from_f(0.f);
+  // GQA-mean observation rows (cache.py:60-64 / scoring.py:17-26), rounded to the dtype
+  const T* q = reinterpret_cast<const T*>(a.q_obs) + (size_t)s * a.qs_seq;
+  for (int i = tid; i < tqu * D; i += 128) {
+    const int r = i / D, dd = i % D;
+    const int row = a.tq - tqu + r;
+    float acc = 0.f;
+    for (int g = 0; g < G; ++g)
+      acc += E::to_f(q[(size_t)(h * G + g) * a.qs_head + (size_t)row * a.qs_tok + dd]);
+    sQ[i] = E::round(acc / (float)G);
+  }
+  __syncthreads();
+  const bool hotcold = L.policy == HC_POLICY_HOTCOLD;
+  if (hotcold && tid < D) {  // logits are linear in q: sum the rows first
+    float acc = 0.f;
+    for (int r = 0; r < tqu; ++r) acc += sQ[r * D + tid];
+    sQ[(size_t)a.tqmax * D + tid] = acc;  // the extra row holds the sum
+  }
+  if (!__syncthreads_and(mbar_wait(bar, 0))) {
+    if (tid == 0) set_status(d.st, HC_DEV_TIMEOUT);
+    mbar_wait(bar, 0);
+    return;
+  }
+
+  const int sub = lane & 7, tk = lane >> 3;
+  const int nrows = hotcold ? 1 : tqu;
+  const float* qrows = hotcold ? sQ + (size_t)a.tqmax * D : sQ;
+  for (int base = warp * 4; base < nt; base += 16) {
+    const int t = base + tk;
+    float kf[NJ * VEC];
+    if (t < nt) {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        uint4 u = *reinterpret_cast<const uint4*>(sK + (size_t)t * D + j * 8 * VEC + sub * VEC);
+        unpack16<DT>(u, kf + j * VEC);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < NJ * VEC; ++e) kf[e] = 0.f;
+    }
+    for (int r = 0; r < nrows; ++r) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc = fmaf(qrows[r * D + j * 8 * VEC + sub * VEC + e], kf[j * VEC + e], acc);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (sub == 0 && t < nt) {
+        if (hotcold) {
+          a.logits[((size_t)s * L.Hk + h) * a.S_max + t0 + t] = acc;
+        } else {
+          const int tg = t0 + t;
+          // observation row r sits at index S - tqu + r; later keys are masked (scoring.py:72-74)
+          const float x = (tg > S - tqu + r) ? kNegInf : acc * L.scale;
+          sL[r * CH + t] = x;
+          a.logits[(((size_t)s * L.Hk + h) * a.tqmax + r) * a.S_max + tg] = x;
+        }
+      }
+    }
+  }
+  if (hotcold) return;
+  __syncthreads();
+  // chunk softmax partials per observation row
+  for (int r = warp; r < tqu; r += 4) {
+    float m = kNegInf;
+    for (int t = lane; t < nt; t += 32) m = fmaxf(m, sL[r * CH + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      const float x = sL[r * CH + t];
+      l += (x == kNegInf) ? 0.f : __expf(x - m);
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      float* p = a.part + ((((size_t)s * L.Hk + h) * a.tqmax + r) * a.max_chunks + c) * 2;
+      p[0] = m;
+      p[1] = l;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// SnapKV softmax statistics and token scores
+// ------------------------------------------------------------------------------------------
+// Per (head, row): max and sum of exp over the whole sequence from the chunk partials.
+template <bool DENSE>
+__global__ void stats_kernel(CompressArgs a) {
+  const hc_layer& L = a.L;
+  const int s = blockIdx.x;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
+  if (!pl.active) return;
+  const int tqu = min(pl.nobs, a.tq);
+  const int nch = (pl.S + kScoreCH - 1) / kScoreCH;
+  for (int i = threadIdx.x; i < L.Hk * tqu; i += blockDim.x) {
+    const int h = i / tqu, r = i % tqu;
+    const float* p = a.part + (((size_t)s * L.Hk + h) * a.tqmax + r) * a.max_chunks * 2;
+    float M = kNegInf;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, p[2 * c]);
+    float S = 0.f;
+    for (int c = 0; c < nch; ++c) S += (p[2 * c] == kNegInf) ? 0.f : p[2 * c + 1] * __expf(p[2 * c] - M);
+    float* o = a.stats + (((size_t)s * L.Hk + h) * a.tqmax + r) * 2;
+    o[0] = M;
+    o[1] = S;
+  }
+}
+
+// importance of token t for head h: sum over rows of softmax probabilities (scoring.py:76-77)
+__device__ __forceinline__ float snap_imp(const CompressArgs& a, int s, int h, int tqu, int t) {
+  float acc = 0.f;
+  for (int r = 0; r < tqu; ++r) {
+    const size_t row = ((size_t)s * a.L.Hk + h) * a.tqmax + r;
+    const float x = a.logits[row * a.S_max + t];
+    const float* st = a.stats + row * 2;
+    acc += (x == kNegInf) ? 0.f : __expf(x - st[0]) / st[1];
+  }
+  return acc;
+}
+
+// token score = mean over KV heads of the pooled importance (scoring.py:40-47,78), or the
+// hot/cold score sum_h logit_h / sqrt(D) / Hk (cache.py:68-69).
+__device__ __forceinline__ float token_score(const CompressArgs& a, int s, int tqu, int S, int t) {
+  const hc_layer& L = a.L;
+  if (L.policy == HC_POLICY_HOTCOLD) {
+    const float inv = 1.f / sqrtf((float)L.D);
+    float acc = 0.f;
+    for (int h = 0; h < L.Hk; ++h) acc += a.logits[((size_t)s * L.Hk + h) * a.S_max + t] * inv;
+    return acc / (float)L.Hk;
+  }
+  const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
+  float tot = 0.f;
+  for (int h = 0; h < L.Hk; ++h) {
+    const float* imp = a.imp + ((size_t)s * L.Hk + h) * a.S_max;
+    float v;
+    if (pad == 0) {
+      v = imp[t];
+    } else if (L.pooling == HC_POOL_MAX) {
+      v = kNegInf;
+      for (int u = max(0, t - pad); u <= min(S - 1, t + pad); ++u) v = fmaxf(v, imp[u]);
+    } else {
+      v = 0.f;
+      for (int u = max(0, t - pad); u <= min(S - 1, t + pad); ++u) v += imp[u];
+      v /= (float)L.pool_kernel;
+    }
+    tot += v;
+  }
+  return tot / (float)L.Hk;
+}
+
+// Large inputs: importance for every (head, token), grid (chunks, n_seq).
+template <bool DENSE>
+__global__ void imp_kernel(CompressArgs a) {
+  const hc_layer& L = a.L;
+  const int s = blockIdx.y;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
+  if (!pl.active) return;
+  const int tqu = min(pl.nobs, a.tq);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < L.Hk * pl.S; i += gridDim.x * blockDim.x) {
+    const int h = i / pl.S, t = i % pl.S;
+    a.imp[((size_t)s * L.Hk + h) * a.S_max + t] = snap_imp(a, s, h, tqu, t);
+  }
+}
+
+template <bool DENSE>
+__global__ void token_kernel(CompressArgs a) {
+  const hc_layer& L = a.L;
+  const int s = blockIdx.y;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
+  if (!pl.active) return;
+  const int tqu = min(pl.nobs, a.tq);
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < pl.S; t += gridDim.x * blockDim.x)
+    a.tok[(size_t)s * a.S_max + t] = token_score(a, s, tqu, pl.S, t);
+}
+
+// ------------------------------------------------------------------------------------------
+// payload copy of one evicted token into the cold ring (+ index vector), one warp
+// ------------------------------------------------------------------------------------------
+template <int DT, int D, bool DENSE>
+__device__ void evict_one(const CompressArgs& a, const hc_seq_desc& d, int s, int src, int dst) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  const hc_layer& L = a.L;
+  const int lane = threadIdx.x & 31;
+  constexpr int PER = (D + 31) / 32;
+  if (dst < 0 || dst >= d.ccap || src < 0 || src >= (DENSE ? a.S_dense : d.cap)) {
+    if (lane == 0) set_status(d.st, HC_DEV_INDEX);
+    return;
+  }
+  float mean[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) mean[i] = 0.f;
+  T* ck = reinterpret_cast<T*>(d.cold_kpre) + (size_t)dst * L.Hk * D;
+  T* cv = reinterpret_cast<T*>(d.cold_v) + (size_t)dst * L.Hk * D;
+  for (int h = 0; h < L.Hk; ++h) {
+    const T* kp;
+    const T* vp;
+    if constexpr (DENSE) {
+      const size_t off = (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)src * a.ss_tok;
+      kp = reinterpret_cast<const T*>(a.src_kpre) + off;
+      vp = reinterpret_cast<const T*>(a.src_v) + off;
+    } else {
+      const size_t off = ((size_t)h * d.cap + src) * D;
+      kp = reinterpret_cast<const T*>(d.hot_kpre) + off;
+      vp = reinterpret_cast<const T*>(d.hot_v) + off;
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int dd = lane + 32 * i;
+      if (dd < D) {
+        const T kv = kp[dd];
+        ck[(size_t)h * D + dd] = kv;
+        cv[(size_t)h * D + dd] = vp[dd];
+        mean[i] += E::to_f(kv);
+      }
+    }
+  }
+  if (lane == 0) d.cold_pos[dst] = DENSE ? a.src_pos[(size_t)s * a.S_dense + src] : d.hot_pos[src];
+  // index vector (controller.py:178-182): mean over heads, pad/crop to F, L2-normalise
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    mean[i] = mean[i] / (float)L.Hk;
+    const int dd = lane + 32 * i;
+    if (dd < D && dd < L.F) ss += mean[i] * mean[i];
+  }
+  ss = warp_sum(ss);
+  const float den = fmaxf(sqrtf(ss), 1e-12f);
+  float* vec = d.cold_vec + (size_t)dst * L.F;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int dd = lane + 32 * i;
+    if (dd < D && dd < L.F) vec[dd] = L.normalize ? mean[i] / den : mean[i];
+  }
+  for (int f = D + lane; f < L.F; f += 32) vec[f] = 0.f;
+}
+
+// ------------------------------------------------------------------------------------------
+// select: top-k of the prefix, compaction, ring plan (one CTA of 1024 threads per sequence)
+// ------------------------------------------------------------------------------------------
+template <int DT, int D, bool DENSE>
+__global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small) {
+  const hc_layer& L = a.L;
+  const int s = blockIdx.x, tid = threadIdx.x;
+  __shared__ int sh[kTopkSmemInts];
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  hc_seq_state* st = d.st;
+  const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
+  int* hdr = a.hdr + (size_t)s * 16;
+  if (DENSE && !pl.active) {
+    // a prompt within the budget is stored whole, in order
+    const int S = min(pl.S, d.cap);
+    for (int t = tid; t < S; t += blockDim.x) a.keep_src[(size_t)s * a.S_max + t] = t;
+    for (int i = tid; i < d.cap - S; i += blockDim.x) d.hot_free[i] = d.cap - 1 - i;
+    if (tid == 0) {
+      if (pl.S > d.cap) set_status(st, HC_DEV_CAPACITY);
+      hdr[4] = 1;
+      hdr[5] = S;
+      hdr[6] = 0;
+      st->n_hot = S;
+      st->n_free = d.cap - S;
+      st->n_evict = 0;
+    }
+    return;
+  }
+  if (!pl.active) {
+    if (tid == 0) {
+      hdr[4] = 0;
+      hdr[5] = 0;
+      hdr[6] = 0;
+      st->n_evict = 0;
+    }
+    return;
+  }
+  const int S = pl.S, tqu = min(pl.nobs, a.tq);
+  float* tok = a.tok + (size_t)s * a.S_max;
+  uint8_t* sel = a.sel + (size_t)s * a.S_max;
+
+  if (small) {
+    if (L.policy == HC_POLICY_SNAPKV) {
+      // softmax statistics per (head, row), one warp each
+      const int warp = tid >> 5, lane = tid & 31;
+      for (int i = warp; i < L.Hk * tqu; i += 32) {
+        const int h = i / tqu, r = i % tqu;
+        const size_t row = ((size_t)s * L.Hk + h) * a.tqmax + r;
+        const float* lg = a.logits + row * a.S_max;
+        float m = kNegInf;
+        for (int t = lane; t < S; t += 32) m = fmaxf(m, lg[t]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int t = lane; t < S; t += 32) l += (lg[t] == kNegInf) ? 0.f : __expf(lg[t] - m);
+        l = warp_sum(l);
+        if (lane == 0) {
+          a.stats[row * 2] = m;
+          a.stats[row * 2 + 1] = l;
+        }
+      }
+      __syncthreads();
+      for (int i = tid; i < L.Hk * S; i += blockDim.x) {
+        const int h = i / S, t = i % S;
+        a.imp[((size_t)s * L.Hk + h) * a.S_max + t] = snap_imp(a, s, h, tqu, t);
+      }
+      __syncthreads();
+    }
+    for (int t = tid; t < S; t += blockDim.x) tok[t] = token_score(a, s, tqu, S, t);
+    __syncthreads();
+  }
+
+  // exact top-n_top of the prefix
+  block_topk_flags([&](int i) { return tok[i]; }, pl.prefix, pl.ntop, sel, sh);
+
+  // order-preserving compaction. keep: selected prefix tokens and the tail; evict: the rest
+  int kept = 0, evicted = 0;
+  const int n_evict_total = pl.prefix - pl.ntop;
+  const int ccap = d.ccap;
+  const int cold_head = st->cold_head, cold_count = st->cold_count;
+  const int n_free0 = DENSE ? 0 : st->n_free;
+  for (int base = 0; base < S; base += blockDim.x) {
+    const int t = base + tid;
+    int keep = 0, ev = 0, phys = -1;
+    if (t < S) {
+      keep = (t >= pl.prefix) || sel[t];
+      ev = !keep;
+      if (!DENSE) phys = d.hot_ord[t];
+    }
+    int tk, te;
+    const int rk = block_exclusive_scan(keep, sh + 256, tk);
+    const int re = block_exclusive_scan(ev, sh + 256, te);
+    // block_exclusive_scan ends with a barrier, so every hot_ord read above is done
+    if (t < S) {
+      if (keep) {
+        if (DENSE) a.keep_src[(size_t)s * a.S_max + kept + rk] = t;
+        else d.hot_ord[kept + rk] = phys;
+      } else {
+        const int j = evicted + re;
+        const int src = DENSE ? t : phys;
+        a.ev_src[(size_t)s * a.S_max + j] = src;
+        // ring slot of the j-th evicted token; a batch larger than the ring keeps its last ccap
+        a.ev_dst[(size_t)s * a.S_max + j] =
+            (j >= n_evict_total - ccap) ? (int)(((long)cold_head + cold_count + j) % ccap) : -1;
+        if (!DENSE && n_free0 + j < d.cap) d.hot_free[n_free0 + j] = phys;
+      }
+    }
+    kept += tk;
+    evicted += te;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    const long total = (long)cold_count + evicted;
+    int nh = cold_head, nc = (int)total;
+    if (total > ccap) {
+      nh = (int)(((long)cold_head + total - ccap) % ccap);
+      nc = ccap;
+    }
+    st->cold_head = nh;
+    st->cold_count = nc;
+    st->n_evict = evicted;
+    if (DENSE) {
+      st->n_hot = kept;
+      st->n_free = d.cap - kept;
+    } else {
+      st->n_hot = kept;
+      st->n_free = n_free0 + evicted;
+    }
+    hdr[0] = S;
+    hdr[4] = 1;
+    hdr[5] = DENSE ? kept : 0;
+    hdr[6] = evicted;
+  }
+  if (DENSE) {
+    for (int i = tid; i < d.cap - kept; i += blockDim.x) d.hot_free[i] = d.cap - 1 - i;
+  }
+  // small decode evictions: copy here, one warp per token
+  if (!DENSE && evicted <= kInlineEvict) {
+    __syncthreads();
+    const int warp = tid >> 5;
+    for (int j = warp; j < evicted; j += 32) {
+      const int dst = a.ev_dst[(size_t)s * a.S_max + j];
+      if (dst >= 0) evict_one<DT, D, false>(a, d, s, a.ev_src[(size_t)s * a.S_max + j], dst);
+    }
+  }
+}
+
+// Large evictions and the prompt store: kept tokens -> slab slots 0..n_keep-1 (prompt),
+// evicted tokens -> cold ring. Grid (blocks, n_seq), 8 warps per block, a warp per token.
+template <int DT, int D, bool DENSE>
+__global__ void __launch_bounds__(256) evict_kernel(CompressArgs a) {
+  using T = typename Elem<DT>::T;
+  const hc_layer& L = a.L;
+  const int s = blockIdx.y;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const int* hdr = a.hdr + (size_t)s * 16;
+  if (!hdr[4]) return;
+  const int n_keep = hdr[5], n_ev = hdr[6];
+  if (!DENSE && n_ev <= kInlineEvict) return;
+  const int lane = threadIdx.x & 31;
+  const int w0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+  for (int item = w0; item < n_keep + n_ev; item += nw) {
+    if (item < n_keep) {
+      if constexpr (DENSE) {
+        const int t = a.keep_src[(size_t)s * a.S_max + item];
+        for (int h = 0; h < L.Hk; ++h) {
+          const size_t src = (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)t * a.ss_tok;
+          const size_t dst = ((size_t)h * d.cap + item) * D;
+          for (int dd = lane; dd < D; dd += 32) {
+            reinterpret_cast<T*>(d.hot_k)[dst + dd] = reinterpret_cast<const T*>(a.src_k)[src + dd];
+            reinterpret_cast<T*>(d.hot_v)[dst + dd] = reinterpret_cast<const T*>(a.src_v)[src + dd];
+            reinterpret_cast<T*>(d.hot_kpre)[dst + dd] = reinterpret_cast<const T*>(a.src_kpre)[src + dd];
+          }
+        }
+        if (lane == 0) {
+          d.hot_pos[item] = a.src_pos[(size_t)s * a.S_dense + t];
+          d.hot_ord[item] = item;
+        }
+      }
+    } else {
+      const int j = item - n_keep;
+      const int dst = a.ev_dst[(size_t)s * a.S_max + j];
+      if (dst >= 0) evict_one<DT, D, DENSE>(a, d, s, a.ev_src[(size_t)s * a.S_max + j], dst);
+    }
+  }
+}
+
+// Stand-alone cold append (add_evicted_to_cold_store, controller.py:190-238): tokens with
+// evicted_idx >= 0 in index order; a batch larger than the ring keeps its newest ccap.
+// One CTA of 256 threads per sequence.
+template <int DT, int D>
+__global__ void __launch_bounds__(256) cold_append_kernel(CompressArgs a, const int64_t* idx, int Te) {
+  const hc_layer& L = a.L;
+  const int s = blockIdx.x, tid = threadIdx.x;
+  __shared__ int sh[64];
+  __shared__ int sdst[1024];
+  __shared__ int ssrc[1024];
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  hc_seq_state* st = d.st;
+  const int head = st->cold_head, count = st->cold_count, ccap = d.ccap;
+  // number of valid tokens
+  int m = 0;
+  for (int base = 0; base < Te; base += blockDim.x) {
+    const int t = base + tid;
+    int tot;
+    block_exclusive_scan((t < Te && idx[(size_t)s * Te + t] >= 0) ? 1 : 0, sh, tot);
+    m += tot;
+  }
+  int j0 = 0;
+  for (int base = 0; base < Te; base += blockDim.x) {
+    const int t = base + tid;
+    const int f = (t < Te && idx[(size_t)s * Te + t] >= 0) ? 1 : 0;
+    int tot;
+    const int r = block_exclusive_scan(f, sh, tot);
+    if (f) {
+      const int j = j0 + r;
+      ssrc[tid] = t;
+      sdst[tid] = (j >= m - ccap) ? (int)(((long)head + count + j) % ccap) : -1;
+    } else {
+      sdst[tid] = -2;
+    }
+    __syncthreads();
+    for (int w = tid >> 5; w < (int)blockDim.x; w += blockDim.x >> 5) {
+      const int dst = sdst[w];
+      if (dst >= 0) evict_one<DT, D, true>(a, d, s, ssrc[w], dst);
+    }
+    __syncthreads();
+    j0 += tot;
+  }
+  if (tid == 0) {
+    const long total = (long)count + m;
+    if (total > ccap) {
+      st->cold_head = (int)(((long)head + total - ccap) % ccap);
+      st->cold_count = ccap;
+    } else {
+      st->cold_count = (int)total;
+    }
+  }
+}
+
+template <int DT, int D>
+static cudaError_t cold_append_t(CompressArgs a, const int64_t* idx, int Te, cudaStream_t stream) {
+  return launch_pdl(cold_append_kernel<DT, D>, dim3(a.L.n_seq), dim3(256), 0, stream, a, idx, Te);
+}
+
+cudaError_t launch_cold_append(const hc_layer& L, const void* kpre, const void* v, int64_t s0, int64_t s1, int64_t s2,
+                               const int64_t* pos, const int64_t* idx, int Te, cudaStream_t stream) {
+  CompressArgs a{};
+  a.L = L;
+  a.src_kpre = kpre;
+  a.src_v = v;
+  a.ss_seq = s0; a.ss_head = s1; a.ss_tok = s2;
+  a.src_pos = pos;
+  a.S_dense = Te;
+  HC_DISPATCH_DT_D(L.dtype, L.D, cold_append_t, a, idx, Te, stream);
+}
+
+// ------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------
+struct CompressLayout {
+  size_t hdr, logits, part, stats, imp, tok, sel, keep_src, ev_src, ev_dst, total;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+CompressLayout compress_layout(const hc_layer& L, int S_max, int tq) {
+  CompressLayout c{};
+  const size_t n = (size_t)L.n_seq, Hk = (size_t)L.Hk, S = (size_t)S_max;
+  const size_t tqm = (size_t)(tq > 0 ? tq : 1);
+  const size_t chunks = (S + kScoreCH - 1) / kScoreCH;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
+  c.hdr = take(n * 16 * sizeof(int));
+  c.logits = take(n * Hk * tqm * S * sizeof(float));
+  c.part = take(n * Hk * tqm * chunks * 2 * sizeof(float));
+  c.stats = take(n * Hk * tqm * 2 * sizeof(float));
+  c.imp = take(n * Hk * S * sizeof(float));
+  c.tok = take(n * S * sizeof(float));
+  c.sel = take(n * S);
+  c.keep_src = take(n * S * sizeof(int));
+  c.ev_src = take(n * S * sizeof(int));
+  c.ev_dst = take(n * S * sizeof(int));
+  c.total = off;
+  return c;
+}
+
+template <int DT, int D, bool DENSE>
+static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cudaStream_t stream) {
+  using T = typename Elem<DT>::T;
+  const hc_layer& L = a.L;
+  const size_t smem = sizeof(T) * kScoreCH * D + sizeof(float) * ((size_t)(a.tqmax + 1) * D + (size_t)a.tqmax * kScoreCH) + 64;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  auto sk = score_kernel<DT, D, DENSE>;
+  cudaError_t e = ensure_smem(sk, 200 * 1024);
+  if (e != cudaSuccess) return e;
+  const int chunks = (S_grid + kScoreCH - 1) / kScoreCH;
+  e = launch_pdl(sk, dim3(chunks, L.Hk, L.n_seq), dim3(128), smem, stream, a);
+  if (e != cudaSuccess) return e;
+  const long work = (long)L.Hk * (L.policy == HC_POLICY_SNAPKV ? a.tqmax : 1) * S_grid;
+  const int small = work <= kSmallSelect ? 1 : 0;
+  if (!small) {
+    const int blocks = (int)((S_grid + 255) / 256) < 592 ? (S_grid + 255) / 256 : 592;
+    if (L.policy == HC_POLICY_SNAPKV) {
+      e = launch_pdl(stats_kernel<DENSE>, dim3(L.n_seq), dim3(256), 0, stream, a);
+      if (e != cudaSuccess) return e;
+      const int ib = (int)(((long)L.Hk * S_grid + 255) / 256) < 1184 ? (int)(((long)L.Hk * S_grid + 255) / 256) : 1184;
+      e = launch_pdl(imp_kernel<DENSE>, dim3(ib, L.n_seq), dim3(256), 0, stream, a);
+      if (e != cudaSuccess) return e;
+    }
+    e = launch_pdl(token_kernel<DENSE>, dim3(blocks > 0 ? blocks : 1, L.n_seq), dim3(256), 0, stream, a);
+    if (e != cudaSuccess) return e;
+  }
+  e = launch_pdl(select_kernel<DT, D, DENSE>, dim3(L.n_seq), dim3(1024), 0, stream, a, small);
+  if (e != cudaSuccess) return e;
+  if (DENSE || n_evict_hint > kInlineEvict) {
+    const int items = DENSE ? S_grid : n_evict_hint;
+    int blocks = (items + 7) / 8;
+    if (blocks > 296) blocks = 296;
+    if (blocks < 1) blocks = 1;
+    e = launch_pdl(evict_kernel<DT, D, DENSE>, dim3(blocks, L.n_seq), dim3(256), 0, stream, a);
+  }
+  return e;
+}
+
+template <int DT, int D>
+static cudaError_t compress_dt(CompressArgs a, bool dense, int S_grid, int n_evict_hint, cudaStream_t stream) {
+  if (dense) return compress_t<DT, D, true>(a, S_grid, n_evict_hint, stream);
+  return compress_t<DT, D, false>(a, S_grid, n_evict_hint, stream);
+}
+
+cudaError_t launch_compress(const hc_layer& L, const void* q_obs, int64_t qs0, int64_t qs1, int64_t qs2, int tq,
+                            int S_dense, const void* sk, const void* sv, const void* skp, int64_t ss0, int64_t ss1,
+                            int64_t ss2, const int64_t* spos, void* scratch, int n_evict_hint, cudaStream_t stream) {
+  const bool dense = sk != nullptr;
+  const int S_grid = dense ? S_dense : L.max_cap;
+  const CompressLayout lay = compress_layout(L, S_grid, tq);
+  char* base = reinterpret_cast<char*>(scratch);
+  CompressArgs a{};
+  a.L = L;
+  a.q_obs = q_obs;
+  a.qs_seq = qs0; a.qs_head = qs1; a.qs_tok = qs2;
+  a.tq = tq;
+  a.tqmax = tq > 0 ? tq : 1;
+  a.S_dense = S_dense;
+  a.S_max = S_grid;
+  a.max_chunks = (S_grid + kScoreCH - 1) / kScoreCH;
+  a.src_k = sk; a.src_v = sv; a.src_kpre = skp;
+  a.ss_seq = ss0; a.ss_head = ss1; a.ss_tok = ss2;
+  a.src_pos = spos;
+  a.hdr = reinterpret_cast<int*>(base + lay.hdr);
+  a.logits = reinterpret_cast<float*>(base + lay.logits);
+  a.part = reinterpret_cast<float*>(base + lay.part);
+  a.stats = reinterpret_cast<float*>(base + lay.stats);
+  a.imp = reinterpret_cast<float*>(base + lay.imp);
+  a.tok = reinterpret_cast<float*>(base + lay.tok);
+  a.sel = reinterpret_cast<uint8_t*>(base + lay.sel);
+  a.keep_src = reinterpret_cast<int*>(base + lay.keep_src);
+  a.ev_src = reinterpret_cast<int*>(base + lay.ev_src);
+  a.ev_dst = reinterpret_cast<int*>(base + lay.ev_dst);
+  if (L.dtype == HC_F32 && L.D == 128) return compress_dt<HC_F32, 128>(a, dense, S_grid, n_evict_hint, stream);
+  if (L.dtype == HC_F16 && L.D == 128) return compress_dt<HC_F16, 128>(a, dense, S_grid, n_evict_hint, stream);
+  if (L.dtype == HC_BF16 && L.D == 128) return compress_dt<HC_BF16, 128>(a, dense, S_grid, n_evict_hint, stream);
+  if (L.dtype == HC_F32 && L.D == 64) return compress_dt<HC_F32, 64>(a, dense, S_grid, n_evict_hint, stream);
+  if (L.dtype == HC_F16 && L.D == 64) return compress_dt<HC_F16, 64>(a, dense, S_grid, n_evict_hint, stream);
+  if (L.dtype == HC_BF16 && L.D == 64) return compress_dt<HC_BF16, 64>(a, dense, S_grid, n_evict_hint, stream);
+  return cudaErrorInvalidValue;
+}
+
+size_t compress_scratch_bytes(const hc_layer& L, int S_max, int tq) { return compress_layout(L, S_max, tq).total; }
+
+}  // namespace hc

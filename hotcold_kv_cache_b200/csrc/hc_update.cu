@@ -1,0 +1,250 @@
+// Hot-tier updates: the decode-step append and the prompt store.
+//
+// The reference appends with four torch.cat calls per decode step (cache.py:145-148),
+// copying the whole hot cache every step. Here the hot slab is preallocated with
+// budget + 1 physical slots; a new token takes a slot from the free-slot stack and
+// its logical position is recorded in hot_ord, so an append writes one token.
+
+#include "hc_common.cuh"
+
+namespace hc {
+
+// One CTA per sequence. Rotates the new query and key (patch.py:161-162 with HF's
+// apply_rotary_pos_emb), appends (k_post, v, k_pre, pos) to the slab, and pushes the
+// mean over query heads of the pre-RoPE query into the query pool ring
+// (controller.py:240-241; the pool is later averaged by controller.py:185).
+template <int DT, int D>
+__global__ void __launch_bounds__(256) append_kernel(hc_layer L, const void* q_pre_, int64_t qss, const void* k_pre_,
+                                                     const void* v_, int64_t kvss, const void* cos_, const void* sin_,
+                                                     const int64_t* pos, void* q_post_) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  constexpr int H = D / 2;
+  const int s = blockIdx.x;
+  __shared__ float sc[D], ss[D];
+  __shared__ int sSlot, sOrdAt;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  hc_seq_state* st = d.st;
+  const int64_t p = pos[s];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    if (cos_) {
+      sc[i] = E::load(reinterpret_cast<const T*>(cos_) + (size_t)s * D + i);
+      ss[i] = E::load(reinterpret_cast<const T*>(sin_) + (size_t)s * D + i);
+    } else {
+      float c, sn;
+      rope_cs<DT>(L.inv_freq[i % H], p, L.rope_scaling, c, sn);
+      sc[i] = c;
+      ss[i] = sn;
+    }
+  }
+  if (threadIdx.x == 0) {
+    const int nf = st->n_free, nh = st->n_hot;
+    int slot = -1;
+    if (nf > 0 && nh < d.cap) {
+      slot = d.hot_free[nf - 1];
+      if (slot < 0 || slot >= d.cap) {
+        set_status(st, HC_DEV_INDEX);
+        slot = -1;
+      }
+    } else {
+      set_status(st, HC_DEV_CAPACITY);
+    }
+    sSlot = slot;
+    sOrdAt = nh;
+  }
+  __syncthreads();
+  const int slot = sSlot;
+  const T* q = reinterpret_cast<const T*>(q_pre_) + (size_t)s * qss;
+  const T* k = reinterpret_cast<const T*>(k_pre_) + (size_t)s * kvss;
+  const T* v = reinterpret_cast<const T*>(v_) + (size_t)s * kvss;
+  T* qo = reinterpret_cast<T*>(q_post_) + (size_t)s * L.Hq * D;
+  // query heads: RoPE -> q_post
+  for (int i = threadIdx.x; i < L.Hq * D; i += blockDim.x) {
+    const int dd = i % D;
+    const float x = E::to_f(q[i]);
+    const float r = dd < H ? -E::to_f(q[i + H]) : E::to_f(q[i - H]);
+    qo[i] = E::from_f(rope_elem<DT>(x, r, sc[dd], ss[dd]));
+  }
+  // key heads: RoPE -> slab (post), pre-RoPE key and value -> slab
+  if (slot >= 0) {
+    T* hk = reinterpret_cast<T*>(d.hot_k);
+    T* hv = reinterpret_cast<T*>(d.hot_v);
+    T* hp = reinterpret_cast<T*>(d.hot_kpre);
+    for (int i = threadIdx.x; i < L.Hk * D; i += blockDim.x) {
+      const int h = i / D, dd = i % D;
+      const float x = E::to_f(k[i]);
+      const float r = dd < H ? -E::to_f(k[i + H]) : E::to_f(k[i - H]);
+      const size_t off = ((size_t)h * d.cap + slot) * D + dd;
+      hk[off] = E::from_f(rope_elem<DT>(x, r, sc[dd], ss[dd]));
+      hp[off] = k[i];
+      hv[off] = v[i];
+    }
+  }
+  // query pool: mean over heads of the pre-RoPE query, rounded to the model dtype
+  if (d.p_max > 0) {
+    const int qh = ((st->qwin_head % d.p_max) + d.p_max) % d.p_max;
+    T* qw = reinterpret_cast<T*>(d.qwin) + (size_t)qh * D;
+    for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
+      float acc = 0.f;
+      for (int h = 0; h < L.Hq; ++h) acc += E::to_f(q[(size_t)h * D + dd]);
+      qw[dd] = E::from_f(acc / (float)L.Hq);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (slot >= 0) {
+      d.hot_ord[sOrdAt] = slot;
+      d.hot_pos[slot] = p;
+      st->n_hot = sOrdAt + 1;
+      st->n_free = st->n_free - 1;
+    }
+    if (d.p_max > 0) st->qwin_head = (((st->qwin_head % d.p_max) + d.p_max) % d.p_max + 1) % d.p_max;
+  }
+  pdl_launch_dependents();
+}
+
+// Append of already-rotated keys (HotColdLayer.update on a one-token step, cache.py:145-148).
+template <int DT, int D>
+__global__ void __launch_bounds__(256) append_rotated_kernel(hc_layer L, const void* kpost_, const void* kpre_,
+                                                             const void* v_, int64_t kvss, const int64_t* pos) {
+  using T = typename Elem<DT>::T;
+  const int s = blockIdx.x;
+  __shared__ int sSlot, sOrdAt;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  hc_seq_state* st = d.st;
+  if (threadIdx.x == 0) {
+    const int nf = st->n_free, nh = st->n_hot;
+    int slot = -1;
+    if (nf > 0 && nh < d.cap) slot = d.hot_free[nf - 1];
+    if (slot < 0 || slot >= d.cap) {
+      set_status(st, HC_DEV_CAPACITY);
+      slot = -1;
+    }
+    sSlot = slot;
+    sOrdAt = nh;
+  }
+  __syncthreads();
+  const int slot = sSlot;
+  if (slot < 0) return;
+  const T* kq = reinterpret_cast<const T*>(kpost_) + (size_t)s * kvss;
+  const T* kp = reinterpret_cast<const T*>(kpre_) + (size_t)s * kvss;
+  const T* vv = reinterpret_cast<const T*>(v_) + (size_t)s * kvss;
+  for (int i = threadIdx.x; i < L.Hk * D; i += blockDim.x) {
+    const int h = i / D, dd = i % D;
+    const size_t off = ((size_t)h * d.cap + slot) * D + dd;
+    reinterpret_cast<T*>(d.hot_k)[off] = kq[i];
+    reinterpret_cast<T*>(d.hot_kpre)[off] = kp[i];
+    reinterpret_cast<T*>(d.hot_v)[off] = vv[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    d.hot_ord[sOrdAt] = slot;
+    d.hot_pos[slot] = pos[s];
+    st->n_hot = sOrdAt + 1;
+    st->n_free = st->n_free - 1;
+  }
+}
+
+// Prompt store without compression: token t -> physical slot t, logical order = identity.
+template <int DT, int D>
+__global__ void store_prompt_kernel(hc_layer L, int S, const void* sk, const void* sv, const void* skp, int64_t ss_seq,
+                                    int64_t ss_head, int64_t ss_tok, const int64_t* spos) {
+  using T = typename Elem<DT>::T;
+  const int s = blockIdx.y;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const int S_src = S;  // row stride of the position array
+  S = min(S, d.cap);
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int t = warp; t < S; t += nw) {
+    for (int h = 0; h < L.Hk; ++h) {
+      const size_t src = (size_t)s * ss_seq + (size_t)h * ss_head + (size_t)t * ss_tok;
+      const size_t dst = ((size_t)h * d.cap + t) * D;
+      for (int dd = lane; dd < D; dd += 32) {
+        reinterpret_cast<T*>(d.hot_k)[dst + dd] = reinterpret_cast<const T*>(sk)[src + dd];
+        reinterpret_cast<T*>(d.hot_v)[dst + dd] = reinterpret_cast<const T*>(sv)[src + dd];
+        reinterpret_cast<T*>(d.hot_kpre)[dst + dd] = reinterpret_cast<const T*>(skp)[src + dd];
+      }
+    }
+    if (lane == 0) {
+      d.hot_pos[t] = spos[(size_t)s * S_src + t];
+      d.hot_ord[t] = t;
+    }
+  }
+  if (blockIdx.x == 0) {
+    // free stack holds the unused slots, the lowest on top
+    for (int i = threadIdx.x; i < d.cap - S; i += blockDim.x) d.hot_free[i] = d.cap - 1 - i;
+    if (threadIdx.x == 0) {
+      d.st->n_hot = S;
+      d.st->n_free = d.cap - S;
+    }
+  }
+}
+
+// Sum over prompt positions of the head-mean pre-RoPE query (each mean rounded to the
+// model dtype, as torch's mean over heads returns that dtype), fp32 (n_seq, D).
+template <int DT, int D>
+__global__ void prompt_query_sum_kernel(hc_layer L, const void* q_, int64_t qs, int64_t qh, int64_t qt, int P,
+                                        float* out) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  const int s = blockIdx.x;
+  pdl_wait();
+  for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
+    float tot = 0.f;
+    for (int p = 0; p < P; ++p) {
+      float acc = 0.f;
+      for (int h = 0; h < L.Hq; ++h)
+        acc += E::to_f(reinterpret_cast<const T*>(q_)[(size_t)s * qs + (size_t)h * qh + (size_t)p * qt + dd]);
+      tot += E::round(acc / (float)L.Hq);
+    }
+    out[(size_t)s * D + dd] = tot;
+  }
+}
+
+template <int DT, int D>
+static cudaError_t append_t(const hc_layer& L, const void* q, int64_t qss, const void* k, const void* v, int64_t kvss,
+                            const void* c, const void* sn, const int64_t* pos, void* qo, cudaStream_t st) {
+  return launch_pdl(append_kernel<DT, D>, dim3(L.n_seq), dim3(256), 0, st, L, q, qss, k, v, kvss, c, sn, pos, qo);
+}
+cudaError_t launch_append(const hc_layer& L, const void* q, int64_t qss, const void* k, const void* v, int64_t kvss,
+                          const void* c, const void* sn, const int64_t* pos, void* qo, cudaStream_t st) {
+  HC_DISPATCH_DT_D(L.dtype, L.D, append_t, L, q, qss, k, v, kvss, c, sn, pos, qo, st);
+}
+
+template <int DT, int D>
+static cudaError_t append_rot_t(const hc_layer& L, const void* kq, const void* kp, const void* v, int64_t kvss,
+                                const int64_t* pos, cudaStream_t st) {
+  return launch_pdl(append_rotated_kernel<DT, D>, dim3(L.n_seq), dim3(256), 0, st, L, kq, kp, v, kvss, pos);
+}
+cudaError_t launch_append_rotated(const hc_layer& L, const void* kq, const void* kp, const void* v, int64_t kvss,
+                                  const int64_t* pos, cudaStream_t st) {
+  HC_DISPATCH_DT_D(L.dtype, L.D, append_rot_t, L, kq, kp, v, kvss, pos, st);
+}
+
+template <int DT, int D>
+static cudaError_t store_t(const hc_layer& L, int S, const void* a, const void* b, const void* c, int64_t s0,
+                           int64_t s1, int64_t s2, const int64_t* pos, cudaStream_t st) {
+  const int blocks = (S + 7) / 8 < 148 ? (S + 7) / 8 : 148;
+  return launch_pdl(store_prompt_kernel<DT, D>, dim3(blocks > 0 ? blocks : 1, L.n_seq), dim3(256), 0, st, L, S, a, b,
+                    c, s0, s1, s2, pos);
+}
+cudaError_t launch_store_prompt(const hc_layer& L, int S, const void* a, const void* b, const void* c, int64_t s0,
+                                int64_t s1, int64_t s2, const int64_t* pos, cudaStream_t st) {
+  HC_DISPATCH_DT_D(L.dtype, L.D, store_t, L, S, a, b, c, s0, s1, s2, pos, st);
+}
+
+template <int DT, int D>
+static cudaError_t pqs_t(const hc_layer& L, const void* q, int64_t a, int64_t b, int64_t c, int P, float* out,
+                         cudaStream_t st) {
+  return launch_pdl(prompt_query_sum_kernel<DT, D>, dim3(L.n_seq), dim3(D), 0, st, L, q, a, b, c, P, out);
+}
+cudaError_t launch_prompt_query_sum(const hc_layer& L, const void* q, int64_t a, int64_t b, int64_t c, int P,
+                                    float* out, cudaStream_t st) {
+  HC_DISPATCH_DT_D(L.dtype, L.D, pqs_t, L, q, a, b, c, P, out, st);
+}
+
+}  // namespace hc

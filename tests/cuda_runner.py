@@ -1,0 +1,79 @@
+"""Drive the CUDA hot path of one layer the way oracle.run_layer drives the
+restatement: a prompt forward, then decode steps, recording the attention
+output, the hot positions and the held set after every step."""
+
+import math
+
+import numpy as np
+import torch
+from transformers import LlamaConfig
+from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding, apply_rotary_pos_emb
+
+from hotcold_kv_cache_b200.controller import KVController
+
+TORCH_DT = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+
+
+def rotary(Hq, D, theta, device, max_pos=1 << 20):
+    cfg = LlamaConfig(hidden_size=Hq * D, num_attention_heads=Hq, num_key_value_heads=1, head_dim=D,
+                      num_hidden_layers=1, rope_theta=theta, vocab_size=16, intermediate_size=16,
+                      max_position_embeddings=max_pos)
+    return LlamaRotaryEmbedding(cfg).to(device)
+
+
+def controller_kwargs(case):
+    c = case
+    return dict(max_capacity_prompt=c["cap"], topk_ratio=c["topk_ratio"], recent_size=c["recent"],
+                cpu_buffer_size=c["ccap"], faiss_dim=c["faiss_dim"], normalize_for_ip=True,
+                window_size=c["window_size"], query_pool_size=c["pool"], lookahead_k=c["R"],
+                hold_retrieved=c["hold"], retrieve_after_prefill=c["rap"], policy=c["policy"],
+                pool_kernel=c.get("pool_kernel", 7))
+
+
+def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True):
+    """Returns dict(outs (n,B,Hq,D) float64, hot [per-step (B,S) int64], held {step: (pos, valid, k)},
+    ctrl). model_cos=True passes HF's cos/sin tables to the append kernel (what the patched
+    forward does); False lets the kernel compute them from inv_freq."""
+    c = case
+    dev = torch.device(device)
+    dt = TORCH_DT[c["dtype"]]
+    B, Hq, Hk, D, T = c["B"], c["Hq"], c["Hk"], c["D"], c["T"]
+
+    def t(x):
+        return torch.from_numpy(np.ascontiguousarray(x).astype(np.float32)).to(device=dev, dtype=dt)
+
+    rot = rotary(Hq, D, c["theta"], dev)
+    ctrl = KVController(**controller_kwargs(c))
+    ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
+    q_pre, k_pre, v = t(inputs["q_pre"]), t(inputs["k_pre"]), t(inputs["v"])
+    ctrl._lazy_init(k_pre, n_layers=1)
+    pos = torch.arange(T, device=dev).unsqueeze(0).expand(B, T)
+    cos, sin = rot(torch.empty(1, dtype=dt, device=dev), pos)
+    q_post, k_post = apply_rotary_pos_emb(q_pre, k_pre, cos, sin)
+    ctrl.prefill_layer(0, q_pre, q_post, k_pre, k_post, v, pos)
+    outs, hot, held = [], [], {}
+    dq, dk, dv = t(inputs["dq"]), t(inputs["dk"]), t(inputs["dv"])
+    for i in range(n_steps):
+        p = T + i
+        pd = torch.full((B,), p, device=dev, dtype=torch.long)
+        if model_cos:
+            c1, s1 = rot(torch.empty(1, dtype=dt, device=dev), pd[:, None])
+            c1, s1 = c1.reshape(B, D), s1.reshape(B, D)
+        else:
+            c1 = s1 = None
+        ready_before = ctrl.dbg["prefetch_ready"]
+        o = ctrl.decode_layer(0, dq[i], dk[i], dv[i], c1, s1, pd)
+        outs.append(o.double().cpu().numpy())
+        a = ctrl.arenas[0]
+        hot.append(a.hot_positions().cpu().numpy())
+        if ctrl.dbg["prefetch_ready"] != ready_before:
+            R = a.r_max
+            held[i + 1] = (a.held_pos[:, :R].cpu().numpy(), a.held_valid[:, :R].cpu().numpy().astype(bool),
+                           a.held_k[:, :, :R].double().cpu().numpy())
+    torch.cuda.synchronize(dev)
+    return dict(outs=np.stack(outs, 0), hot=hot, held=held, ctrl=ctrl)
+
+
+def cold_positions(ctrl, li=0):
+    a = ctrl.arenas[li]
+    return [a.cold_pos[b].index_select(0, a.cold_order(b)).cpu().numpy() for b in range(a.n_seq)]

@@ -1,0 +1,111 @@
+"""CUDA hot path of one layer against the CPU oracle and against the golden
+vectors of the reference itself: attention outputs, hot sets after every step,
+cold ring contents, retrieved sets, re-rotated held keys and debug counters."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from golden_cases import LAYER_CASES, assert_close, inputs, load, oracle_kwargs, split_hot
+
+pytestmark = pytest.mark.gpu
+
+from oracle import hotcold_oracle as O  # noqa: E402
+
+
+def _run(case, model_cos=True):
+    from cuda_runner import run_cuda_layer
+    return run_cuda_layer(case, inputs(case), case["steps"], model_cos=model_cos)
+
+
+def _compare_layer(res, case, layer, o_outs, o_hot, near_tie=1e-4):
+    """Step-by-step comparison. A hot-set difference is accepted only where the oracle's
+    selection boundary has a relative score gap within `near_tie`; the states differ from
+    there on, so the comparison stops. Returns the number of steps compared."""
+    dt = case["dtype"]
+    n = len(o_hot)
+    for i in range(n):
+        if not np.array_equal(res["hot"][i], o_hot[i]):
+            gaps = [e["gap"] for e in layer.compress_log if e["step"] == i + 1]
+            assert gaps and min(gaps) <= near_tie, f"hot set differs at step {i + 1} (gap {gaps})"
+            return i
+        assert_close(res["outs"][i], o_outs[i], dt, f"attention step {i + 1}")
+    return n
+
+
+@pytest.mark.parametrize("name", LAYER_CASES)
+@pytest.mark.parametrize("model_cos", [True, False])
+def test_layer_vs_oracle_and_golden(name, model_cos):
+    g = load(name)
+    c = g["case"]
+    layer, o_outs, o_hot = O.run_layer(inputs(c), c["steps"], **oracle_kwargs(c))
+    res = _run(c, model_cos)
+    steps = _compare_layer(res, c, layer, o_outs, o_hot)
+    assert steps == c["steps"], "golden cases are chosen free of near-ties"
+    # against the reference's own outputs
+    assert_close(res["outs"], g["outs"], c["dtype"], "attention vs reference")
+    for i, (a, b) in enumerate(zip(res["hot"], split_hot(g))):
+        assert np.array_equal(a, b), f"hot set vs reference, step {i + 1}"
+    from cuda_runner import cold_positions
+    cold = cold_positions(res["ctrl"])
+    if g["cold_pos"].size:
+        assert np.array_equal(np.stack(cold), g["cold_pos"])
+    for b, cp in enumerate(layer.cold_positions()):
+        assert np.array_equal(cold[b], cp)
+    # retrieved sets: same steps, same positions and validity, held keys re-rotated alike
+    assert sorted(res["held"]) == [e["step"] for e in layer.events]
+    for e in layer.events:
+        pos, valid, k = res["held"][e["step"]]
+        assert np.array_equal(valid, e["valid"]), e["step"]
+        assert np.array_equal(pos[valid], e["pos"][e["valid"]]), e["step"]
+        assert_close(k, e["kmem"], c["dtype"], f"held keys step {e['step']}")
+    if "ret_pos" in g:
+        for e, p, v in zip(sorted(res["held"]), g["ret_pos"], g["ret_valid"]):
+            pos, valid, _ = res["held"][e]
+            assert np.array_equal(valid, v) and np.array_equal(pos[valid], p[v])
+    # counters
+    ctrl = res["ctrl"]
+    for k, v in layer.dbg.items():
+        assert ctrl.dbg[k] == v, (k, ctrl.dbg[k], v)
+    assert ctrl.dbg["triton_decode_calls"] == c["steps"]
+    assert ctrl.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("policy", ["hotcold", "snapkv"])
+def test_random_configs_vs_oracle(dtype, policy):
+    """Seeded random geometry: batch 2, GQA 4, small budgets so that compression fires at
+    prefill and during decode, ring wrap, retrieval every 3 steps with hold."""
+    from hotcold_kv_cache_b200 import synth
+    c = dict(B=2, Hq=8, Hk=2, D=128, T=300, steps=25, dtype=dtype, policy=policy, cap=64, recent=16,
+             topk_ratio=0.5, pool_kernel=7, ccap=200, faiss_dim=128, window_size=3, pool=4, R=12, hold=True,
+             rap=True, theta=500000.0, seed=4242)
+    inp = synth.layer_inputs(c["seed"], c["B"], c["Hq"], c["Hk"], c["D"], c["T"], c["steps"], dtype)
+    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], **oracle_kwargs(c))
+    from cuda_runner import run_cuda_layer
+    res = run_cuda_layer(c, inp, c["steps"])
+    near = 1e-4 if dtype == "float32" else 2e-3 if dtype == "float16" else 2e-2
+    steps = _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near)
+    assert steps >= 1
+    assert res["ctrl"].device_status() == 0
+
+
+def test_cfg0_full_size():
+    """The CPU-runnable configuration at full size: one layer, fp32, 4096-token prompt,
+    SnapKV (window 32, max-pool 7, budget 512), prompt-end retrieval of 64 from the last 8
+    queries, held, 63 decode steps — compared step by step with the oracle."""
+    from hotcold_kv_cache_b200 import synth
+    c = dict(B=1, Hq=32, Hk=8, D=128, T=4096, steps=63, dtype="float32", policy="snapkv", cap=512, recent=32,
+             topk_ratio=0.0, pool_kernel=7, ccap=4096, faiss_dim=128, window_size=1 << 20, pool=8, R=64,
+             hold=True, rap=True, theta=500000.0, seed=0)
+    inp = synth.layer_inputs(c["seed"], 1, 32, 8, 128, 4096, 63, "float32")
+    layer, o_outs, o_hot = O.run_layer(inp, 63, **oracle_kwargs(c))
+    from cuda_runner import run_cuda_layer
+    res = run_cuda_layer(c, inp, 63)
+    steps = _compare_layer(res, c, layer, o_outs, o_hot)
+    assert steps >= 1
+    if steps == 63:
+        for k, v in layer.dbg.items():
+            assert res["ctrl"].dbg[k] == v, k

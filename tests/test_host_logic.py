@@ -1,0 +1,56 @@
+"""Host-side logic on CPU: the compression plan the host mirrors agrees with the
+oracle's (hence with cache.py:44-53 and scoring.py:117-120), seeded inputs are
+reproducible, and the ragged-batch partition is balanced."""
+
+import numpy as np
+import pytest
+
+from hotcold_kv_cache_b200 import synth
+from hotcold_kv_cache_b200.arena import plan_keep
+from oracle.hotcold_oracle import Policy, plan_keep as oracle_plan
+
+
+@pytest.mark.parametrize("policy", ["hotcold", "snapkv"])
+def test_plan_matches_oracle(policy):
+    for budget in (1, 2, 31, 32, 64, 128, 512, 1000, 2048):
+        for recent in (0, 1, 16, 32, 128):
+            for ratio in (0.0, 0.15, 0.5, 0.99):
+                for S in (0, 1, 5, budget, budget + 1, budget + 7, 4096, 131072):
+                    p = oracle_plan(Policy(policy=policy, cap=budget, recent=recent, topk_ratio=ratio), S)
+                    q = plan_keep(policy, budget, recent, ratio, S)
+                    assert (p is None and q is None) or (p[:2] == q), (policy, budget, recent, ratio, S, p, q)
+
+
+def test_benchmark_topk_ratio():
+    # run_baselines.py:86-87: budget 512, recent 128 -> 0.5 -> keep 256 + 128
+    ratio = max(0.05, 0.75 - 128 / 512)
+    assert plan_keep("hotcold", 512, 128, ratio, 8192) == (8064, 256)
+    assert plan_keep("snapkv", 512, 32, 0.0, 8192) == (8160, 480)
+    assert plan_keep("snapkv", 512, 32, 0.0, 513) == (481, 480)
+
+
+def test_inputs_are_reproducible():
+    a = synth.layer_inputs(3, 1, 4, 2, 64, 10, 2, "float16")
+    b = synth.layer_inputs(3, 1, 4, 2, 64, 10, 2, "float16")
+    for k in a:
+        assert np.array_equal(a[k], b[k])
+    assert a["q_pre"].dtype == np.float16
+
+
+def test_bf16_rounding_is_round_to_nearest_even():
+    x = np.array([1.0, 1.00390625, 1.005859375, -2.5e-3, 3.0e38], np.float32)
+    r = synth.round_bf16(x)
+    bits = r.view(np.uint32)
+    assert np.all(bits & 0xFFFF == 0)
+    assert r[0] == 1.0 and r[1] == 1.0 and r[2] == np.float32(1.0078125)
+
+
+def test_balanced_partition():
+    items = synth.ragged_batch(7, 64)
+    assert len(items) == 64 and all(2048 <= L <= 32768 for L, _ in items)
+    assert [b for _, b in items[:6]] == [512, 1024, 2048, 512, 1024, 2048]
+    for n in (1, 2, 4, 8):
+        parts = synth.balanced_partition(items, n)
+        assert sorted(i for p in parts for i in p) == list(range(64))
+        loads = [sum(items[i][0] + items[i][1] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= max(L + b for L, b in items)
