@@ -91,7 +91,7 @@ class ClockSampler:
     def start(self):
         cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
         if self.gpu_id is not None:
-            cmd += ["-i", self.gpu_id]
+            cmd += ["-i", str(self.gpu_id)]
         try:
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
@@ -236,8 +236,7 @@ def run_ours(a, rank, world):
     dbg0 = dict(ctrl.dbg)
     gpu_id = None
     try:
-        gpu_id = torch.cuda.get_device_properties(dev).pci_bus_id if hasattr(
-            torch.cuda.get_device_properties(dev), "pci_bus_id") else str(dev.index)
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
         gpu_id = None
     clocks = ClockSampler(gpu_id if rank == 0 else None)
@@ -293,7 +292,7 @@ def run_ours(a, rank, world):
            "dtype": "f16", "data": "synthetic N(0,1) pre-RoPE q/k/v, seeded; no weights or dataset",
            "config": workload_config(c, {"parallelism": f"replicas{world}"}),
            "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "clocks": clk,
-           "ops_us_per_layer_step": {k: round(v["us"], 3) for k, v in ops.items()},
+           "ops_us_per_layer_step": {k: round(v["us"], 3) for k, v in ops.items() if not k.startswith("_")},
            "hbm_gbs_per_layer_step": round(ops["_step_bytes"] / (value * 1e-6) / 1e9, 1)}
     return res
 

@@ -21,6 +21,9 @@ int fail(int code, const char* fmt, ...) {
 
 int check_cuda(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return HC_OK;
+  // a rejected launch leaves the runtime's last-error set; clear it so the caller's next,
+  // unrelated CUDA call does not report it
+  (void)cudaGetLastError();
   return fail(HC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/hotcold_b200.h"
 
 namespace hc {
@@ -214,18 +216,36 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// Raise a kernel's dynamic shared memory limit once per device.
+// Raise a kernel's dynamic shared memory limit, once per (kernel, device). The cache is keyed
+// on the kernel's address: every template instance needs its own attribute.
 template <typename K>
 inline cudaError_t ensure_smem(K kern, size_t bytes) {
-  static unsigned long long done = 0;
+  struct Entry {
+    const void* fn;
+    unsigned long long devs;
+    size_t bytes;
+  };
+  static Entry cache[256];
+  static int n = 0;
+  static std::mutex mu;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const unsigned long long bit = 1ull << (dev & 63);
-  if (done & bit) return cudaSuccess;
+  const void* fn = reinterpret_cast<const void*>(kern);
+  std::lock_guard<std::mutex> lock(mu);
+  int i = 0;
+  for (; i < n; ++i)
+    if (cache[i].fn == fn) break;
+  if (i < n && (cache[i].devs & bit) && cache[i].bytes >= bytes) return cudaSuccess;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  if (e == cudaSuccess) done |= bit;
-  return e;
+  if (e != cudaSuccess) return e;
+  if (i == n && n < 256) cache[n++] = Entry{fn, 0ull, bytes};
+  if (i < n) {
+    cache[i].devs |= bit;
+    cache[i].bytes = bytes;
+  }
+  return cudaSuccess;
 }
 
 #define HC_DISPATCH_DT_D(dtype, D, FN, ...)                                     \
