@@ -144,6 +144,74 @@ def profiled_traffic(kernel: str):
 
 
 # ------------------------------------------------------------------------------------------
+# CUDA runtime helpers (graph upload, event nodes recorded inside a capture)
+# ------------------------------------------------------------------------------------------
+_RT = None
+
+
+def _rt():
+    global _RT
+    if _RT is None:
+        import ctypes
+        rt = ctypes.CDLL("libcudart.so.12")
+        rt.cudaGraphUpload.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        rt.cudaEventCreate.argtypes = [ctypes.POINTER(ctypes.c_void_p)]
+        rt.cudaEventRecordWithFlags.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint]
+        rt.cudaEventElapsedTime.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.c_void_p, ctypes.c_void_p]
+        rt.cudaEventDestroy.argtypes = [ctypes.c_void_p]
+        _RT = rt
+    return _RT
+
+
+def _handle(x) -> int:
+    import ctypes
+    if isinstance(x, int):
+        return x
+    try:
+        return int(x)
+    except TypeError:
+        get = ctypes.pythonapi.PyCapsule_GetPointer
+        get.restype, get.argtypes = ctypes.c_void_p, [ctypes.py_object, ctypes.c_char_p]
+        return get(x, None)
+
+
+def graph_upload(g, stream) -> None:
+    """Upload an instantiated graph so that its first launch does not pay for it."""
+    rc = _rt().cudaGraphUpload(_handle(g.raw_cuda_graph_exec()), stream.cuda_stream)
+    if rc != 0:
+        raise RuntimeError(f"cudaGraphUpload failed ({rc})")
+
+
+class EventPool:
+    """Events recorded as graph nodes (cudaEventRecordExternal) during a capture."""
+
+    def __init__(self):
+        import ctypes
+        self.ct = ctypes
+        self.events = []
+
+    def record(self, stream_handle: int):
+        ev = self.ct.c_void_p()
+        if _rt().cudaEventCreate(self.ct.byref(ev)) != 0:
+            raise RuntimeError("cudaEventCreate failed")
+        if _rt().cudaEventRecordWithFlags(ev, self.ct.c_void_p(stream_handle), 1) != 0:
+            raise RuntimeError("cudaEventRecordWithFlags failed")
+        self.events.append(ev)
+        return ev
+
+    def elapsed_us(self, a, b) -> float:
+        ms = self.ct.c_float()
+        if _rt().cudaEventElapsedTime(self.ct.byref(ms), a, b) != 0:
+            raise RuntimeError("cudaEventElapsedTime failed")
+        return ms.value * 1e3
+
+    def close(self):
+        for ev in self.events:
+            _rt().cudaEventDestroy(ev)
+        self.events = []
+
+
+# ------------------------------------------------------------------------------------------
 # GPU arm
 # ------------------------------------------------------------------------------------------
 class Workload:
@@ -245,14 +313,15 @@ def run_ours(a, rank, world):
     torch.cuda.synchronize(dev)
     if rank == 0:
         clocks.start()
+    cur = torch.cuda.current_stream(dev)
     for i in range(W, total_steps):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             with torch.cuda.graph(g, stream=stream):
                 wl.step(i)
+        graph_upload(g, cur)
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        cur = torch.cuda.current_stream(dev)
         e0.record(cur)
         g.replay()
         e1.record(cur)
@@ -275,8 +344,8 @@ def run_ours(a, rank, world):
     if status:
         raise RuntimeError(f"device status word set: {status}")
 
-    # ---- per-op device time of one layer-step, isolated behind a GPU sleep ----------------
-    ops = per_op_times(wl, total_steps, dev)
+    # ---- per-op device time inside the captured steps (event nodes around each op) --------
+    ops = per_op_live(wl, total_steps, min(K, 16), dev)
 
     # ---- end to end through the public API with host buffers ------------------------------
     e2e = run_e2e(wl, total_steps + 0, min(K, 8), dev)
@@ -297,59 +366,70 @@ def run_ours(a, rank, world):
     return res
 
 
-def per_op_times(wl, start_step, dev, reps=3):
-    """Device time of each op of one layer-step: a GPU sleep first, so the op's launches are
-    queued before the GPU reaches them and host latency stays out of the interval."""
+def per_op_live(wl, start, n, dev):
+    """Device time of each op of a layer-step inside captured decode steps: event nodes
+    (cudaEventRecordExternal) bracket every op of every layer, the graph is uploaded, L2 is
+    flushed, the step is replayed once. Returns per-op medians over the layer-steps where the
+    op launched kernels, with the op's algorithmic bytes and GB/s."""
     import torch
-    from hotcold_kv_cache_b200 import arena as arena_mod  # noqa: F401
     ctrl, c = wl.ctrl, wl.c
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    acc = {"append": [], "compress": [], "retrieve": [], "attend": []}
-    nbytes_att = []
-    i = start_step
-    for r in range(reps):
-        for li in range(c["layers"]):
-            a = ctrl.arenas[li]
-            q, k, v = wl.dq[i, li], wl.dk[i, li], wl.dv[i, li]
-            cs, sn, p = wl.cos[i:i + 1], wl.sin[i:i + 1], wl.pos[i]
+    stream = torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+    rec = {k: [] for k in ("append", "retrieve", "compress", "attend")}
+    for i in range(start, start + n):
+        pool = EventPool()
+        marks = []
 
-            def timed(fn):
-                flush.zero_()
-                torch.cuda._sleep(200000)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                out = fn()
-                e1.record()
-                e1.synchronize()
-                return e0.elapsed_time(e1) * 1e3, out
+        def hook(name, phase):
+            h = torch.cuda.current_stream(dev).cuda_stream
+            if phase == "begin":
+                marks.append([name, pool.record(h), None, (ctrl.dbg["retrieval_launched"], ctrl.dbg["compress_calls"])])
+            else:
+                m = marks[-1]
+                m[2] = pool.record(h)
+                r0, c0 = m[3]
+                m[3] = not ((name == "retrieve" and ctrl.dbg["retrieval_launched"] == r0) or
+                            (name == "compress" and ctrl.dbg["compress_calls"] == c0))
 
-            t_app, qp = timed(lambda: a.append(q, k, v, cs, sn, p))
-            n_pool, extra, extra_n = ctrl._pool(li)
-            t_ret, _ = timed(lambda: a.retrieve(n_pool=max(n_pool, 1), extra_sum=extra, extra_n=extra_n))
-            t_cmp, _ = timed(lambda: a.compress_decode(qp.view(1, a.Hq, 1, a.D)))
-            t_att, _ = timed(lambda: a.attend(qp, p, True))
-            acc["append"].append(t_app)
-            acc["retrieve"].append(t_ret)
-            acc["compress"].append(t_cmp)
-            acc["attend"].append(t_att)
-            n_tok = int(a.n_hot[0]) + a.r_max
-            nbytes_att.append(n_tok * a.Hk * a.D * 2 * 2 + 2 * a.Hq * a.D * 2)
-        i += 1
-    Hk, D, R = c["Hk"], c["D"], c["lookahead_k"]
+        ctrl.op_hook = hook
+        g = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    wl.step(i)
+        finally:
+            ctrl.op_hook = None
+        graph_upload(g, cur)
+        flush.zero_()
+        g.replay()
+        torch.cuda.synchronize(dev)
+        for name, a, b, launched in marks:
+            if launched:
+                rec[name].append(pool.elapsed_us(a, b))
+        pool.close()
+        del g
+    Hk, D, R, Hq = c["Hk"], c["D"], c["lookahead_k"], c["Hq"]
     a = ctrl.arenas[0]
-    n_cold = int(a.cold_count[0])
+    n_hot, n_cold = int(a.n_hot[0]), int(a.cold_count[0])
     bytes_ = {
-        "attend": float(np.mean(nbytes_att)),
-        "append": (c["Hq"] * D * 2) * 2 + Hk * D * 2 * 4,
-        "compress": (int(a.n_hot[0]) + 1) * Hk * D * 2 + Hk * D * 2 * 2 + c["faiss_dim"] * 4,
-        "retrieve": n_cold * c["faiss_dim"] * 4 + R * Hk * D * 2 * 4,
+        # K and V rows of the held and hot tokens, plus the query in and the output
+        "attend": float((n_hot + R) * Hk * D * 2 * 2 + 2 * Hq * D * 2),
+        # pre-RoPE q/k/v in, q_post out, k_post/k_pre/v into the slab
+        "append": float((Hq + 2 * Hk) * D * 2 + Hq * D * 2 + 3 * Hk * D * 2),
+        # post-RoPE keys scored once, one evicted token's payload + index vector
+        "compress": float(n_hot * Hk * D * 2 + 2 * Hk * D * 2 * 2 + c["faiss_dim"] * 4),
+        # index scan over the live ring, gather of R hits (k_pre, v), held segment written
+        "retrieve": float(n_cold * c["faiss_dim"] * 4 + R * Hk * D * 2 * 4),
     }
     out = {}
-    for k, v in acc.items():
+    for k, v in rec.items():
+        if not v:
+            continue
         us = float(np.median(v))
-        out[k] = {"us": us, "bytes": bytes_[k], "gbs": bytes_[k] / (us * 1e-6) / 1e9}
-    out["_step_bytes"] = bytes_["attend"] + bytes_["append"] + bytes_["compress"] + bytes_["retrieve"] / c[
-        "window_size"]
+        out[k] = {"us": us, "bytes": bytes_[k], "gbs": bytes_[k] / (us * 1e-6) / 1e9, "n": len(v)}
+    step_bytes = sum(bytes_[k] for k in ("attend", "append", "compress")) + bytes_["retrieve"] / c["window_size"]
+    out["_step_bytes"] = step_bytes
     return out
 
 

@@ -134,6 +134,8 @@ class KVController:
         self.last_injected_len = 0
         self.workspace: Optional[Workspace] = None
         self.rotary = None  # (inv_freq tensor, attention_scaling); else the active rotary module
+        # optional callable(op_name, "begin"|"end") around each op of decode_layer (timing probes)
+        self.op_hook = None
         self.dbg = {k: (0.0 if k == "prefetch_copy_ms_sum" else 0) for k in DBG_KEYS}
 
     # ------------------------------------------------------------------ setup
@@ -402,11 +404,18 @@ class KVController:
         model dtype or None, pos (B,) int64 on the device. Returns (B,Hq,D)."""
         li = int(layer_idx)
         a = self.arena(li, q_pre.shape[1], k_pre.dtype, k_pre.device)
+        hook = self.op_hook or (lambda name, phase: None)
+        hook("append", "begin")
         q_post = a.append(q_pre, k_pre, v, cos, sin, pos)
+        hook("append", "end")
         self._qpool[li].append(1)
+        hook("retrieve", "begin")
         self.maybe_launch_async_retrieval(li)
+        hook("retrieve", "end")
+        hook("compress", "begin")
         ev = a.compress_decode(q_post.view(a.n_seq, a.Hq, 1, a.D))
         self._count_eviction(ev)
+        hook("compress", "end")
         use_held = False
         if self._staged[li]:
             self._staged[li] = False
@@ -423,7 +432,10 @@ class KVController:
         if use_held:
             self.dbg["injection_used"] += 1
         self.dbg["triton_decode_calls"] += 1
-        return a.attend(q_post, pos, use_held, self.overflow_nan)
+        hook("attend", "begin")
+        out = a.attend(q_post, pos, use_held, self.overflow_nan)
+        hook("attend", "end")
+        return out
 
     def device_status(self) -> int:
         """OR of the device status words of every layer (synchronises): HC_DEV_* bits."""
