@@ -56,6 +56,8 @@ SIGNATURES = {
     "hc_attention_dense_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "hc_attention_dense": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
                                    _P, _P, c_size_t, _P]),
+    "hc_attention_dense_noalloc": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int,
+                                           c_float, c_int, _P]),
     "hc_append": (c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, _P, _P]),
     "hc_append_rotated": (c_int, [_P, _P, _P, _P, _I64, _P, _P]),
     "hc_cold_append": (c_int, [_P, _P, _P, _I64, _I64, _I64, _P, _P, c_int, _P]),

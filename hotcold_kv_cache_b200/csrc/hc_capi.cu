@@ -47,6 +47,10 @@ int check_layer(const hc_layer* L) {
 
 }  // namespace
 
+namespace hc {
+void set_last_error(const char* msg) { snprintf(g_err, sizeof(g_err), "%s", msg); }
+}  // namespace hc
+
 extern "C" {
 
 const char* hc_version(void) { return "hotcold_b200 1.0 (sm_100a)"; }

@@ -49,6 +49,9 @@ cudaError_t launch_append_rotated(const hc_layer& L, const void* kpost, const vo
 cudaError_t launch_cold_append(const hc_layer& L, const void* kpre, const void* v, int64_t s0, int64_t s1, int64_t s2,
                                const int64_t* pos, const int64_t* idx, int Te, cudaStream_t st);
 size_t retrieve_scratch_bytes(const hc_layer& L);
+// Set the message hc_last_error() returns on the calling thread.
+void set_last_error(const char* msg);
+
 cudaError_t launch_shard_merge(const float* cs, const int32_t* cid, int n_shards, int k, int32_t* out_id,
                                float* out_score, cudaStream_t stream);
 

@@ -133,6 +133,21 @@ HC_API int hc_attention_dense(const void* q, const void* k, const void* v, const
                        void* stream);
 
 /*
+ * hc_attention_dense for callers that cannot allocate device memory (no
+ * counterpart in the reference): a host that binds this library over FFI and
+ * passes only its inputs and outputs, or a process whose device memory is all
+ * reserved by its own pool. Scratch and counters live in static device arrays
+ * of the library (8 MiB + 4096 counters, held on every GPU that loads it until
+ * exit); shapes needing more are rejected with HC_ERR_UNSUPPORTED. Calls share
+ * those arrays, so calls that overlap on the GPU race. The first call on a
+ * device resolves the arrays' addresses; make it before any stream capture.
+ * Allocates nothing: no cudaMalloc/cudaFree.
+ */
+HC_API int hc_attention_dense_noalloc(const void* q, const void* k, const void* v, const uint8_t* mask, void* out,
+                                      int64_t* evict_idx, int B, int Hq, int Hk, int S, int D, int dtype,
+                                      float scale, int overflow_nan, void* stream);
+
+/*
  * Decode-step append: RoPE of the new query/key with the model's cos/sin
  * (patch.py:161-162), append of (k_post, v, k_pre, pos) to the hot slab
  * (HotColdLayer.update, cache.py:130-151) and push of the head-mean query to
