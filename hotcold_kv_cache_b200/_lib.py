@@ -74,6 +74,7 @@ SIGNATURES = {
     "hc_attend_scratch_bytes": (c_size_t, [_P]),
     "hc_attend": (c_int, [_P, _P, _P, c_int, _P, c_int, _P, c_size_t, _P]),
     "hc_shard_merge": (c_int, [_P, _P, c_int, c_int, _P, _P, _P]),
+    "hc_step": (c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, c_int, _P, c_int, _P]),
 }
 
 _lib = None

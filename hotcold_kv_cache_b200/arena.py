@@ -103,6 +103,8 @@ class LayerArena:
         self.ws = workspace or Workspace(dev)
 
         self.pool_kernel, self.pooling, self.normalize, self.rope_scaling = pool_kernel, pooling, normalize, rope_scaling
+        self._step_ok: dict = {}
+        self.launches = 0  # kernels launched by the decode-path ops (append/compress/retrieve/attend/step)
         self._build_descriptors()
         # host mirrors
         self.n_hot = np.zeros(n_seq, np.int64)
@@ -201,6 +203,7 @@ class LayerArena:
                 self.st[s, 1] += g - c
         self.caps = grown
         self.max_cap = mc
+        self._step_ok = {}
         self._build_descriptors()
 
     # ------------------------------------------------------------------ helpers
@@ -208,10 +211,12 @@ class LayerArena:
         return _lib.stream_of(self.device)
 
     def _row_major(self, t: torch.Tensor, rows: int) -> tuple[torch.Tensor, int]:
-        """(n_seq, rows, D) view with contiguous rows; returns (tensor, seq stride)."""
+        """(n_seq, rows, D) view with contiguous, 16-byte aligned rows; returns (tensor, seq stride)."""
         t = t.reshape(self.n_seq, rows, self.D) if t.dim() != 3 else t
         if t.stride(2) != 1 or t.stride(1) != self.D:
             t = t.contiguous()
+        if t.data_ptr() % 16 or (t.stride(0) * t.element_size()) % 16:
+            t = t.clone(memory_format=torch.contiguous_format)
         return t, t.stride(0)
 
     def plan(self, s: int, S: int):
@@ -272,8 +277,60 @@ class LayerArena:
             sin = sin.reshape(self.n_seq, self.D).contiguous()
         call("hc_append", byref(self.L), ptr(q), qss, ptr(k), ptr(vv), kss, ptr(cos), ptr(sin), ptr(pos),
              ptr(self.q_post), self._stream())
+        self.launches += 1
         self.n_hot += 1
         return self.q_post
+
+    def step_supported(self, use_held: bool) -> bool:
+        """Whether the fused decode step fits this layer (one 16-CTA cluster per sequence)."""
+        key = bool(use_held)
+        if key not in self._step_ok:
+            ok = self.n_seq >= 1 and 16 % self.Hk == 0 and self.Hk <= 16
+            if ok:
+                # shared memory per CTA: K/V rows of its token part plus the leader's arrays
+                P = 16 // self.Hk
+                tokens = (self.r_max if use_held else 0) + self.max_cap
+                tpc = -(-tokens // P)
+                esz = self.hot_k.element_size()
+                G = self.Hq // self.Hk
+                need = 2 * tpc * self.D * esz + 4 * (self.Hk * self.max_cap * 2 + G * max(tpc, self.D) + 2048)
+                ok = need <= 220 * 1024
+            self._step_ok[key] = ok
+        return self._step_ok[key]
+
+    def step(self, q_pre, k_pre, v, cos, sin, pos, use_held: bool, overflow_nan: bool = True):
+        """Fused decode step: append + compression with eviction + attention over [held | hot]
+        in one launch (hc_step). Returns the output (n_seq,Hq,D), or None when the fused
+        kernel does not fit this layer (nothing launched; use append/compress/attend)."""
+        if (self.n_hot + 1 > np.asarray(self.caps)).any() or not self.step_supported(use_held):
+            return None
+        q, qss = self._row_major(q_pre, self.Hq)
+        k, kss = self._row_major(k_pre, self.Hk)
+        vv, vss = self._row_major(v, self.Hk)
+        if vss != kss:
+            k, vv = k.contiguous(), vv.contiguous()
+            kss = k.stride(0)
+        if cos is not None:
+            cos = cos.reshape(self.n_seq, self.D).contiguous()
+            sin = sin.reshape(self.n_seq, self.D).contiguous()
+        rc = _lib.load().hc_step(byref(self.L), ptr(q), qss, ptr(k), ptr(vv), kss, ptr(cos), ptr(sin), ptr(pos),
+                                 1 if use_held else 0, ptr(self.out), 1 if overflow_nan else 0, self._stream())
+        if rc == 3:  # HC_ERR_UNSUPPORTED: nothing was launched
+            self._step_ok[bool(use_held)] = False
+            return None
+        if rc != 0:
+            raise RuntimeError(f"hc_step failed (code {rc}): {_lib.load().hc_last_error().decode()}")
+        self.launches += 1
+        ev = np.zeros(self.n_seq, np.int64)
+        self.n_hot += 1
+        for s in range(self.n_seq):
+            p = self.plan(s, int(self.n_hot[s]))
+            if p is not None:
+                ev[s] = p[0] - p[1]
+        self.n_hot -= ev
+        for s in range(self.n_seq):
+            self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + ev[s])
+        return self.out, ev
 
     def append_rotated(self, k_post, k_pre, v, pos):
         if (self.n_hot + 1 > np.asarray(self.caps)).any():
@@ -304,6 +361,7 @@ class LayerArena:
         ws = self.ws.get(nbytes)
         call("hc_compress_ex", byref(self.L), ptr(q_obs), qs[0], qs[1], qs[2], tq, 0, None, None, None, 0, 0, 0, None,
              ptr(ws), ws.numel(), int(ev.max()), self._stream())
+        self.launches += 2 + (1 if int(ev.max()) > 32 else 0)
         self.n_hot -= ev
         for s in range(self.n_seq):
             self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + ev[s])
@@ -321,6 +379,7 @@ class LayerArena:
         mc = int(self.cold_count.max())
         call("hc_retrieve_ex", byref(self.L), ptr(q_dense), qd[0], qd[1], qd[2], P, int(n_pool), ptr(extra_sum),
              int(extra_n), ptr(qvec), ptr(ws), ws.numel(), mc, self._stream())
+        self.launches += 3 if qvec is not None else 4
 
     def prompt_query_sum(self, q_dense):
         out = torch.empty((self.n_seq, self.D), dtype=torch.float32, device=self.device)
@@ -335,6 +394,7 @@ class LayerArena:
         q = q_post if q_post.is_contiguous() else q_post.contiguous()
         call("hc_attend", byref(self.L), ptr(q), ptr(cur_pos), 1 if use_held else 0, ptr(self.out),
              1 if overflow_nan else 0, ptr(ws), ws.numel(), self._stream())
+        self.launches += 1
         return self.out
 
     def cold_append(self, k_pre, v, pos, evicted_idx):

@@ -136,6 +136,8 @@ class KVController:
         self.rotary = None  # (inv_freq tensor, attention_scaling); else the active rotary module
         # optional callable(op_name, "begin"|"end") around each op of decode_layer (timing probes)
         self.op_hook = None
+        # decode steps without a search run as one fused launch (hc_step) when the layer fits
+        self.fused_step = True
         self.dbg = {k: (0.0 if k == "prefetch_copy_ms_sum" else 0) for k in DBG_KEYS}
 
     # ------------------------------------------------------------------ setup
@@ -405,6 +407,21 @@ class KVController:
         li = int(layer_idx)
         a = self.arena(li, q_pre.shape[1], k_pre.dtype, k_pre.device)
         hook = self.op_hook or (lambda name, phase: None)
+        if self.fused_step and not self._retrieval_fires(li):
+            # no search this step: append + compression + attention in one launch
+            use_held = self._poll_use_held(li)
+            hook("step", "begin")
+            res = a.step(q_pre, k_pre, v, cos, sin, pos, use_held, self.overflow_nan)
+            hook("step", "end")
+            if res is not None:
+                self._qpool[li].append(1)
+                self.maybe_launch_async_retrieval(li)  # counts the call; no search fires here
+                out, ev = res
+                self._count_eviction(ev)
+                self._count_injection(a, use_held)
+                self.dbg["triton_decode_calls"] += 1
+                return out
+            self._undo_poll(li, use_held)
         hook("append", "begin")
         q_post = a.append(q_pre, k_pre, v, cos, sin, pos)
         hook("append", "end")
@@ -416,6 +433,27 @@ class KVController:
         ev = a.compress_decode(q_post.view(a.n_seq, a.Hq, 1, a.D))
         self._count_eviction(ev)
         hook("compress", "end")
+        use_held = self._poll_use_held(li)
+        self._count_injection(a, use_held)
+        self.dbg["triton_decode_calls"] += 1
+        hook("attend", "begin")
+        out = a.attend(q_post, pos, use_held, self.overflow_nan)
+        hook("attend", "end")
+        return out
+
+    def _retrieval_fires(self, li: int) -> bool:
+        """Whether the next maybe_launch_async_retrieval(li) launches a search."""
+        if self.lookahead_k <= 0 or (self.step_count[li] + 1) % self.window_size != 0:
+            return False
+        if self.cold_size(li) == 0:
+            return False
+        n_pool, _, extra_n = self._pool(li)
+        return n_pool + 1 > 0 or extra_n > 0
+
+    def _poll_use_held(self, li: int) -> bool:
+        """patch.py:241-261: attend the retrieved set staged since the last step (and keep it
+        when holding), or the held set."""
+        self._poll_undo = (self._staged[li], self._held_active[li], dict(self.dbg))
         use_held = False
         if self._staged[li]:
             self._staged[li] = False
@@ -428,14 +466,15 @@ class KVController:
             use_held = True
         if not self.hold_retrieved:
             self._held_active[li] = use_held
+        return use_held
+
+    def _undo_poll(self, li: int, use_held: bool):
+        self._staged[li], self._held_active[li], self.dbg = self._poll_undo
+
+    def _count_injection(self, a, use_held: bool):
         self.last_injected_len = a.r_max if use_held else 0
         if use_held:
             self.dbg["injection_used"] += 1
-        self.dbg["triton_decode_calls"] += 1
-        hook("attend", "begin")
-        out = a.attend(q_post, pos, use_held, self.overflow_nan)
-        hook("attend", "end")
-        return out
 
     def device_status(self) -> int:
         """OR of the device status words of every layer (synchronises): HC_DEV_* bits."""

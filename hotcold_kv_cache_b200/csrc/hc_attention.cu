@@ -87,10 +87,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
     mbar_init(&bars[1], 1);
     fence_mbar_init();
   }
-  // query heads of this KV head -> shared (float)
-  const T* qg = reinterpret_cast<const T*>(a.q) + ((size_t)s * a.Hq + (size_t)h * G) * D;
-  for (int i = tid; i < G * D; i += kAttnThreads) sQ[i] = E::to_f(qg[i]);
-  __syncthreads();
 
   // ---- resolve rows and issue the bulk copies -------------------------------------------
   const T* krow = nullptr;
@@ -139,6 +135,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
       sV[(size_t)tid * D + i] = E::from_f(0.f);
     }
   }
+  // query heads of this KV head -> shared (float), while the rows are in flight
+  const T* qg = reinterpret_cast<const T*>(a.q) + ((size_t)s * a.Hq + (size_t)h * G) * D;
+  for (int i = tid; i < G * D; i += kAttnThreads) sQ[i] = E::to_f(qg[i]);
+  __syncthreads();
   // q fragments in registers: lane `sub` owns d = j*8*VEC + sub*VEC + e
   const int sub = lane & 7, tk = lane >> 3;
   float qr[G][NJ * VEC];

@@ -108,6 +108,10 @@ int hc_append(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const 
   if (!q_pre || !k_pre || !v || !pos || !q_post) return fail(HC_ERR_ARG, "NULL tensor argument");
   if ((cos == nullptr) != (sin == nullptr)) return fail(HC_ERR_ARG, "cos and sin must both be given or both NULL");
   if (!cos && !L->inv_freq) return fail(HC_ERR_ARG, "no cos/sin and no inv_freq");
+  const int64_t esz = L->dtype == HC_F32 ? 4 : 2;
+  if (!aligned16(q_pre) || !aligned16(k_pre) || !aligned16(v) || ((q_stride_seq * esz) & 15) ||
+      ((kv_stride_seq * esz) & 15))
+    return fail(HC_ERR_ARG, "query/key/value rows must be 16-byte aligned");
   return check_cuda(hc::launch_append(*L, q_pre, q_stride_seq, k_pre, v, kv_stride_seq, cos, sin, pos, q_post,
                                       reinterpret_cast<cudaStream_t>(stream)),
                     "append");
@@ -243,6 +247,26 @@ int hc_attend(const hc_layer* L, const void* q_post, const int64_t* cur_pos, int
   return check_cuda(hc::launch_attention(a, L->dtype, L->D, L->Hq / L->Hk, L->n_seq, max_tokens, false,
                                          reinterpret_cast<cudaStream_t>(stream)),
                     "attend");
+}
+
+int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const void* k_pre, const void* v,
+            int64_t kv_stride_seq, const void* cos, const void* sin, const int64_t* pos, int use_held, void* out,
+            int overflow_nan, void* stream) {
+  if (int rc = check_layer(L)) return rc;
+  if (!q_pre || !k_pre || !v || !pos || !out) return fail(HC_ERR_ARG, "NULL tensor argument");
+  if ((cos == nullptr) != (sin == nullptr)) return fail(HC_ERR_ARG, "cos and sin must both be given or both NULL");
+  if (!cos && !L->inv_freq) return fail(HC_ERR_ARG, "no cos/sin and no inv_freq");
+  if (!hc::step_parts(L->Hk)) return fail(HC_ERR_UNSUPPORTED, "KV heads %d do not divide a 16-CTA cluster", L->Hk);
+  const size_t smem = hc::step_smem_bytes(*L, use_held);
+  if (smem == 0 || smem > 227 * 1024)
+    return fail(HC_ERR_UNSUPPORTED, "fused step needs %zu bytes of shared memory per CTA", smem);
+  const cudaError_t e = hc::launch_step(*L, q_pre, q_stride_seq, k_pre, v, kv_stride_seq, cos, sin, pos, use_held, out,
+                                        overflow_nan, reinterpret_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported) {
+    (void)cudaGetLastError();
+    return fail(HC_ERR_UNSUPPORTED, "no resident 16-CTA cluster for this shared memory size");
+  }
+  return check_cuda(e, "step");
 }
 
 int hc_shard_merge(const float* cand_score, const int32_t* cand_id, int n_shards, int k, int32_t* out_id,

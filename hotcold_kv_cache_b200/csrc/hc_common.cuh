@@ -192,7 +192,13 @@ __device__ __forceinline__ void set_status(hc_seq_state* st, int bits) {
 // Programmatic dependent launch: let the next kernel in the stream start its prologue,
 // and wait for the previous one before touching its outputs.
 // ----------------------------------------------------------------------------------------
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Waits for the preceding kernel of the stream, then lets the next one begin launching at once:
+// every kernel launched with programmatic serialization starts with this call, so a dependent
+// never reads this kernel's results before this kernel has completed.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }

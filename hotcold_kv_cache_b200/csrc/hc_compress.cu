@@ -23,17 +23,15 @@
 //                  tokens into the slab.
 // Scores are float32 throughout (the reference rounds its GPU logits to the model dtype).
 
+#include "hc_internal.cuh"
 #include "hc_topk.cuh"
 
 namespace hc {
 
 constexpr int kScoreCH = 64;        // tokens per score CTA
 constexpr int kInlineEvict = 32;    // evictions copied by the select CTA itself
-constexpr int kSmallSelect = 1 << 20;  // Hk*tq*S up to which select computes token scores
+constexpr size_t kSelectSmemMax = 200 * 1024;  // shared memory of the selection CTA's small path
 
-struct Plan {
-  int S, prefix, ntop, nobs, active;
-};
 
 // cache.py:44-53 (hot/cold) or scoring.py:117-120 with the trigger of cache.py:44 (SnapKV).
 __device__ __forceinline__ Plan make_plan(const hc_layer& L, int budget, int S) {
@@ -337,28 +335,48 @@ __device__ void evict_one(const CompressArgs& a, const hc_seq_desc& d, int s, in
   float mean[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) mean[i] = 0.f;
-  T* ck = reinterpret_cast<T*>(d.cold_kpre) + (size_t)dst * L.Hk * D;
-  T* cv = reinterpret_cast<T*>(d.cold_v) + (size_t)dst * L.Hk * D;
-  for (int h = 0; h < L.Hk; ++h) {
-    const T* kp;
-    const T* vp;
-    if constexpr (DENSE) {
-      const size_t off = (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)src * a.ss_tok;
-      kp = reinterpret_cast<const T*>(a.src_kpre) + off;
-      vp = reinterpret_cast<const T*>(a.src_v) + off;
-    } else {
-      const size_t off = ((size_t)h * d.cap + src) * D;
-      kp = reinterpret_cast<const T*>(d.hot_kpre) + off;
-      vp = reinterpret_cast<const T*>(d.hot_v) + off;
+  T* __restrict__ ck = reinterpret_cast<T*>(d.cold_kpre) + (size_t)dst * L.Hk * D;
+  T* __restrict__ cv = reinterpret_cast<T*>(d.cold_v) + (size_t)dst * L.Hk * D;
+  // heads in groups of 8: all loads of a group first, then the stores (no load waits on a store)
+  for (int h0 = 0; h0 < L.Hk; h0 += 8) {
+    const int nh = min(8, L.Hk - h0);
+    T kr[8][PER], vr[8][PER];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= nh) break;
+      const int h = h0 + j;
+      const T* __restrict__ kp;
+      const T* __restrict__ vp;
+      if constexpr (DENSE) {
+        const size_t off = (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)src * a.ss_tok;
+        kp = reinterpret_cast<const T*>(a.src_kpre) + off;
+        vp = reinterpret_cast<const T*>(a.src_v) + off;
+      } else {
+        const size_t off = ((size_t)h * d.cap + src) * D;
+        kp = reinterpret_cast<const T*>(d.hot_kpre) + off;
+        vp = reinterpret_cast<const T*>(d.hot_v) + off;
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int dd = lane + 32 * i;
+        if (dd < D) {
+          kr[j][i] = kp[dd];
+          vr[j][i] = vp[dd];
+        }
+      }
     }
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int dd = lane + 32 * i;
-      if (dd < D) {
-        const T kv = kp[dd];
-        ck[(size_t)h * D + dd] = kv;
-        cv[(size_t)h * D + dd] = vp[dd];
-        mean[i] += E::to_f(kv);
+    for (int j = 0; j < 8; ++j) {
+      if (j >= nh) break;
+      const int h = h0 + j;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int dd = lane + 32 * i;
+        if (dd < D) {
+          ck[(size_t)h * D + dd] = kr[j][i];
+          cv[(size_t)h * D + dd] = vr[j][i];
+          mean[i] += E::to_f(kr[j][i]);
+        }
       }
     }
   }
@@ -425,13 +443,25 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
   uint8_t* sel = a.sel + (size_t)s * a.S_max;
 
   if (small) {
-    if (L.policy == HC_POLICY_SNAPKV) {
-      // softmax statistics per (head, row), one warp each
+    // everything in shared memory: logits [rows][S] -> (SnapKV) importance [Hk][S] -> scores [S]
+    extern __shared__ __align__(16) float dyn[];
+    const bool snap = L.policy == HC_POLICY_SNAPKV;
+    const int rows = L.Hk * (snap ? tqu : 1);
+    float* sLg = dyn;                      // rows * S
+    float* sImp = sLg + (size_t)rows * S;  // Hk * S (SnapKV)
+    float* sStat = sImp + (snap ? (size_t)L.Hk * S : 0);  // rows * 2
+    float* sTok = sStat + 2 * rows;        // S
+    uint8_t* sSel = reinterpret_cast<uint8_t*>(sTok + S);
+    for (int i = tid; i < rows * S; i += blockDim.x) {
+      const int row = i / S, t = i % S;
+      const size_t g = snap ? (((size_t)s * L.Hk + row / tqu) * a.tqmax + row % tqu) : ((size_t)s * L.Hk + row);
+      sLg[i] = a.logits[g * a.S_max + t];
+    }
+    __syncthreads();
+    if (snap) {
       const int warp = tid >> 5, lane = tid & 31;
-      for (int i = warp; i < L.Hk * tqu; i += 32) {
-        const int h = i / tqu, r = i % tqu;
-        const size_t row = ((size_t)s * L.Hk + h) * a.tqmax + r;
-        const float* lg = a.logits + row * a.S_max;
+      for (int r = warp; r < rows; r += blockDim.x >> 5) {
+        const float* lg = sLg + (size_t)r * S;
         float m = kNegInf;
         for (int t = lane; t < S; t += 32) m = fmaxf(m, lg[t]);
         m = warp_max(m);
@@ -439,19 +469,53 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
         for (int t = lane; t < S; t += 32) l += (lg[t] == kNegInf) ? 0.f : __expf(lg[t] - m);
         l = warp_sum(l);
         if (lane == 0) {
-          a.stats[row * 2] = m;
-          a.stats[row * 2 + 1] = l;
+          sStat[2 * r] = m;
+          sStat[2 * r + 1] = l;
         }
       }
       __syncthreads();
       for (int i = tid; i < L.Hk * S; i += blockDim.x) {
         const int h = i / S, t = i % S;
-        a.imp[((size_t)s * L.Hk + h) * a.S_max + t] = snap_imp(a, s, h, tqu, t);
+        float acc = 0.f;
+        for (int r = 0; r < tqu; ++r) {
+          const int row = h * tqu + r;
+          const float x = sLg[(size_t)row * S + t];
+          acc += (x == kNegInf) ? 0.f : __expf(x - sStat[2 * row]) / sStat[2 * row + 1];
+        }
+        sImp[i] = acc;
       }
       __syncthreads();
+      const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
+      for (int t = tid; t < S; t += blockDim.x) {
+        float tot = 0.f;
+        for (int h = 0; h < L.Hk; ++h) {
+          const float* imp = sImp + (size_t)h * S;
+          float v;
+          if (pad == 0) {
+            v = imp[t];
+          } else if (L.pooling == HC_POOL_MAX) {
+            v = kNegInf;
+            for (int u = max(0, t - pad); u <= min(S - 1, t + pad); ++u) v = fmaxf(v, imp[u]);
+          } else {
+            v = 0.f;
+            for (int u = max(0, t - pad); u <= min(S - 1, t + pad); ++u) v += imp[u];
+            v /= (float)L.pool_kernel;
+          }
+          tot += v;
+        }
+        sTok[t] = tot / (float)L.Hk;
+      }
+    } else {
+      const float inv = 1.f / sqrtf((float)L.D);
+      for (int t = tid; t < S; t += blockDim.x) {
+        float acc = 0.f;
+        for (int h = 0; h < L.Hk; ++h) acc += sLg[(size_t)h * S + t] * inv;
+        sTok[t] = acc / (float)L.Hk;
+      }
     }
-    for (int t = tid; t < S; t += blockDim.x) tok[t] = token_score(a, s, tqu, S, t);
     __syncthreads();
+    tok = sTok;
+    sel = sSel;
   }
 
   // exact top-n_top of the prefix
@@ -683,8 +747,12 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
   const int chunks = (S_grid + kScoreCH - 1) / kScoreCH;
   e = launch_pdl(sk, dim3(chunks, L.Hk, L.n_seq), dim3(128), smem, stream, a);
   if (e != cudaSuccess) return e;
-  const long work = (long)L.Hk * (L.policy == HC_POLICY_SNAPKV ? a.tqmax : 1) * S_grid;
-  const int small = work <= kSmallSelect ? 1 : 0;
+  // the selection CTA computes the token scores itself when its inputs fit shared memory
+  const bool snap = L.policy == HC_POLICY_SNAPKV;
+  const size_t rows = (size_t)L.Hk * (snap ? a.tqmax : 1);
+  const size_t sel_smem =
+      4 * (rows * S_grid + (snap ? (size_t)L.Hk * S_grid : 0) + 2 * rows + (size_t)S_grid) + S_grid + 64;
+  const int small = sel_smem <= kSelectSmemMax ? 1 : 0;
   if (!small) {
     const int blocks = (int)((S_grid + 255) / 256) < 592 ? (S_grid + 255) / 256 : 592;
     if (L.policy == HC_POLICY_SNAPKV) {
@@ -697,7 +765,10 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
     e = launch_pdl(token_kernel<DENSE>, dim3(blocks > 0 ? blocks : 1, L.n_seq), dim3(256), 0, stream, a);
     if (e != cudaSuccess) return e;
   }
-  e = launch_pdl(select_kernel<DT, D, DENSE>, dim3(L.n_seq), dim3(1024), 0, stream, a, small);
+  auto selk = select_kernel<DT, D, DENSE>;
+  e = ensure_smem(selk, kSelectSmemMax);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(selk, dim3(L.n_seq), dim3(1024), small ? sel_smem : 0, stream, a, small);
   if (e != cudaSuccess) return e;
   if (DENSE || n_evict_hint > kInlineEvict) {
     const int items = DENSE ? S_grid : n_evict_hint;

@@ -4,6 +4,12 @@
 
 namespace hc {
 
+// A compression of S hot tokens: keep the top n_top of the first `prefix` plus the tail;
+// `nobs` caps the observation query rows; active = 0 when nothing is compressed.
+struct Plan {
+  int S, prefix, ntop, nobs, active;
+};
+
 struct AttnArgs {
   // slab mode
   const hc_seq_desc* desc;
@@ -49,6 +55,12 @@ cudaError_t launch_append_rotated(const hc_layer& L, const void* kpost, const vo
 cudaError_t launch_cold_append(const hc_layer& L, const void* kpre, const void* v, int64_t s0, int64_t s1, int64_t s2,
                                const int64_t* pos, const int64_t* idx, int Te, cudaStream_t st);
 size_t retrieve_scratch_bytes(const hc_layer& L);
+cudaError_t launch_step(const hc_layer& L, const void* q, int64_t qss, const void* k, const void* v, int64_t kvss,
+                        const void* c, const void* sn, const int64_t* pos, int use_held, void* out, int overflow_nan,
+                        cudaStream_t stream);
+size_t step_smem_bytes(const hc_layer& L, int use_held);
+int step_parts(int Hk);
+
 // Set the message hc_last_error() returns on the calling thread.
 void set_last_error(const char* msg);
 

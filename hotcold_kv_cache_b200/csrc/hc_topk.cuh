@@ -28,9 +28,17 @@ __device__ void block_topk_flags(Getter x, int n, int k, uint8_t* sel, int* sh) 
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int b = tid; b < 256; b += nthr) hist[b] = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += nthr) {
-      const uint32_t key = fkey(x(i));
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    // scores cluster into few bins, so lanes of a warp that hit the same bin add once together
+    for (int base = 0; base < n; base += nthr) {
+      const int i = base + tid;
+      const uint32_t key = i < n ? fkey(x(i)) : 0u;
+      const bool live = i < n && (key & mask) == prefix;
+      const unsigned act = __ballot_sync(0xffffffffu, live);
+      if (live) {
+        const uint32_t bin = (key >> shift) & 255u;
+        const unsigned same = __match_any_sync(act, bin);
+        if ((threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
+      }
     }
     __syncthreads();
     if (tid < 32) {

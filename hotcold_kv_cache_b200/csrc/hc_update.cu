@@ -13,13 +13,47 @@ namespace hc {
 // apply_rotary_pos_emb), appends (k_post, v, k_pre, pos) to the slab, and pushes the
 // mean over query heads of the pre-RoPE query into the query pool ring
 // (controller.py:240-241; the pool is later averaged by controller.py:185).
+// 16 bytes of elements as floats, and back.
+template <int DT>
+__device__ __forceinline__ void load_vec(const typename Elem<DT>::T* __restrict__ p, float* f) {
+  unpack16<DT>(*reinterpret_cast<const uint4*>(p), f);
+}
+template <int DT>
+__device__ __forceinline__ void store_vec(typename Elem<DT>::T* __restrict__ p, const float* f) {
+  using T = typename Elem<DT>::T;
+  constexpr int V = 16 / sizeof(T);
+  alignas(16) T tmp[V];
+#pragma unroll
+  for (int e = 0; e < V; ++e) tmp[e] = Elem<DT>::from_f(f[e]);
+  *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(tmp);
+}
+
+// RoPE of one (head, 16-byte chunk) pair: lo = x[j*V..], hi = x[H + j*V..].
 template <int DT, int D>
-__global__ void __launch_bounds__(256) append_kernel(hc_layer L, const void* q_pre_, int64_t qss, const void* k_pre_,
-                                                     const void* v_, int64_t kvss, const void* cos_, const void* sin_,
-                                                     const int64_t* pos, void* q_post_) {
+__device__ __forceinline__ void rope_pair(const typename Elem<DT>::T* __restrict__ x, int j, const float* c,
+                                          const float* s, float* lo, float* hi) {
+  constexpr int H = D / 2, V = 16 / sizeof(typename Elem<DT>::T);
+  float xl[V], xh[V];
+  load_vec<DT>(x + j * V, xl);
+  load_vec<DT>(x + H + j * V, xh);
+#pragma unroll
+  for (int e = 0; e < V; ++e) {
+    lo[e] = rope_elem<DT>(xl[e], -xh[e], c[e], s[e]);
+    hi[e] = rope_elem<DT>(xh[e], xl[e], c[V + e], s[V + e]);
+  }
+}
+
+template <int DT, int D>
+__global__ void __launch_bounds__(256) append_kernel(hc_layer L, const void* __restrict__ q_pre_, int64_t qss,
+                                                     const void* __restrict__ k_pre_, const void* __restrict__ v_,
+                                                     int64_t kvss, const void* __restrict__ cos_,
+                                                     const void* __restrict__ sin_, const int64_t* __restrict__ pos,
+                                                     void* __restrict__ q_post_) {
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int H = D / 2;
+  constexpr int V = 16 / sizeof(T);
+  constexpr int NV = H / V;  // 16-byte chunks per half row
   const int s = blockIdx.x;
   __shared__ float sc[D], ss[D];
   __shared__ int sSlot, sOrdAt;
@@ -55,30 +89,40 @@ __global__ void __launch_bounds__(256) append_kernel(hc_layer L, const void* q_p
   }
   __syncthreads();
   const int slot = sSlot;
-  const T* q = reinterpret_cast<const T*>(q_pre_) + (size_t)s * qss;
-  const T* k = reinterpret_cast<const T*>(k_pre_) + (size_t)s * kvss;
-  const T* v = reinterpret_cast<const T*>(v_) + (size_t)s * kvss;
-  T* qo = reinterpret_cast<T*>(q_post_) + (size_t)s * L.Hq * D;
-  // query heads: RoPE -> q_post
-  for (int i = threadIdx.x; i < L.Hq * D; i += blockDim.x) {
-    const int dd = i % D;
-    const float x = E::to_f(q[i]);
-    const float r = dd < H ? -E::to_f(q[i + H]) : E::to_f(q[i - H]);
-    qo[i] = E::from_f(rope_elem<DT>(x, r, sc[dd], ss[dd]));
-  }
-  // key heads: RoPE -> slab (post), pre-RoPE key and value -> slab
-  if (slot >= 0) {
-    T* hk = reinterpret_cast<T*>(d.hot_k);
-    T* hv = reinterpret_cast<T*>(d.hot_v);
-    T* hp = reinterpret_cast<T*>(d.hot_kpre);
-    for (int i = threadIdx.x; i < L.Hk * D; i += blockDim.x) {
-      const int h = i / D, dd = i % D;
-      const float x = E::to_f(k[i]);
-      const float r = dd < H ? -E::to_f(k[i + H]) : E::to_f(k[i - H]);
-      const size_t off = ((size_t)h * d.cap + slot) * D + dd;
-      hk[off] = E::from_f(rope_elem<DT>(x, r, sc[dd], ss[dd]));
-      hp[off] = k[i];
-      hv[off] = v[i];
+  const T* __restrict__ q = reinterpret_cast<const T*>(q_pre_) + (size_t)s * qss;
+  const T* __restrict__ k = reinterpret_cast<const T*>(k_pre_) + (size_t)s * kvss;
+  const T* __restrict__ v = reinterpret_cast<const T*>(v_) + (size_t)s * kvss;
+  T* __restrict__ qo = reinterpret_cast<T*>(q_post_) + (size_t)s * L.Hq * D;
+  // one work item = (head, 16-byte chunk j of the first half) -> both RoPE halves
+  const int n_q = L.Hq * NV, n_k = L.Hk * NV;
+  for (int it = threadIdx.x; it < n_q + n_k; it += blockDim.x) {
+    const bool isq = it < n_q;
+    const int h = (isq ? it : it - n_q) / NV, j = (isq ? it : it - n_q) % NV;
+    float c[2 * V], sn[2 * V], lo[V], hi[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      c[e] = sc[j * V + e];
+      sn[e] = ss[j * V + e];
+      c[V + e] = sc[H + j * V + e];
+      sn[V + e] = ss[H + j * V + e];
+    }
+    if (isq) {
+      rope_pair<DT, D>(q + (size_t)h * D, j, c, sn, lo, hi);
+      store_vec<DT>(qo + (size_t)h * D + j * V, lo);
+      store_vec<DT>(qo + (size_t)h * D + H + j * V, hi);
+    } else if (slot >= 0) {
+      // post-RoPE key, pre-RoPE key and value of KV head h into the slab
+      rope_pair<DT, D>(k + (size_t)h * D, j, c, sn, lo, hi);
+      const size_t off = ((size_t)h * d.cap + slot) * D;
+      T* hk = reinterpret_cast<T*>(d.hot_k) + off;
+      T* hp = reinterpret_cast<T*>(d.hot_kpre) + off;
+      T* hv = reinterpret_cast<T*>(d.hot_v) + off;
+      store_vec<DT>(hk + j * V, lo);
+      store_vec<DT>(hk + H + j * V, hi);
+      *reinterpret_cast<uint4*>(hp + j * V) = *reinterpret_cast<const uint4*>(k + (size_t)h * D + j * V);
+      *reinterpret_cast<uint4*>(hp + H + j * V) = *reinterpret_cast<const uint4*>(k + (size_t)h * D + H + j * V);
+      *reinterpret_cast<uint4*>(hv + j * V) = *reinterpret_cast<const uint4*>(v + (size_t)h * D + j * V);
+      *reinterpret_cast<uint4*>(hv + H + j * V) = *reinterpret_cast<const uint4*>(v + (size_t)h * D + H + j * V);
     }
   }
   // query pool: mean over heads of the pre-RoPE query, rounded to the model dtype
@@ -87,6 +131,7 @@ __global__ void __launch_bounds__(256) append_kernel(hc_layer L, const void* q_p
     T* qw = reinterpret_cast<T*>(d.qwin) + (size_t)qh * D;
     for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
       float acc = 0.f;
+#pragma unroll 8
       for (int h = 0; h < L.Hq; ++h) acc += E::to_f(q[(size_t)h * D + dd]);
       qw[dd] = E::from_f(acc / (float)L.Hq);
     }

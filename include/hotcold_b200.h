@@ -263,6 +263,18 @@ HC_API int hc_attend(const hc_layer* L, const void* q_post, const int64_t* cur_p
               int overflow_nan, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * Fused decode step of one layer: hc_append, hc_compress (decode, slab source)
+ * and hc_attend in one launch (patch.py:151-305 with cache.py:37-151 and the
+ * kernel of kernels.py:9-74), one 16-CTA thread-block cluster per sequence
+ * (CTA = KV head x token part). Same arguments and results as the three calls
+ * in sequence; out (n_seq,Hq,D). Returns HC_ERR_UNSUPPORTED (nothing launched)
+ * when the layer does not fit one cluster; callers then use the three calls.
+ */
+HC_API int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const void* k_pre, const void* v,
+                   int64_t kv_stride_seq, const void* cos, const void* sin, const int64_t* pos, int use_held,
+                   void* out, int overflow_nan, void* stream);
+
+/*
  * Multi-GPU cold search over a token-range shard: merge of per-shard top-k
  * candidates gathered from all ranks (no reference counterpart; the reference
  * is single-device). cand_score/cand_id (n_shards*k) fp32/int32, global ids;

@@ -30,7 +30,7 @@ def controller_kwargs(case):
                 pool_kernel=c.get("pool_kernel", 7))
 
 
-def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True):
+def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused=True):
     """Returns dict(outs (n,B,Hq,D) float64, hot [per-step (B,S) int64], held {step: (pos, valid, k)},
     ctrl). model_cos=True passes HF's cos/sin tables to the append kernel (what the patched
     forward does); False lets the kernel compute them from inv_freq."""
@@ -44,6 +44,7 @@ def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True):
 
     rot = rotary(Hq, D, c["theta"], dev)
     ctrl = KVController(**controller_kwargs(c))
+    ctrl.fused_step = fused
     ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
     q_pre, k_pre, v = t(inputs["q_pre"]), t(inputs["k_pre"]), t(inputs["v"])
     ctrl._lazy_init(k_pre, n_layers=1)

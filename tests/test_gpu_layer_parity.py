@@ -73,6 +73,46 @@ def test_layer_vs_oracle_and_golden(name, model_cos):
     assert ctrl.device_status() == 0
 
 
+@pytest.mark.parametrize("name", LAYER_CASES)
+def test_fused_step_matches_split_ops(name):
+    """hc_step (one cluster launch) against hc_append + hc_compress + hc_attend."""
+    from cuda_runner import run_cuda_layer
+    c = load(name)["case"]
+    fused = run_cuda_layer(c, inputs(c), c["steps"], fused=True)
+    split = run_cuda_layer(c, inputs(c), c["steps"], fused=False)
+    for i in range(c["steps"]):
+        assert np.array_equal(fused["hot"][i], split["hot"][i]), f"hot set differs at step {i + 1}"
+        assert_close(fused["outs"][i], split["outs"][i], c["dtype"], f"attention step {i + 1}")
+    assert sorted(fused["held"]) == sorted(split["held"])
+    assert fused["ctrl"].dbg == split["ctrl"].dbg
+    a_f, a_s = fused["ctrl"].arenas[0], split["ctrl"].arenas[0]
+    assert a_f.launches < a_s.launches, "the fused step did not run"
+    assert fused["ctrl"].device_status() == 0
+
+
+@pytest.mark.parametrize("policy", ["snapkv", "hotcold"])
+def test_fused_step_bench_geometry(policy):
+    """The benchmark's layer geometry (fp16, 32/8 heads, budget 512, 64 held): 289 tokens per
+    CTA, more than its 256 threads. Fused against the oracle and against the split ops."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import run_cuda_layer
+    recent = 32 if policy == "snapkv" else 128
+    c = dict(B=1, Hq=32, Hk=8, D=128, T=1024, steps=8, dtype="float16", policy=policy, cap=512, recent=recent,
+             topk_ratio=0.0 if policy == "snapkv" else 0.5, pool_kernel=7, ccap=4096, faiss_dim=128,
+             window_size=1 << 20, pool=4, R=64, hold=True, rap=True, theta=500000.0, seed=77)
+    inp = synth.layer_inputs(c["seed"], 1, 32, 8, 128, c["T"], c["steps"], "float16")
+    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], **oracle_kwargs(c))
+    fused = run_cuda_layer(c, inp, c["steps"], fused=True)
+    split = run_cuda_layer(c, inp, c["steps"], fused=False)
+    # one launch per fused step, plus the 4 kernels of the prompt-end retrieval
+    assert fused["ctrl"].arenas[0].launches == c["steps"] + 4, "the fused step did not run"
+    for i in range(c["steps"]):
+        assert np.array_equal(fused["hot"][i], split["hot"][i]), f"fused vs split hot set, step {i + 1}"
+        assert_close(fused["outs"][i], split["outs"][i], "float16", f"fused vs split, step {i + 1}")
+    assert _compare_layer(fused, c, layer, o_outs, o_hot, near_tie=2e-3) >= 1
+    assert fused["ctrl"].device_status() == 0
+
+
 @pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
 @pytest.mark.parametrize("policy", ["hotcold", "snapkv"])
 def test_random_configs_vs_oracle(dtype, policy):
