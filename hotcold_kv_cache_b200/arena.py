@@ -285,17 +285,10 @@ class LayerArena:
         """Whether the fused decode step fits this layer (one 16-CTA cluster per sequence)."""
         key = bool(use_held)
         if key not in self._step_ok:
-            ok = self.n_seq >= 1 and 16 % self.Hk == 0 and self.Hk <= 16
-            if ok:
-                # shared memory per CTA: K/V rows of its token part plus the leader's arrays
-                P = 16 // self.Hk
-                tokens = (self.r_max if use_held else 0) + self.max_cap
-                tpc = -(-tokens // P)
-                esz = self.hot_k.element_size()
-                G = self.Hq // self.Hk
-                need = 2 * tpc * self.D * esz + 4 * (self.Hk * self.max_cap * 2 + G * max(tpc, self.D) + 2048)
-                ok = need <= 220 * 1024
-            self._step_ok[key] = ok
+            # structural limits; the shared memory fit is decided by hc_step itself, which
+            # returns HC_ERR_UNSUPPORTED without launching anything
+            self._step_ok[key] = (self.n_seq >= 1 and self.Hk <= 16 and 16 % self.Hk == 0
+                                  and self.Hq // self.Hk in (1, 2, 4, 8))
         return self._step_ok[key]
 
     def step(self, q_pre, k_pre, v, cos, sin, pos, use_held: bool, overflow_nan: bool = True):
