@@ -40,12 +40,12 @@ class HcLayer(Structure):
                 ("n_seq", c_int32), ("Hq", c_int32), ("Hk", c_int32), ("D", c_int32), ("F", c_int32),
                 ("dtype", c_int32), ("policy", c_int32), ("recent", c_int32), ("pool_kernel", c_int32),
                 ("pooling", c_int32), ("normalize", c_int32), ("max_cap", c_int32), ("max_r", c_int32),
-                ("max_ccap", c_int32), ("scale", c_float), ("rope_scaling", c_float)]
+                ("max_ccap", c_int32), ("scale", c_float), ("rope_scaling", c_float), ("kmaps", c_void_p)]
 
 
 assert ctypes.sizeof(HcSeqState) == 64
 assert ctypes.sizeof(HcSeqDesc) == 160
-assert ctypes.sizeof(HcLayer) == 96
+assert ctypes.sizeof(HcLayer) == 104
 
 _P = c_void_p
 _I64 = c_int64
@@ -74,6 +74,7 @@ SIGNATURES = {
     "hc_attend_scratch_bytes": (c_size_t, [_P]),
     "hc_attend": (c_int, [_P, _P, _P, c_int, _P, c_int, _P, c_size_t, _P]),
     "hc_shard_merge": (c_int, [_P, _P, c_int, c_int, _P, _P, _P]),
+    "hc_encode_kmap": (c_int, [_P, _P, c_int, _I64, c_int, c_int]),
     "hc_step": (c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, c_int, _P, c_int, _P]),
 }
 

@@ -151,7 +151,27 @@ class LayerArena:
         L.max_cap, L.max_r, L.max_ccap = mc, self.r_max, C
         L.scale = 1.0 / math.sqrt(self.D)
         L.rope_scaling = float(self.rope_scaling)
+        L.kmaps = self._encode_kmaps()
         self.L = L
+
+    def _encode_kmaps(self):
+        """TMA tensor maps of the hot K slab (all sequences as rows of D, 64-row boxes) and the
+        held K rows (8-row boxes) for the fused step's 16-bit path; 0 when unavailable."""
+        self.kmaps = None
+        if self.dtype not in (torch.float16, torch.bfloat16):
+            return 0
+        buf = (ctypes.c_uint8 * 256)()
+        code = _lib.dtype_code(self.dtype)
+        lib = _lib.load()
+        rc = lib.hc_encode_kmap(ctypes.addressof(buf), self.hot_k.data_ptr(), code,
+                                self.hot_k.numel() // self.D, self.D, 64)
+        if rc == 0:
+            rc = lib.hc_encode_kmap(ctypes.addressof(buf) + 128, self.held_k.data_ptr(), code,
+                                    self.held_k.numel() // self.D, self.D, 8)
+        if rc != 0:
+            return 0
+        self.kmaps = torch.frombuffer(bytearray(bytes(buf)), dtype=torch.uint8).to(self.device)
+        return self.kmaps.data_ptr()
 
     def ensure_hot_capacity(self, need):
         """Grow the physical hot slab so that sequence s can hold need[s] tokens (capped at

@@ -1,8 +1,13 @@
 // C ABI of the hot/cold decode path: argument checks, scratch carving, launches.
 // Declarations and the reference function each entry replaces: include/hotcold_b200.h.
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
+#include <mutex>
 
 #include "hc_internal.cuh"
 
@@ -249,6 +254,42 @@ int hc_attend(const hc_layer* L, const void* q_post, const int64_t* cur_pos, int
                     "attend");
 }
 
+int hc_encode_kmap(void* out, const void* base, int dtype, int64_t rows, int D, int box_rows) {
+  if (!out || !base) return fail(HC_ERR_ARG, "NULL argument");
+  if (rows <= 0 || (D != 64 && D != 128) || box_rows < 1 || box_rows > 256)
+    return fail(HC_ERR_ARG, "rows %lld, D %d, box_rows %d out of range", (long long)rows, D, box_rows);
+  if (dtype != HC_F16 && dtype != HC_BF16) return fail(HC_ERR_UNSUPPORTED, "tensor maps serve 16-bit K only");
+  if (reinterpret_cast<uintptr_t>(base) % 16) return fail(HC_ERR_ARG, "base must be 16-byte aligned");
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!encode) {
+      cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+      void* fn = nullptr;
+      const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        (void)cudaGetLastError();
+        return fail(HC_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available");
+      }
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = encode(&m, dtype == HC_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
+  std::memcpy(out, &m, sizeof(m));
+  return HC_OK;
+}
+
 int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const void* k_pre, const void* v,
             int64_t kv_stride_seq, const void* cos, const void* sin, const int64_t* pos, int use_held, void* out,
             int overflow_nan, void* stream) {
@@ -260,6 +301,7 @@ int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const vo
   const size_t smem = hc::step_smem_bytes(*L, use_held);
   if (smem == 0 || smem > 227 * 1024)
     return fail(HC_ERR_UNSUPPORTED, "fused step needs %zu bytes of shared memory per CTA", smem);
+  if (L->dtype != HC_F32 && !L->kmaps) return fail(HC_ERR_UNSUPPORTED, "16-bit fused step needs hc_layer.kmaps");
   const cudaError_t e = hc::launch_step(*L, q_pre, q_stride_seq, k_pre, v, kv_stride_seq, cos, sin, pos, use_held, out,
                                         overflow_nan, reinterpret_cast<cudaStream_t>(stream));
   if (e == cudaErrorNotSupported) {

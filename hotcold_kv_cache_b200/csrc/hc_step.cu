@@ -5,21 +5,26 @@
 // (patch.py:161-305 with cache.py:130-151 and cache.py:37-128). Split into separate kernels
 // (hc_append, hc_compress, hc_attend) the step pays a launch and a global round trip per
 // stage; at batch 1 that latency, not HBM bandwidth, sets the time. Here CTA (h, p) of the
-// cluster owns KV head h and part p of P = 16/Hk parts:
-//   1. it gathers (cp.async, 16-byte chunks) the K rows of its 1/P of the token list
-//      [held | hot | new] and the V columns p*D/P .. (p+1)*D/P of every token, RoPEs the new
-//      token's query heads of its group (and, if the new token is its own, the key), and scores
-//      its tokens on the tensor cores: one m16n8k16 MMA tile row per query head plus a row
-//      for the GQA-mean query, whose product is the eviction logit;
-//   2. attention logits go to the other CTAs of head h and eviction logits to every CTA
-//      through distributed shared memory (cluster barrier 1);
-//   3. every CTA applies the policy to all hot tokens (hot/cold sum, or SnapKV softmax +
-//      pooling + head mean), ranks the tokens of its own 32-token words against the whole
-//      prefix (exact top-k, ties to the lower index) and publishes their eviction bits and
-//      counts (cluster barrier 2); there is no leader CTA on the critical path;
-//   4. every CTA masks the evicted tokens, takes the softmax over all tokens of head h and
-//      writes its D/P output columns; the owners of each word compact the logical order,
-//      push freed slots and copy evicted payloads into the cold ring with their index vectors.
+// cluster owns KV head h and part p of P = 16/Hk parts of head h's rows in PHYSICAL order,
+// [held rows 0..r_max) ++ [slab slots 0..cap): order does not matter to attention, and
+// physical order makes each part contiguous in HBM.
+//   1. Right after the dependency wait one thread starts TMA bulk copies of the part's K and
+//      V rows (at most two copies each); meanwhile the CTA reads the counters, maps its slots
+//      to logical indices (free slots stay unmapped and are masked), and RoPEs the new token's
+//      query heads of its group and, if the new slot is its own, the new key.
+//   2. Scoring on the CUDA cores (packed f32x2 FMAs, 8 lanes per row): G attention logits
+//      and the eviction logit (GQA-mean query . k) per row. Eviction logits go, by logical
+//      index, to every CTA of head h through distributed shared memory (cluster barrier 1).
+//   3. Policy: the SnapKV softmax and pooling (or the raw hot/cold logit) of head h are
+//      computed by the CTAs of that head, each for its share of the prefix, and sent to the
+//      CTA owning the token's 32-token word (barrier 2). Owners take the mean over heads. A
+//      single evicted token (the steady state) is the minimum over the owners' candidates
+//      (barrier 3); more evictions rank every owned token against all prefix keys (barriers
+//      3 and 4). Exact top-k with ties to the lower index; no CTA works alone.
+//   4. Each CTA masks evicted rows, computes its flash-decode partial (max, sum, P.V) and
+//      sends each column block to the CTA of head h that finalizes it (last barrier). Owners of
+//      words compact the logical order, push freed slots and copy evicted payloads into the
+//      cold ring with their index vectors; the last CTA pushes the query pool.
 // The result equals hc_append + hc_compress + hc_attend on the same state.
 
 #include <cooperative_groups.h>
@@ -36,23 +41,25 @@ constexpr int kStepMaxCluster = 16;
 
 // Sizes shared by the host and the kernel.
 struct StepGeom {
-  int P;     // parts per KV head; cluster = Hk * P = 16
-  int tpc;   // scored rows per CTA (multiple of 8)
-  int tmax;  // tokens of [held | hot] at most (multiple of 8)
-  int s_cap; // hot tokens at most
-  int wpc;   // 32-token words a CTA owns at most
-  int dpc;   // V columns per CTA
+  int P;      // parts per KV head; cluster = Hk * P = 16
+  int chunk;  // physical rows per CTA (multiple of 8)
+  int krows;  // rows of the K area: with tensor-core scoring, whole 128-row tiles and the slack of
+              // the last 64-row TMA box
+  int r8;     // held rows in the physical order, a multiple of 8 (rows past r_max are masked)
+  int s_cap;  // hot tokens at most
+  int wpc;    // 32-token words a CTA owns at most
 };
 
-__host__ __device__ inline StepGeom step_geom(int Hk, int D, int max_cap, int max_r, int use_held) {
+__host__ __device__ inline StepGeom step_geom(int Hk, int max_cap, int max_r, int use_held, bool mma) {
   StepGeom g{};
   g.P = (Hk >= 1 && Hk <= kStepMaxCluster && kStepMaxCluster % Hk == 0) ? kStepMaxCluster / Hk : 0;
   if (!g.P) return g;
   g.s_cap = max_cap;
-  g.tmax = ((use_held ? max_r : 0) + max_cap + 7) & ~7;
-  g.tpc = (((g.tmax + g.P - 1) / g.P) + 7) & ~7;
+  g.r8 = use_held ? (max_r + 7) & ~7 : 0;
+  const int rows = g.r8 + max_cap;
+  g.chunk = (((rows + g.P - 1) / g.P) + 7) & ~7;
+  g.krows = mma ? ((g.chunk + 64 + 127) & ~127) : g.chunk;
   g.wpc = ((max_cap + 31) / 32 + kStepMaxCluster - 1) / kStepMaxCluster;
-  g.dpc = D / g.P;
   return g;
 }
 
@@ -72,38 +79,48 @@ struct StepArgs {
 };
 
 struct StepSmem {
-  size_t k, v, qh, q, a, ord, fre, held, e, pool, key, red, best, mask, cnt, word, flag, evl, misc, total;
+  size_t k, qb, v, q, knew, a, inv, ord, fre, held, e, pool, key, red, best, mask, cnt, word, flag, evl, o, ml, qp,
+      misc, tmem, bars, total;
 };
 
 __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
 
-__host__ __device__ inline StepSmem step_smem(int D, int esz, int G, int Hk, const StepGeom& g) {
+__host__ __device__ inline StepSmem step_smem(int D, int esz, int G, int Hk, int max_r, const StepGeom& g) {
   StepSmem m{};
   size_t o = 0;
   auto take = [&](size_t b) { size_t r = o; o += al16(b); return r; };
-  // K rows of this CTA's tokens; after scoring the same area holds the P.V partial sums
-  const size_t kb = (size_t)g.tpc * D * esz;
-  const size_t rb = (size_t)kStepWarps * G * (g.dpc + 1) * 4;
+  // K rows of this CTA's part (16-bit: D/64 planes of 128-byte swizzled rows, 1024-aligned);
+  // after scoring the same area holds the P.V partial sums
+  const size_t kb = (size_t)g.krows * D * esz;
+  const size_t rb = (size_t)kStepWarps * G * D * 4;
   m.k = take(kb > rb ? kb : rb);
-  m.v = take((size_t)g.tmax * g.dpc * esz);
-  m.qh = take((size_t)16 * (D + 8) * esz);   // MMA query operand: G heads, the mean, zero rows
-  m.q = take((size_t)(G + 1) * D * 4);
-  m.a = take((size_t)G * g.tmax * 4);        // attention logits, then probabilities
+  o = (o + 1023) & ~size_t(1023);
+  m.qb = take((size_t)16 * D * esz);  // MMA query operand: G heads, the mean, zero rows (N = 16)
+  m.v = take((size_t)g.chunk * D * esz);
+  m.q = take((size_t)(G + 1) * D * 4);       // RoPE'd query heads and their GQA mean
+  m.knew = take((size_t)D * esz);            // the new key after RoPE
+  m.a = take((size_t)G * g.chunk * 4);       // attention logits, then probabilities
+  m.inv = take((size_t)g.chunk * 4);         // logical index of each row, -1 when not attended
   m.ord = take((size_t)g.s_cap * 4);         // logical order (physical slot per logical index)
   m.fre = take((size_t)g.s_cap * 4);         // free-slot stack
-  m.held = take((size_t)g.tmax * 4);         // held rows attended this step
-  m.e = take((size_t)g.tmax * 4);            // eviction logits of head h, by token index
+  m.held = take((size_t)(max_r > 0 ? max_r : 1) * 4);  // held rows attended this step
+  m.e = take((size_t)g.s_cap * 4);           // eviction logits of head h, by logical index
   m.pool = take((size_t)Hk * g.wpc * 32 * 4);  // per-head policy values of the tokens this CTA owns
   m.key = take((size_t)g.s_cap * 4);         // policy score keys, by logical index
   m.red = take((size_t)(4 * kStepMaxCluster + 4 * kStepWarps) * 8);
-  m.best = take((size_t)kStepMaxCluster * 8);
+  m.best = take((size_t)kStepMaxCluster * g.wpc * 8);
   m.mask = take((size_t)((g.s_cap + 31) / 32) * 4);
   m.cnt = take((size_t)2 * kStepMaxCluster * 4);
   m.word = take((size_t)g.wpc * 4);
   m.flag = take((size_t)g.wpc * 32 * 4);
   m.evl = take((size_t)3 * g.wpc * 32 * 4);
+  m.o = take((size_t)G * D * 4);             // partials of this CTA's column block from every part
+  m.ml = take((size_t)2 * G * kStepMaxCluster * 4);
+  m.qp = take((size_t)G * Hk * D * esz);  // the new token's pre-RoPE query rows (query-pool push)
   m.misc = take(64);
-  m.total = o;
+  m.tmem = take(16);
+  m.bars = take(32);
+  m.total = o + 1024;  // room to align the dynamic shared memory base to 1024 bytes
   return m;
 }
 
@@ -172,6 +189,56 @@ __device__ void step_evict_one(const hc_layer& L, const hc_seq_desc& d, int slot
   for (int f = D + lane; f < L.F; f += 32) vec[f] = 0.f;
 }
 
+// Index vector and position of one evicted token (controller.py:178-182, 200-212): mean over
+// heads of the pre-RoPE key, L2-normalised, zero-padded to F; one warp.
+template <int DT, int D>
+__device__ void step_evict_vec(const hc_layer& L, const hc_seq_desc& d, int slot, int dst, int64_t posv) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  constexpr int PER = (D + 31) / 32;
+  const int lane = threadIdx.x & 31;
+  float mean[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) mean[i] = 0.f;
+  for (int h0 = 0; h0 < L.Hk; h0 += 8) {
+    const int nh = min(8, L.Hk - h0);
+    T kr[8][PER];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= nh) break;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int dd = lane + 32 * i;
+        if (dd < D) kr[j][i] = reinterpret_cast<const T*>(d.hot_kpre)[((size_t)(h0 + j) * d.cap + slot) * D + dd];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= nh) break;
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        if (lane + 32 * i < D) mean[i] += E::to_f(kr[j][i]);
+    }
+  }
+  if (lane == 0) d.cold_pos[dst] = posv;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    mean[i] = mean[i] / (float)L.Hk;
+    const int dd = lane + 32 * i;
+    if (dd < D && dd < L.F) ss += mean[i] * mean[i];
+  }
+  ss = warp_sum(ss);
+  const float den = fmaxf(sqrtf(ss), 1e-12f);
+  float* vec = d.cold_vec + (size_t)dst * L.F;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int dd = lane + 32 * i;
+    if (dd < D && dd < L.F) vec[dd] = L.normalize ? mean[i] / den : mean[i];
+  }
+  for (int f = D + lane; f < L.F; f += 32) vec[f] = 0.f;
+}
+
 __device__ __forceinline__ Plan step_plan(const hc_layer& L, int budget, int S) {
   Plan p{S, 0, 0, 0, 0};
   if (S <= budget) return p;
@@ -193,12 +260,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int ESZ = sizeof(T);
-  constexpr int KCH = D * ESZ / 16;  // 16-byte chunks per K row; chunk c of row i sits at c ^ (i & 7)
-  constexpr int VE = 16 / ESZ;       // elements per chunk
-  constexpr int QSTR = D + 8;        // padded row of the MMA query operand (no bank conflicts)
+  constexpr int ROWB = D * ESZ;
+  constexpr int KCH = ROWB / 16;  // 16-byte chunks per row
+  constexpr int VE = 16 / ESZ;    // elements per chunk
+  constexpr int CPL = KCH / 8;    // chunks per lane when 8 lanes share a row
+  constexpr int EPL = CPL * VE;   // elements per lane
   constexpr int H = D / 2;
   constexpr int RP = ((G + 1) * H + kStepThreads - 1) / kStepThreads;  // RoPE pairs per thread
-  static_assert(KCH >= 8, "the chunk swizzle needs rows of at least 128 bytes");
+  constexpr bool QREG = (G + 1) * EPL <= 80;  // query rows kept in registers while scoring (fp32)
+  constexpr bool MMA = DT != HC_F32;          // 16-bit: tcgen05 scoring on TMA-loaded, swizzled K
+  constexpr int N8 = 16;                      // MMA N (M = 128 takes N in steps of 16): heads + mean, padded
+  constexpr int NL = ((G + 1 + 7) / 8) * 8;   // accumulator columns read back
+  constexpr int PL = D / 64;                  // 128-byte planes of a K row
+  static_assert(KCH % 8 == 0, "rows must be a multiple of 128 bytes");
+  static_assert(G + 1 <= 16, "query heads per KV head");
   cg::cluster_group cluster = cg::this_cluster();
   const hc_layer& L = a.L;
   const StepGeom& gm = a.g;
@@ -207,37 +282,118 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const int h = rank / P, p = rank % P;
   const int s = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int tmax = gm.tmax, dpc = gm.dpc;
+  const int chunk = gm.chunk;
 
   // arrival: this CTA has started; waited on before the first distributed shared memory store
   cluster_arrive_relaxed();
 
-  extern __shared__ __align__(128) unsigned char smem[];
-  const StepSmem M = step_smem(D, ESZ, G, L.Hk, gm);
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const StepSmem M = step_smem(D, ESZ, G, L.Hk, L.max_r, gm);
   T* sK = reinterpret_cast<T*>(smem + M.k);
+  T* sQb = reinterpret_cast<T*>(smem + M.qb);
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(smem + M.tmem);
   T* sV = reinterpret_cast<T*>(smem + M.v);
-  T* sQh = reinterpret_cast<T*>(smem + M.qh);
   float* sQ = reinterpret_cast<float*>(smem + M.q);
+  T* sKnew = reinterpret_cast<T*>(smem + M.knew);
   float* sA = reinterpret_cast<float*>(smem + M.a);
+  int* sInv = reinterpret_cast<int*>(smem + M.inv);
   int* sOrd = reinterpret_cast<int*>(smem + M.ord);
   int* sFree = reinterpret_cast<int*>(smem + M.fre);
   int* sHeld = reinterpret_cast<int*>(smem + M.held);
   float* sE = reinterpret_cast<float*>(smem + M.e);
   float* sPool = reinterpret_cast<float*>(smem + M.pool);
-  unsigned long long* sBest = reinterpret_cast<unsigned long long*>(smem + M.best);
   uint32_t* sKey = reinterpret_cast<uint32_t*>(smem + M.key);
   float* sRed = reinterpret_cast<float*>(smem + M.red);  // per-warp partials and per-head statistics
-  unsigned long long* sRed64 = reinterpret_cast<unsigned long long*>(smem + M.red);
+  unsigned long long* sBest = reinterpret_cast<unsigned long long*>(smem + M.best);
   uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + M.mask);
   int* sCnt = reinterpret_cast<int*>(smem + M.cnt);
   uint32_t* sWord = reinterpret_cast<uint32_t*>(smem + M.word);
   int* sFlag = reinterpret_cast<int*>(smem + M.flag);
   int* sEvl = reinterpret_cast<int*>(smem + M.evl);
+  float* sO = reinterpret_cast<float*>(smem + M.o);
+  float* sML = reinterpret_cast<float*>(smem + M.ml);
   int* sMisc = reinterpret_cast<int*>(smem + M.misc);
+  T* sQP = reinterpret_cast<T*>(smem + M.qp);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + M.bars);
 
   // the descriptor is written once when the layer is set up, so it is read before the wait
   const hc_seq_desc d = L.desc[s];
+  // this part's rows: physical index u in [held rows 0..R) ++ [slots 0..cap)
+  const int R = a.use_held ? gm.r8 : 0;  // held rows, padded to 8; rows past r_max are masked
+  const int Un = R + d.cap;
+  const int u0 = min(p * chunk, Un), u1 = min(u0 + chunk, Un), nrows = u1 - u0;
+  const int hb = u0, nh = max(0, min(u1, R) - hb);          // held rows [hb, hb + nh), nh % 8 == 0
+  const int nhr = max(0, min(hb + nh, d.r_max) - hb);       // of which real held rows
+  const int sb = max(u0, R) - R, ns = max(0, u1 - max(u0, R));  // slots [sb, sb + ns)
+  // L2 prefetch of the step's state and of this part's rows while the preceding kernel still
+  // runs. A prefetch only warms L2, so it is safe before the dependency wait even for lines
+  // that kernel writes.
+  {
+    const int nl_ord = (d.cap * 4 + 127) / 128, nl_pos = (d.r_max * 8 + 127) / 128;
+    if (tid == 0) {
+      prefetch_l2(d.st);
+      if (d.held_valid) prefetch_l2(d.held_valid);
+      if (nhr > 0) {
+        const size_t off = ((size_t)h * d.r_max + hb) * ROWB;
+        bulk_prefetch_l2(reinterpret_cast<const char*>(d.held_k) + off, (uint32_t)(nhr * ROWB));
+        bulk_prefetch_l2(reinterpret_cast<const char*>(d.held_v) + off, (uint32_t)(nhr * ROWB));
+      }
+      if (ns > 0) {
+        const size_t off = ((size_t)h * d.cap + sb) * ROWB;
+        bulk_prefetch_l2(reinterpret_cast<const char*>(d.hot_k) + off, (uint32_t)(ns * ROWB));
+        bulk_prefetch_l2(reinterpret_cast<const char*>(d.hot_v) + off, (uint32_t)(ns * ROWB));
+      }
+    } else if (tid <= nl_ord) {
+      prefetch_l2(reinterpret_cast<const char*>(d.hot_ord) + (size_t)(tid - 1) * 128);
+      prefetch_l2(reinterpret_cast<const char*>(d.hot_free) + (size_t)(tid - 1) * 128);
+    } else if (a.use_held && d.held_pos && tid <= nl_ord + nl_pos) {
+      prefetch_l2(reinterpret_cast<const char*>(d.held_pos) + (size_t)(tid - 1 - nl_ord) * 128);
+    }
+  }
   pdl_wait();
+
+  // ---- this part's K rows (TMA tensor boxes into the swizzled MMA layout for 16-bit types,
+  //      else bulk copies) and V rows (bulk copies, at most two); lanes of warp 0 issue them ----
+  if (warp == 0) {
+    const uint32_t vbytes = (uint32_t)((nhr + ns) * ROWB);
+    const int nhb = nh >> 3, nsb = (ns + 63) >> 6;  // 8-row held boxes, 64-row slot boxes
+    if (lane == 0) {
+      mbar_init(&bars[0], 1);
+      mbar_init(&bars[1], 1);
+      mbar_init(&bars[2], 1);
+      fence_mbar_init();
+      if constexpr (MMA) mbar_arrive_expect_tx(&bars[0], (uint32_t)((nh + 64 * nsb) * 128 * PL));
+      else mbar_arrive_expect_tx(&bars[0], vbytes);
+      mbar_arrive_expect_tx(&bars[1], vbytes);
+    }
+    __syncwarp();
+    if constexpr (MMA) {
+      const char* kmaps = reinterpret_cast<const char*>(L.kmaps);
+      const int y_held = (s * L.Hk + h) * d.r_max + hb;
+      const int y_hot = (s * L.Hk) * L.max_cap + h * d.cap + sb;
+      const int nb = nhb + nsb;
+      for (int b = lane; b < nb * PL; b += 32) {
+        const int pl = b / nb, j = b - pl * nb;
+        unsigned char* plane = reinterpret_cast<unsigned char*>(sK) + (size_t)pl * gm.krows * 128;
+        if (j < nhb) tma_load_2d(plane + (size_t)j * 8 * 128, kmaps + 128, pl * 64, y_held + 8 * j, &bars[0]);
+        else tma_load_2d(plane + (size_t)(nh + 64 * (j - nhb)) * 128, kmaps, pl * 64, y_hot + 64 * (j - nhb), &bars[0]);
+      }
+    } else {
+      if (lane == 1 && nhr > 0)
+        bulk_g2s(sK, reinterpret_cast<const T*>(d.held_k) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
+                 &bars[0]);
+      if (lane == 2 && ns > 0)
+        bulk_g2s(sK + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + sb) * D,
+                 (uint32_t)(ns * ROWB), &bars[0]);
+    }
+    if (lane == 3 && nhr > 0)
+      bulk_g2s(sV, reinterpret_cast<const T*>(d.held_v) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
+               &bars[1]);
+    if (lane == 4 && ns > 0)
+      bulk_g2s(sV + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_v) + ((size_t)h * d.cap + sb) * D,
+               (uint32_t)(ns * ROWB), &bars[1]);
+  }
 
   // ---- one round trip: counters, logical order, free stack, held flags, new token inputs ----
   hc_seq_state* st = d.st;
@@ -269,7 +425,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       }
     }
   }
-  const T vnew = tid < dpc ? vp[p * dpc + tid] : E::from_f(0.f);
+  const T vnew = tid < D ? vp[tid] : E::from_f(0.f);
+  // the last CTA stages the query rows for the query-pool push
+  const bool qpush = rank == ncta - 1 && d.p_max > 0;
+  constexpr int kQP = 16;
+  T tq[kQP];
+  if (qpush)
+#pragma unroll
+    for (int j = 0; j < kQP; ++j)
+      if (tid + j * kStepThreads < L.Hq * D) tq[j] = qp[tid + j * kStepThreads];
   // all loads first, then the stores: one round trip for up to kPre entries per thread
   constexpr int kPre = 4;
   int ov[kPre], fv[kPre];
@@ -281,10 +445,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       fv[j] = d.hot_free[i];
     }
   }
-  const int t_h = tid;
-  const bool hv_ok = a.use_held && t_h < d.r_max;
-  const uint8_t hval = hv_ok ? d.held_valid[t_h] : 0;
-  const int64_t hpos = hv_ok ? d.held_pos[t_h] : 0;
+  const bool hv_ok = a.use_held && tid < d.r_max;
+  const uint8_t hval = hv_ok ? d.held_valid[tid] : 0;
+  const int64_t hpos = hv_ok ? d.held_pos[tid] : 0;
 #pragma unroll
   for (int j = 0; j < kPre; ++j) {
     const int i = tid + j * kStepThreads;
@@ -297,7 +460,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     sOrd[i] = d.hot_ord[i];
     sFree[i] = d.hot_free[i];
   }
-  if (hv_ok) sHeld[t_h] = hval != 0 && hpos <= cur_pos;
+  if (hv_ok) sHeld[tid] = hval != 0 && hpos <= cur_pos;
+  if (qpush) {
+#pragma unroll
+    for (int j = 0; j < kQP; ++j)
+      if (tid + j * kStepThreads < L.Hq * D) sQP[tid + j * kStepThreads] = tq[j];
+    for (int k = tid + kQP * kStepThreads; k < L.Hq * D; k += kStepThreads) sQP[k] = qp[k];
+  }
   if (a.use_held)
     for (int t = tid + kStepThreads; t < d.r_max; t += kStepThreads)
       sHeld[t] = d.held_valid[t] != 0 && d.held_pos[t] <= cur_pos;
@@ -306,90 +475,66 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     sMisc[3] = 0;
     sMisc[4] = 0;
   }
+  for (int i = tid; i < kStepMaxCluster * gm.wpc; i += kStepThreads) sBest[i] = ~0ull;
+  for (int i = tid; i < chunk; i += kStepThreads) sInv[i] = -1;
   __syncthreads();
 
   const int n_held = a.use_held ? max(0, min(held_len, d.r_max)) : 0;
   const int new_slot = (n_free > 0 && n_free <= cap) ? sFree[n_free - 1] : -1;
+
   const int S = n_hot + 1;  // hot tokens after the append (logical index n_hot is the new one)
-  const int T_all = n_held + S;
-  // every CTA reads the same counters (nothing writes them before barrier 1): a uniform exit
-  if (n_hot < 0 || S > cap || S > gm.s_cap || T_all > tmax || new_slot < 0 || new_slot >= cap) {
+  // every CTA reads the same counters (nothing writes them before the last barrier): a
+  // uniform exit, after this CTA's bulk copies have landed
+  if (n_hot < 0 || S > cap || S > gm.s_cap || new_slot < 0 || new_slot >= cap) {
     if (rank == 0 && tid == 0) set_status(st, HC_DEV_CAPACITY);
+    mbar_wait(&bars[0], 0);
+    mbar_wait(&bars[1], 0);
     cluster_wait();
     return;
   }
   const Plan pl = step_plan(L, d.budget, S);
   const int n_ev_plan = pl.active ? pl.prefix - pl.ntop : 0;
-  const int chunk = (((T_all + P - 1) / P) + 7) & ~7;
-  const int t0 = min(p * chunk, T_all);
-  int ntl = max(0, min(chunk, T_all - t0));
-  if (ntl > gm.tpc) {  // host sizing rules this out
-    if (tid == 0) set_status(st, HC_DEV_CAPACITY);
-    ntl = gm.tpc;
-  }
-  const int new_t = n_held + n_hot;
+  const bool policy = pl.active && n_ev_plan > 0;
   const int nwords = (S + 31) >> 5;
   // CTA r owns the 32-token words w with w * ncta / nwords == r
   const int w0 = (rank * nwords + ncta - 1) / ncta, w1 = ((rank + 1) * nwords + ncta - 1) / ncta;
   const int own0 = w0 * 32, own_n = max(0, min(w1 * 32, S) - own0), nw_own = w1 - w0;
   const int qwin_slot = d.p_max > 0 ? ((qwin_head % d.p_max) + d.p_max) % d.p_max : 0;
+  // query pool push: mean over all query heads of the pre-RoPE query (controller.py:240-241)
+  if (qpush && tid < D) {
+    float acc = 0.f;
+    for (int hh = 0; hh < L.Hq; ++hh) acc += E::to_f(sQP[hh * D + tid]);
+    reinterpret_cast<T*>(d.qwin)[(size_t)qwin_slot * D + tid] = E::from_f(acc / (float)L.Hq);
+  }
   auto phys_of = [&](int li) { return li < n_hot ? sOrd[li] : new_slot; };
+  auto row_of_slot = [&](int slot) { return (slot >= sb && slot < sb + ns) ? nh + slot - sb : -1; };
 
-  // ---- gathers: K rows of this CTA's tokens, V columns of every token ---------------------
-  // 8 lanes per row, so each warp-wide copy covers whole 128-byte lines of 4 rows
-  const T* hk = reinterpret_cast<const T*>(d.hot_k);
-  const T* hv = reinterpret_cast<const T*>(d.hot_v);
-  const T* gk = reinterpret_cast<const T*>(d.held_k);
-  const T* gv = reinterpret_cast<const T*>(d.held_v);
-  const int sub8 = tid & 7, rg = tid >> 3;
-  for (int i = rg; i < ntl; i += kStepThreads / 8) {
-    const int t = t0 + i;
-    if (t == new_t) continue;
-    const T* src = hk;
-    int nb = 16;
-    if (t < n_held) {
-      src = gk + ((size_t)h * d.r_max + t) * D;
-    } else {
-      const int slot = sOrd[t - n_held];
-      if (slot >= 0 && slot < cap) src = hk + ((size_t)h * cap + slot) * D;
-      else nb = 0;  // zero-filled; the token is masked
+  // ---- logical index of every own slot row; free slots stay -1 and are masked --------------
+  for (int li = tid; li < n_hot; li += kStepThreads) {
+    const int slot = sOrd[li];
+    if (slot < 0 || slot >= cap) {
+      set_status(st, HC_DEV_INDEX);
+      continue;
     }
-#pragma unroll
-    for (int j = 0; j < KCH / 8; ++j) {
-      const int c = j * 8 + sub8;
-      cp_async16(sK + (size_t)i * D + (size_t)((c ^ (i & 7)) * VE), nb ? src + c * VE : src, nb);
-    }
+    const int i = row_of_slot(slot);
+    if (i >= 0) sInv[i] = li;
   }
-  cp_async_commit();
-  const int vch = dpc / VE, vsh = __ffs(vch) - 1;
-  const int lpr = vch < 8 ? vch : 8, lsh = __ffs(lpr) - 1;  // lanes per V row
-  for (int k = tid; k < (T_all << lsh); k += kStepThreads) {
-    const int t = k >> lsh, l0 = k & (lpr - 1);
-    if (t == new_t) continue;
-    const T* src = hv;
-    int nb = 16;
-    if (t < n_held) {
-      src = gv + ((size_t)h * d.r_max + t) * D + p * dpc;
-    } else {
-      const int slot = sOrd[t - n_held];
-      if (slot >= 0 && slot < cap) src = hv + ((size_t)h * cap + slot) * D + p * dpc;
-      else nb = 0;
-    }
-    for (int c = l0; c < vch; c += lpr) cp_async16(sV + (size_t)t * dpc + c * VE, nb ? src + c * VE : src, nb);
-  }
-  cp_async_commit();
+  const int i_new = row_of_slot(new_slot);
+  if (tid == 0 && i_new >= 0) sInv[i_new] = n_hot;
 
-  // ---- RoPE of the new token (patch.py:161-162), while the gathers are in flight -----------
-  const int new_i = (new_t >= t0 && new_t < t0 + ntl) ? new_t - t0 : -1;
+  // ---- RoPE of the new token (patch.py:161-162) while the bulk copies are in flight --------
 #pragma unroll
   for (int j = 0; j < RP; ++j) {
     const int k = tid + j * kStepThreads;
     if (k >= (G + 1) * H) continue;
     const int g = k / H, i = k % H;
-    if (g == G && new_i < 0) continue;
+    if (g == G && i_new < 0) continue;
     float c0, s0, c1, s1;
     if (a.cos) {
-      c0 = rc[j][0]; c1 = rc[j][1]; s0 = rs[j][0]; s1 = rs[j][1];
+      c0 = rc[j][0];
+      c1 = rc[j][1];
+      s0 = rs[j][0];
+      s1 = rs[j][1];
     } else {
       rope_cs<DT>(rc[j][0], cur_pos, L.rope_scaling, c0, s0);
       c1 = c0;
@@ -401,13 +546,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     if (g < G) {
       sQ[g * D + i] = E::round(o0);
       sQ[g * D + i + H] = E::round(o1);
-      sQh[g * QSTR + i] = E::from_f(o0);
-      sQh[g * QSTR + i + H] = E::from_f(o1);
     } else {
       const T k0 = E::from_f(o0), k1 = E::from_f(o1);
-      sK[(size_t)new_i * D + (((i / VE) ^ (new_i & 7)) * VE) + i % VE] = k0;
-      sK[(size_t)new_i * D + ((((i + H) / VE) ^ (new_i & 7)) * VE) + (i + H) % VE] = k1;
-      // the owner of the new token writes its slab rows for head h (cache.py:145-148)
+      sKnew[i] = k0;
+      sKnew[i + H] = k1;
+      // the owner of the new slot writes its slab rows for head h (cache.py:145-148)
       const size_t off = ((size_t)h * cap + new_slot) * D + i;
       reinterpret_cast<T*>(d.hot_k)[off] = k0;
       reinterpret_cast<T*>(d.hot_k)[off + H] = k1;
@@ -415,147 +558,157 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       reinterpret_cast<T*>(d.hot_kpre)[off + H] = E::from_f(rx[j][1]);
     }
   }
-  if (new_i >= 0)
-    for (int i = tid; i < D; i += kStepThreads)
-      reinterpret_cast<T*>(d.hot_v)[((size_t)h * cap + new_slot) * D + i] = vp[i];
-  if (tid < dpc) sV[(size_t)new_t * dpc + tid] = vnew;
-  for (int i = tid; i < (15 - G) * QSTR; i += kStepThreads) sQh[(G + 1) * QSTR + i] = E::from_f(0.f);
+  if (i_new >= 0 && tid < D) reinterpret_cast<T*>(d.hot_v)[((size_t)h * cap + new_slot) * D + tid] = vnew;
   __syncthreads();
   // GQA-mean query of this KV head, rounded to the dtype (cache.py:60-64 / scoring.py:17-26)
   for (int dd = tid; dd < D; dd += kStepThreads) {
     float acc = 0.f;
 #pragma unroll
     for (int g = 0; g < G; ++g) acc += sQ[g * D + dd];
-    const float qb = E::round(acc / (float)G);
-    sQ[G * D + dd] = qb;
-    sQh[G * QSTR + dd] = E::from_f(qb);
+    sQ[G * D + dd] = E::round(acc / (float)G);
   }
-  cp_async_wait<1>();
+  // K rows landed: the new key replaces the stale copy of its slot
+  if (!__syncthreads_and(mbar_wait(&bars[0], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
+  if (i_new >= 0)
+    for (int i = tid; i < D; i += kStepThreads) {
+      if constexpr (MMA) {
+        // row i_new of plane i/64, 16-byte chunk swizzled by the row (the TMA's 128-byte pattern)
+        const int c = (i & 63) >> 3;
+        reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(sK) + (size_t)(i >> 6) * gm.krows * 128 +
+                             (size_t)i_new * 128 + ((c ^ (i_new & 7)) << 4))[i & 7] = sKnew[i];
+      } else {
+        sK[(size_t)i_new * D + i] = sKnew[i];
+      }
+    }
+  if constexpr (MMA) {
+    // B operand: N8 rows (query heads, their mean, zeros) x D, K-major, 128-byte swizzle
+    for (int k = tid; k < N8 * D; k += kStepThreads) {
+      const int n = k / D, i = k % D, c = (i & 63) >> 3;
+      reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(sQb) + (size_t)(i >> 6) * N8 * 128 + (size_t)n * 128 +
+                           ((c ^ (n & 7)) << 4))[i & 7] = E::from_f(n <= G ? sQ[n * D + i] : 0.f);
+    }
+    fence_proxy_async_smem();  // generic writes above are read by the tensor cores
+  }
   __syncthreads();
 
-  // ---- scoring: G attention logits + the eviction logit per token --------------------------
-  auto put = [&](int i, int g, float v) {
-    if (i >= ntl || g > G) return;
-    const int t = t0 + i;
-    if (g < G) {
-      bool valid = true;
-      if (t < n_held) {
-        valid = sHeld[t] != 0;
-      } else if (t != new_t) {
-        const int slot = sOrd[t - n_held];
-        valid = slot >= 0 && slot < cap;
-        if (!valid && g == 0) set_status(st, HC_DEV_INDEX);
-      }
-      sA[g * tmax + t] = valid ? v * L.scale : kNegInf;
+  // ---- scoring: G attention logits + the eviction logit (GQA-mean query . k) per row --------
+  cluster_wait();  // every CTA of the cluster has started
+  auto emit = [&](int i, const float* tot) {
+    const int u = u0 + i;
+    bool valid;
+    int li = -1;
+    if (u < R) {
+      valid = u < n_held && sHeld[u] != 0;
+      sInv[i] = valid ? -2 : -1;  // -2: an attended held row
     } else {
-      sE[t] = v;
+      li = sInv[i];
+      valid = li >= 0;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) sA[g * chunk + i] = valid ? tot[g] * L.scale : kNegInf;
+    if (policy && li >= 0) {
+      sE[li] = tot[G];
+      for (int pp = 0; pp < P; ++pp)
+        if (pp != p) cluster.map_shared_rank(sE, h * P + pp)[li] = tot[G];
     }
   };
-  if constexpr (DT != HC_F32) {
-    const int gid = lane >> 2, tig = lane & 3;
-    uint32_t af[D / 16][4];
+  if constexpr (MMA) {
+    // tcgen05: one thread issues, per 128-row tile, D/16 MMAs of 128 x N8 x 16 into TMEM; warps
+    // then read their lane quarter of each tile with tcgen05.ld
+    const int ntiles = (nrows + 127) >> 7;
+    const int need = gm.krows / 128 * N8;
+    const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : 256u;
+    if (warp == 0) tmem_alloc(sTmem, ncols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *sTmem;
+    if (tid == 0 && ntiles > 0) {
+      constexpr uint32_t fmt = DT == HC_BF16 ? 1u : 0u;
+      constexpr uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(N8 >> 3) << 17) |
+                                 ((uint32_t)(128 >> 4) << 24);
+      const uint32_t a0 = smem_u32(sK), b0 = smem_u32(sQb);
+      for (int mt = 0; mt < ntiles; ++mt)
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const int kk = ks * 16 + 2 * tig;
-      af[ks][0] = *reinterpret_cast<const uint32_t*>(sQh + gid * QSTR + kk);
-      af[ks][1] = *reinterpret_cast<const uint32_t*>(sQh + (gid + 8) * QSTR + kk);
-      af[ks][2] = *reinterpret_cast<const uint32_t*>(sQh + gid * QSTR + kk + 8);
-      af[ks][3] = *reinterpret_cast<const uint32_t*>(sQh + (gid + 8) * QSTR + kk + 8);
-    }
-    const int ntiles = (ntl + 7) >> 3;
-    const int mat = lane >> 3, r8 = lane & 7;
-    // two independent tiles per pass keep two MMA chains in flight
-    for (int nt = warp; nt < ntiles; nt += 2 * kStepWarps) {
-      const bool two = nt + kStepWarps < ntiles;  // warp-uniform
-      const T* row0 = sK + (size_t)(nt * 8 + r8) * D;
-      const T* row1 = sK + (size_t)((nt + kStepWarps) * 8 + r8) * D;
-      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kq = 0; kq < D / 32; ++kq) {
-        const int ch = ((kq * 4 + mat) ^ r8) * VE;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(row0 + ch, b0, b1, b2, b3);
-        mma16816<DT>(c0, af[2 * kq], b0, b1);
-        mma16816<DT>(c0, af[2 * kq + 1], b2, b3);
-        if (two) {
-          ldsm_x4(row1 + ch, b0, b1, b2, b3);
-          mma16816<DT>(c1, af[2 * kq], b0, b1);
-          mma16816<DT>(c1, af[2 * kq + 1], b2, b3);
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t pl = ks >> 2, kin = ks & 3;
+          const uint32_t aa = a0 + pl * (uint32_t)gm.krows * 128u + (uint32_t)mt * 128u * 128u + kin * 32u;
+          const uint32_t bb = b0 + pl * (uint32_t)N8 * 128u + kin * 32u;
+          umma_f16(tbase + (uint32_t)(mt * N8), umma_desc_k_sw128(aa), umma_desc_k_sw128(bb), idesc, ks > 0);
         }
-      }
-      const int n0 = nt * 8 + 2 * tig;
-      put(n0, gid, c0[0]);
-      put(n0 + 1, gid, c0[1]);
-      put(n0, gid + 8, c0[2]);
-      put(n0 + 1, gid + 8, c0[3]);
-      if (two) {
-        const int n1 = n0 + kStepWarps * 8;
-        put(n1, gid, c1[0]);
-        put(n1 + 1, gid, c1[1]);
-        put(n1, gid + 8, c1[2]);
-        put(n1 + 1, gid + 8, c1[3]);
-      }
+      umma_commit(&bars[2]);
     }
-  } else {
-    const int sub = lane & 7, tk = lane >> 3;
-    for (int base = warp * 4; base < ntl; base += 4 * kStepWarps) {
-      const int i = base + tk;
-      float acc[G + 1];
+    if (ntiles > 0 && !__syncthreads_and(mbar_wait(&bars[2], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
+    tc_fence_after();
+    const int mt = warp >> 2, q4 = warp & 3;
+    if (mt < ntiles) {
+      float v[NL];
 #pragma unroll
-      for (int g = 0; g <= G; ++g) acc[g] = 0.f;
-      if (i < ntl) {
+      for (int c = 0; c < NL; c += 8) tmem_ld_x8(tbase + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mt * N8 + c), v + c);
+      const int i = mt * 128 + q4 * 32 + lane;
+      if (i < nrows) emit(i, v);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tbase, ncols);
+  } else
+  {
+    const int sub = lane & 7, tk = lane >> 3;
+    float2 qr[QREG ? G + 1 : 1][QREG ? EPL / 2 : 1];
+    if constexpr (QREG) {
+#pragma unroll
+      for (int g = 0; g <= G; ++g)
+#pragma unroll
+        for (int j = 0; j < CPL; ++j)
+#pragma unroll
+          for (int e = 0; e < VE / 2; ++e) {
+            const int dd = (j * 8 + sub) * VE + 2 * e;
+            qr[g][j * (VE / 2) + e] = make_float2(sQ[g * D + dd], sQ[g * D + dd + 1]);
+          }
+    }
+    for (int base = warp * 4; base < nrows; base += 4 * kStepWarps) {
+      const int i = base + tk;
+      float2 acc[G + 1];
+#pragma unroll
+      for (int g = 0; g <= G; ++g) acc[g] = make_float2(0.f, 0.f);
+      if (i < nrows) {
         const T* row = sK + (size_t)i * D;
 #pragma unroll
-        for (int j = 0; j < KCH / 8; ++j) {
+        for (int j = 0; j < CPL; ++j) {
           const int c = j * 8 + sub;
-          const float4 kv = *reinterpret_cast<const float4*>(row + ((c ^ (i & 7)) * VE));
+          float kf[VE];
+          unpack16<DT>(*reinterpret_cast<const uint4*>(row + c * VE), kf);
 #pragma unroll
-          for (int g = 0; g <= G; ++g) {
-            const float4 q = *reinterpret_cast<const float4*>(sQ + g * D + c * VE);
-            acc[g] = fmaf(q.x, kv.x, acc[g]);
-            acc[g] = fmaf(q.y, kv.y, acc[g]);
-            acc[g] = fmaf(q.z, kv.z, acc[g]);
-            acc[g] = fmaf(q.w, kv.w, acc[g]);
-          }
+          for (int g = 0; g <= G; ++g)
+#pragma unroll
+            for (int e = 0; e < VE / 2; ++e) {
+              float2 q2;
+              if constexpr (QREG) q2 = qr[g][j * (VE / 2) + e];
+              else q2 = *reinterpret_cast<const float2*>(sQ + g * D + c * VE + 2 * e);
+              acc[g] = __ffma2_rn(q2, make_float2(kf[2 * e], kf[2 * e + 1]), acc[g]);
+            }
         }
       }
+      float tot[G + 1];
 #pragma unroll
       for (int g = 0; g <= G; ++g) {
-        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 4);
-        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 2);
-        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
+        tot[g] = acc[g].x + acc[g].y;
+        tot[g] += __shfl_xor_sync(0xffffffffu, tot[g], 4);
+        tot[g] += __shfl_xor_sync(0xffffffffu, tot[g], 2);
+        tot[g] += __shfl_xor_sync(0xffffffffu, tot[g], 1);
       }
-      if (sub == 0)
-#pragma unroll
-        for (int g = 0; g <= G; ++g) put(i, g, acc[g]);
+      if (sub == 0 && i < nrows) emit(i, tot);
     }
   }
-  __syncthreads();
-
-  // ---- exchange within head h: attention logits and the eviction row ------------------------
-  // Rows are copied as 16-byte vectors: t0 and tmax are multiples of 8, and the up to 3
-  // floats past this CTA's tokens land on positions no CTA owns.
-  const bool policy = pl.active && n_ev_plan > 0;
-  cluster_wait();  // every CTA of the cluster has started
-  const int n4 = (ntl + 3) >> 2;
-  if (P > 1 && n4 > 0) {
-    const int rows = G + (policy ? 1 : 0);
-    const int n = rows * n4;
-    for (int k = tid; k < (P - 1) * n; k += kStepThreads) {
-      const int j = k / n, r = k - j * n, g = r / n4, i = r - g * n4;
-      float* base = g < G ? sA + (size_t)g * tmax : sE;
-      const size_t idx = (size_t)t0 + 4 * i;
-      *reinterpret_cast<float4*>(cluster.map_shared_rank(base, h * P + (j < p ? j : j + 1)) + idx) =
-          *reinterpret_cast<const float4*>(base + idx);
-    }
-  }
-  cluster.sync();
+  if (policy) cluster.sync();  // every CTA of head h holds the full eviction row
+  else __syncthreads();
 
   // ---- policy: per-head values pooled by the CTAs of each head, summed by token owners ------
   int n_ev = 0;
+  int ev_slot = -1, ev_dst = -1, ev_li = -1;  // the single evicted token, when exactly one leaves
   if (policy) {
     const int wpc32 = gm.wpc * 32;
-    float* x = sE + n_held;  // eviction logit of logical index li of head h
+    float* x = sE;  // eviction logit of logical index li of head h
     const int pb = p * pl.prefix / P, pe = (p + 1) * pl.prefix / P;  // this CTA's share of the prefix
     auto send = [&](int li, float v) {
       const int w = li >> 5;
@@ -632,39 +785,50 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     }
     n_ev = n_ev_plan;
     if (n_ev == 1) {
-      // one token leaves: the lowest key, equal keys evict the higher index
+      // one token leaves: the lowest key, equal keys evict the higher index. Each warp holding
+      // own tokens sends its candidate to every CTA; unused entries keep their initial maximum.
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
         best = y < best ? y : best;
       }
-      if (lane == 0) sRed64[warp] = best;
-      __syncthreads();
-      if (tid < ncta) {
-        unsigned long long b = sRed64[0];
-#pragma unroll
-        for (int w = 1; w < kStepWarps; ++w) b = sRed64[w] < b ? sRed64[w] : b;
-        cluster.map_shared_rank(sBest, tid)[rank] = b;
-      }
+      if (warp * 32 < own_n && warp < gm.wpc && lane < ncta)
+        cluster.map_shared_rank(sBest, lane)[rank * gm.wpc + warp] = best;
       cluster.sync();
-      best = sBest[0];
-      for (int r2 = 1; r2 < ncta; ++r2) best = sBest[r2] < best ? sBest[r2] : best;
+      // every warp reduces the candidates itself (a shuffle tree, no further barrier)
+      best = ~0ull;
+      for (int r2 = lane; r2 < ncta * gm.wpc; r2 += 32) best = sBest[r2] < best ? sBest[r2] : best;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
+        best = y < best ? y : best;
+      }
       const int li_ev = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
+      ev_slot = phys_of(li_ev);
+      ev_li = li_ev;
+      ev_dst = cold_head + cold_count;  // cold_head < ccap and cold_count <= ccap
+      if (ev_dst >= d.ccap) ev_dst -= d.ccap;
+      if (d.ccap <= 0) ev_dst = -1;
+      // warm L2 for the copies into the cold ring done at the end of the kernel
+      if (ev_slot >= 0 && ev_slot < cap) {
+        constexpr int LPR = ROWB / 128;  // 128-byte lines per row
+        if (p == 0 && tid < 2 * LPR) {
+          const char* src = reinterpret_cast<const char*>(tid & 1 ? d.hot_v : d.hot_kpre);
+          prefetch_l2(src + ((size_t)h * cap + ev_slot) * ROWB + (tid >> 1) * 128);
+        }
+        if (rank == ncta - 1 && tid < L.Hk * LPR)
+          prefetch_l2(reinterpret_cast<const char*>(d.hot_kpre) + ((size_t)(tid / LPR) * cap + ev_slot) * ROWB +
+                      (tid % LPR) * 128);
+      }
       // compaction of own words: entries after li_ev move down by one
       for (int i = tid; i < own_n; i += kStepThreads) {
         const int li = own0 + i;
         const int ph = phys_of(li);
-        if (li > li_ev) {
-          d.hot_ord[li - 1] = ph;
-        } else if (li == li_ev) {
-          if (n_free - 1 < cap) d.hot_free[n_free - 1] = ph;
-          sEvl[0] = ph;
-          sEvl[1] = d.ccap > 0 ? (int)(((long)cold_head + cold_count) % d.ccap) : -1;
-          sEvl[2] = li;
-          sMisc[4] = 1;
-        }
+        if (li > li_ev) d.hot_ord[li - 1] = ph;
+        else if (li == li_ev && n_free - 1 < cap) d.hot_free[n_free - 1] = ph;
       }
-      if (tid < G) sA[tid * tmax + n_held + li_ev] = kNegInf;
+      const int i_ev = row_of_slot(phys_of(li_ev));
+      if (i_ev >= 0 && tid < G) sA[tid * chunk + i_ev] = kNegInf;
       __syncthreads();
     } else {
       // keys of own tokens to every CTA, then the rank of each own token among the prefix
@@ -748,21 +912,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         }
         if (lane == 0) sMisc[4] = nloc;
       }
-      for (int li = tid; li < S; li += kStepThreads)
-        if ((sMask[li >> 5] >> (li & 31)) & 1u)
+      for (int i = tid; i < nrows; i += kStepThreads) {
+        const int li = sInv[i];
+        if (li >= 0 && ((sMask[li >> 5] >> (li & 31)) & 1u))
 #pragma unroll
-          for (int g = 0; g < G; ++g) sA[g * tmax + n_held + li] = kNegInf;
+          for (int g = 0; g < G; ++g) sA[g * chunk + i] = kNegInf;
+      }
       __syncthreads();
     }
   }
 
-  // ---- softmax over every token of head h, P.V for this CTA's columns ----------------------
-  float* sPm = sRed + 4 * kStepMaxCluster;
+  // ---- flash-decode partial over this part's rows -------------------------------------------
+  float* sPm = sRed + 4 * kStepMaxCluster;              // per-warp maxima
+  float* sLw = sRed + 4 * kStepMaxCluster + kStepWarps;  // per-warp probability sums [warp][g]
   {
     constexpr int WPG = kStepWarps / G;
     const int g = warp % G, sl = warp / G;
     float m = kNegInf;
-    for (int t = sl * 32 + lane; t < T_all; t += WPG * 32) m = fmaxf(m, sA[g * tmax + t]);
+    for (int i = sl * 32 + lane; i < nrows; i += WPG * 32) m = fmaxf(m, sA[g * chunk + i]);
     m = warp_max(m);
     if (lane == 0) sPm[warp] = m;
   }
@@ -771,71 +938,106 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     float m = kNegInf;
+#pragma unroll
     for (int sl = 0; sl < kStepWarps / G; ++sl) m = fmaxf(m, sPm[sl * G + g]);
     mg[g] = m;
   }
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-    for (int t = tid; t < T_all; t += kStepThreads) {
-      const float x = sA[g * tmax + t];
-      sA[g * tmax + t] = (x == kNegInf) ? 0.f : __expf(x - mg[g]);
-    }
-  cp_async_wait<0>();
-  __syncthreads();
-  float* red = reinterpret_cast<float*>(smem + M.k);  // the K rows are no longer needed
-  float* redl = red + (size_t)kStepWarps * G * dpc;
   {
-    const int c = tid & (vch - 1), grp = tid >> vsh, ngrp = kStepThreads >> vsh;
-    float o[G][VE], l[G];
+    float ls[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      l[g] = 0.f;
-#pragma unroll
-      for (int e = 0; e < VE; ++e) o[g][e] = 0.f;
+      ls[g] = 0.f;
+      for (int i = tid; i < nrows; i += kStepThreads) {
+        const float x = sA[g * chunk + i];
+        const float pr = (x == kNegInf) ? 0.f : __expf(x - mg[g]);
+        sA[g * chunk + i] = pr;
+        ls[g] += pr;
+      }
     }
-    for (int t = grp; t < T_all; t += ngrp) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float v = warp_sum(ls[g]);
+      if (lane == 0) sLw[warp * G + g] = v;
+    }
+  }
+  // V rows landed: the new value replaces the stale copy of its slot
+  if (!__syncthreads_and(mbar_wait(&bars[1], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
+  if (i_new >= 0 && tid < D) sV[(size_t)i_new * D + tid] = vnew;
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(smem + M.k);  // the K rows are no longer needed
+  {
+    const int c = tid % KCH, grp = tid / KCH, ngrp = kStepThreads / KCH;
+    float2 o[G][VE / 2];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int e = 0; e < VE / 2; ++e) o[g][e] = make_float2(0.f, 0.f);
+    for (int i = grp; i < nrows; i += ngrp) {
+      if (sInv[i] == -1) continue;  // free slot or unattended held row: never read its V
       float vf[VE];
-      unpack16<DT>(*reinterpret_cast<const uint4*>(sV + (size_t)t * dpc + c * VE), vf);
+      unpack16<DT>(*reinterpret_cast<const uint4*>(sV + (size_t)i * D + c * VE), vf);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float pr = sA[g * tmax + t];
-        l[g] += pr;
+        const float pr = sA[g * chunk + i];
+        const float2 p2 = make_float2(pr, pr);
 #pragma unroll
-        for (int e = 0; e < VE; ++e) o[g][e] = fmaf(pr, vf[e], o[g][e]);
+        for (int e = 0; e < VE / 2; ++e) o[g][e] = __ffma2_rn(p2, make_float2(vf[2 * e], vf[2 * e + 1]), o[g][e]);
       }
     }
-    for (int off = vch; off < 32; off <<= 1) {
+    for (int off = KCH; off < 32; off <<= 1) {
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        l[g] += __shfl_xor_sync(0xffffffffu, l[g], off);
+      for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int e = 0; e < VE; ++e) o[g][e] += __shfl_xor_sync(0xffffffffu, o[g][e], off);
-      }
+        for (int e = 0; e < VE / 2; ++e) {
+          o[g][e].x += __shfl_xor_sync(0xffffffffu, o[g][e].x, off);
+          o[g][e].y += __shfl_xor_sync(0xffffffffu, o[g][e].y, off);
+        }
     }
-    if (lane < vch) {
+    if (lane < KCH) {
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
+      for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int e = 0; e < VE; ++e) red[((size_t)warp * G + g) * dpc + c * VE + e] = o[g][e];
-        if (c == 0) redl[warp * G + g] = l[g];
-      }
+        for (int e = 0; e < VE / 2; ++e)
+          *reinterpret_cast<float2*>(red + ((size_t)warp * G + g) * D + c * VE + 2 * e) = o[g][e];
     }
   }
   __syncthreads();
-  T* outp = reinterpret_cast<T*>(a.out) + ((size_t)s * L.Hq + (size_t)h * G) * D + (size_t)p * dpc;
+  // ---- each column block goes to the CTA of head h that finalizes it ------------------------
+  const int DB = D / P;
+  for (int k = tid; k < G * D; k += kStepThreads) {
+    const int g = k / D, dd = k - g * D;
+    float v = 0.f;
 #pragma unroll
-  for (int g = 0; g < G; ++g)
-    for (int dd = tid; dd < dpc; dd += kStepThreads) {
-      float os = 0.f, ls = 0.f;
-#pragma unroll 4
-      for (int w = 0; w < kStepWarps; ++w) {
-        os += red[((size_t)w * G + g) * dpc + dd];
-        ls += redl[w * G + g];
-      }
-      float r = os / ls;
-      if (a.overflow_nan && mg[g] >= kExpOverflow) r = __int_as_float(0x7fc00000);
-      outp[(size_t)g * D + dd] = E::from_f(r);
+    for (int w = 0; w < kStepWarps; ++w) v += red[((size_t)w * G + g) * D + dd];
+    const int q = dd / DB, col = dd - q * DB;
+    float* dst = q == p ? sO : cluster.map_shared_rank(sO, h * P + q);
+    dst[((size_t)p * G + g) * DB + col] = v;
+  }
+  if (tid < G * P) {
+    const int g = tid % G, q = tid / G;
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kStepWarps; ++w) l += sLw[w * G + g];
+    float* dst = q == p ? sML : cluster.map_shared_rank(sML, h * P + q);
+    dst[2 * (p * G + g)] = mg[g];
+    dst[2 * (p * G + g) + 1] = l;
+  }
+  cluster.sync();  // last barrier: no distributed shared memory access after this point
+  T* outp = reinterpret_cast<T*>(a.out) + ((size_t)s * L.Hq + (size_t)h * G) * D + (size_t)p * DB;
+  for (int k = tid; k < G * DB; k += kStepThreads) {
+    const int g = k / DB, col = k - g * DB;
+    float Mx = kNegInf;
+    for (int q = 0; q < P; ++q) Mx = fmaxf(Mx, sML[2 * (q * G + g)]);
+    float Ls = 0.f, Os = 0.f;
+    for (int q = 0; q < P; ++q) {
+      const float w = __expf(sML[2 * (q * G + g)] - Mx);
+      Ls = fmaf(sML[2 * (q * G + g) + 1], w, Ls);
+      Os = fmaf(sO[((size_t)q * G + g) * DB + col], w, Os);
     }
+    float r = Os / Ls;
+    if (a.overflow_nan && Mx >= kExpOverflow) r = __int_as_float(0x7fc00000);
+    outp[(size_t)g * D + col] = E::from_f(r);
+  }
 
   // ---- counters (one thread of CTA 0) --------------------------------------------------------
   if (rank == 0 && tid == 0) {
@@ -855,23 +1057,35 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     st->n_free = n_free - 1 + n_ev;
     if (d.p_max > 0) st->qwin_head = (qwin_slot + 1) % d.p_max;
   }
-  // ---- work nothing in this kernel waits for: evicted payloads, query pool -------------------
-  if (n_ev > 0) {
+  // ---- work nothing in this kernel waits for: evicted payloads into the cold ring -----------
+  if (n_ev == 1) {
+    // spread over the cluster: the first CTA of each head copies that head's rows, the last
+    // CTA writes the index vector and the position
+    if (ev_dst >= 0 && ev_slot >= 0 && ev_slot < cap) {
+      if (p == 0 && warp == 0) {
+        const size_t roff = ((size_t)h * cap + ev_slot) * D;
+        const size_t doff = ((size_t)ev_dst * L.Hk + h) * D;
+        for (int c = lane; c < KCH; c += 32) {
+          reinterpret_cast<uint4*>(reinterpret_cast<T*>(d.cold_kpre) + doff)[c] =
+              reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(d.hot_kpre) + roff)[c];
+          reinterpret_cast<uint4*>(reinterpret_cast<T*>(d.cold_v) + doff)[c] =
+              reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(d.hot_v) + roff)[c];
+        }
+      }
+      if (rank == ncta - 1 && warp == kStepWarps - 1) {
+        const int64_t pv = ev_li == n_hot ? cur_pos : d.hot_pos[ev_slot];
+        step_evict_vec<DT, D>(L, d, ev_slot, ev_dst, pv);
+      }
+    } else if (ev_dst >= 0 && rank == 0 && tid == 0) {
+      set_status(st, HC_DEV_INDEX);
+    }
+  } else if (n_ev > 1) {
     const int nloc = sMisc[4];
     for (int q = warp; q < nloc; q += kStepWarps) {
       const int slot = sEvl[3 * q], dst = sEvl[3 * q + 1], li = sEvl[3 * q + 2];
       if (dst < 0) continue;  // more tokens evicted than the ring holds: the oldest are dropped
       const int64_t pv = li == n_hot ? cur_pos : (slot >= 0 && slot < cap ? d.hot_pos[slot] : -1);
       step_evict_one<DT, D>(L, d, slot, dst, pv);
-    }
-  }
-  // query pool push: mean over all query heads of the pre-RoPE query (controller.py:240-241)
-  if (rank == ncta - 1 && d.p_max > 0) {
-    for (int dd = tid; dd < D; dd += kStepThreads) {
-      float acc = 0.f;
-#pragma unroll 8
-      for (int hh = 0; hh < L.Hq; ++hh) acc += E::to_f(qp[(size_t)hh * D + dd]);
-      reinterpret_cast<T*>(d.qwin)[(size_t)qwin_slot * D + dd] = E::from_f(acc / (float)L.Hq);
     }
   }
 }
@@ -882,7 +1096,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 int step_parts(int Hk) { return (Hk >= 1 && Hk <= kStepMaxCluster && kStepMaxCluster % Hk == 0) ? kStepMaxCluster / Hk : 0; }
 
 static StepGeom layer_geom(const hc_layer& L, int use_held) {
-  return step_geom(L.Hk, L.D, L.max_cap, L.max_r, use_held);
+  return step_geom(L.Hk, L.max_cap, L.max_r, use_held, L.dtype != HC_F32);
 }
 
 size_t step_smem_bytes(const hc_layer& L, int use_held) {
@@ -890,8 +1104,8 @@ size_t step_smem_bytes(const hc_layer& L, int use_held) {
   if (!g.P || L.Hq % L.Hk) return 0;
   const int esz = L.dtype == HC_F32 ? 4 : 2;
   const int G = L.Hq / L.Hk;
-  if (G > 8 || g.dpc * esz < 16 || (g.dpc * esz) % 16 || (L.D * esz) < 128) return 0;
-  return step_smem(L.D, esz, G, L.Hk, g).total;
+  if (G > 8 || (L.D * esz) % 128 || L.D % g.P) return 0;
+  return step_smem(L.D, esz, G, L.Hk, L.max_r, g).total;
 }
 
 // Per-(kernel, shared memory size) launch checks, done once: the cluster-size opt-in and
@@ -932,7 +1146,7 @@ static cudaError_t step_prepare(K kern, cudaLaunchConfig_t* cfg) {
 template <int DT, int D, int G>
 static cudaError_t step_t(const StepArgs& a, cudaStream_t stream) {
   using T = typename Elem<DT>::T;
-  const StepSmem M = step_smem(D, sizeof(T), G, a.L.Hk, a.g);
+  const StepSmem M = step_smem(D, sizeof(T), G, a.L.Hk, a.L.max_r, a.g);
   auto kern = step_kernel<DT, D, G>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.L.Hk * a.g.P, a.L.n_seq);

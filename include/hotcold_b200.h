@@ -110,7 +110,11 @@ typedef struct hc_layer {
   int32_t max_ccap;        /* max cold ring capacity over sequences */
   float scale;             /* attention scale, 1/sqrt(D) */
   float rope_scaling;      /* rotary attention_scaling */
-} hc_layer;                /* 96 bytes */
+  const void* kmaps;       /* optional device array of two 128-byte TMA tensor maps written by
+                              hc_encode_kmap (f16/bf16): [0] the hot K slab of all sequences as
+                              rows of D elements, box 64 x 64 rows; [1] the held K rows, box
+                              64 x 8 rows. hc_step needs them for 16-bit dtypes. */
+} hc_layer;                /* 104 bytes */
 
 /* Library and error reporting. */
 HC_API const char* hc_version(void);
@@ -261,6 +265,16 @@ HC_API int hc_prompt_query_sum(const hc_layer* L, const void* q_dense, int64_t q
 HC_API size_t hc_attend_scratch_bytes(const hc_layer* L);
 HC_API int hc_attend(const hc_layer* L, const void* q_post, const int64_t* cur_pos, int use_held, void* out,
               int overflow_nan, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * TMA tensor map for hc_layer.kmaps, encoded on the host into `out` (128 bytes, copy it to
+ * 64-byte aligned device memory): a 2-D map over `rows` rows of D elements of dtype
+ * (HC_F16 or HC_BF16) starting at device address `base` (16-byte aligned, rows contiguous),
+ * box 64 elements x box_rows rows (1..256), 128-byte swizzle, out-of-range rows read as
+ * zero. No counterpart in the reference: it serves the TMA loads of the fused step.
+ * Returns HC_ERR_UNSUPPORTED when the driver offers no tensor-map encoder.
+ */
+HC_API int hc_encode_kmap(void* out, const void* base, int dtype, int64_t rows, int D, int box_rows);
 
 /*
  * Fused decode step of one layer: hc_append, hc_compress (decode, slab source)
