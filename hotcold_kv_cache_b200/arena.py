@@ -305,10 +305,11 @@ class LayerArena:
         """Whether the fused decode step fits this layer (one 16-CTA cluster per sequence)."""
         key = bool(use_held)
         if key not in self._step_ok:
-            # structural limits; the shared memory fit is decided by hc_step itself, which
-            # returns HC_ERR_UNSUPPORTED without launching anything
-            self._step_ok[key] = (self.n_seq >= 1 and self.Hk <= 16 and 16 % self.Hk == 0
-                                  and self.Hq // self.Hk in (1, 2, 4, 8))
+            ok = self.n_seq >= 1 and self.Hk <= 16 and 16 % self.Hk == 0 and self.Hq // self.Hk in (1, 2, 4, 8)
+            if ok:
+                with torch.cuda.device(self.device):
+                    ok = _lib.load().hc_step_check(byref(self.L), 1 if key else 0) == 0
+            self._step_ok[key] = ok
         return self._step_ok[key]
 
     def step(self, q_pre, k_pre, v, cos, sin, pos, use_held: bool, overflow_nan: bool = True):
@@ -392,7 +393,37 @@ class LayerArena:
         mc = int(self.cold_count.max())
         call("hc_retrieve_ex", byref(self.L), ptr(q_dense), qd[0], qd[1], qd[2], P, int(n_pool), ptr(extra_sum),
              int(extra_n), ptr(qvec), ptr(ws), ws.numel(), mc, self._stream())
-        self.launches += 3 if qvec is not None else 4
+        self.launches += 1 if self._retr_fused() else (3 if qvec is not None else 4)
+
+    def _retr_fused(self) -> bool:
+        """Whether hc_retrieve runs as the one-launch cluster kernel (its shared memory fits)."""
+        p2 = lambda x: 1 << max(0, int(x) - 1).bit_length()
+        nloc2 = p2(max(32, -(-self.max_ccap // 16)))
+        R2 = p2(max(1, self.r_max))
+        r16 = lambda b: (b + 15) // 16 * 16
+        nr = 1
+        while nr * 32 < nloc2:
+            nr <<= 1
+        RL = max(R2, 32)
+        smem = (r16(self.Hq * self.D * 4) + r16(self.F * 4) + 128 + r16(max(nloc2, 32) * 8 + RL * 8)
+                + r16(nr * RL * 8) + r16(16 * RL * 8) + 2 * r16(R2 * 4) + r16(-(-R2 // 16) * self.D * 4 + 16))
+        return smem <= 200 * 1024 and self.F <= 4096 and R2 <= 256
+
+    def retrieve_decode(self, q_pre, n_pool: int) -> bool:
+        """One-launch search + gather + re-RoPE with this step's q_pre (n_seq, Hq, D) as the
+        newest query-pool entry plus the n_pool newest pool entries. False when the fused
+        retrieval kernel does not fit (nothing launched)."""
+        nbytes = size("hc_retrieve_scratch_bytes", byref(self.L))
+        ws = self.ws.get(nbytes)
+        q, qss = self._row_major(q_pre, self.Hq)
+        rc = _lib.load().hc_retrieve_decode(byref(self.L), ptr(q), qss, int(n_pool), ptr(ws), ws.numel(),
+                                            self._stream())
+        if rc == 3:
+            return False
+        if rc != 0:
+            raise RuntimeError(f"hc_retrieve_decode failed (code {rc}): {_lib.load().hc_last_error().decode()}")
+        self.launches += 1
+        return True
 
     def prompt_query_sum(self, q_dense):
         out = torch.empty((self.n_seq, self.D), dtype=torch.float32, device=self.device)

@@ -407,21 +407,10 @@ class KVController:
         li = int(layer_idx)
         a = self.arena(li, q_pre.shape[1], k_pre.dtype, k_pre.device)
         hook = self.op_hook or (lambda name, phase: None)
-        if self.fused_step and not self._retrieval_fires(li):
-            # no search this step: append + compression + attention in one launch
-            use_held = self._poll_use_held(li)
-            hook("step", "begin")
-            res = a.step(q_pre, k_pre, v, cos, sin, pos, use_held, self.overflow_nan)
-            hook("step", "end")
-            if res is not None:
-                self._qpool[li].append(1)
-                self.maybe_launch_async_retrieval(li)  # counts the call; no search fires here
-                out, ev = res
-                self._count_eviction(ev)
-                self._count_injection(a, use_held)
-                self.dbg["triton_decode_calls"] += 1
+        if self.fused_step:
+            out = self._decode_fused(li, a, hook, q_pre, k_pre, v, cos, sin, pos)
+            if out is not None:
                 return out
-            self._undo_poll(li, use_held)
         hook("append", "begin")
         q_post = a.append(q_pre, k_pre, v, cos, sin, pos)
         hook("append", "end")
@@ -440,6 +429,53 @@ class KVController:
         out = a.attend(q_post, pos, use_held, self.overflow_nan)
         hook("attend", "end")
         return out
+
+    def _decode_fused(self, li, a, hook, q_pre, k_pre, v, cos, sin, pos):
+        """The decode step as one hc_step launch, preceded on search steps by one fused
+        retrieval launch whose pooled query takes this step's q_pre as the newest entry (its
+        query-pool push happens inside hc_step). Returns None, with nothing launched and no
+        counter changed, when the fused kernels do not fit; the caller then runs the split ops."""
+        fires = self._retrieval_fires(li)
+        if fires:
+            pool = list(self._qpool[li]) + [1]
+            pool = pool[-(self._qpool[li].maxlen or len(pool)):]
+            if any(isinstance(e, tuple) for e in pool) or not a.step_supported(self._poll_peek(li, True)):
+                return None  # the prompt's queries are still in the pool: the split ops handle it
+            hook("retrieve", "begin")
+            ok = a.retrieve_decode(q_pre, len(pool) - 1)
+            hook("retrieve", "end")
+            if not ok:
+                return None
+            # the bookkeeping of maybe_launch_async_retrieval + _retrieve for a search that fired
+            self.step_count[li] += 1
+            self.dbg["retrieval_ready_cpu"] += 1
+            self.dbg["prefetch_launched"] += 1
+            self.dbg["retrieval_launched"] += 1
+            self._staged[li] = True
+        use_held = self._poll_use_held(li)
+        hook("step", "begin")
+        res = a.step(q_pre, k_pre, v, cos, sin, pos, use_held, self.overflow_nan)
+        hook("step", "end")
+        if res is None:
+            self._undo_poll(li, use_held)
+            if fires:
+                raise RuntimeError("hc_step refused a layer after its retrieval ran")
+            return None
+        self._qpool[li].append(1)
+        if not fires:
+            self.maybe_launch_async_retrieval(li)  # counts the call; no search fires here
+        out, ev = res
+        self._count_eviction(ev)
+        self._count_injection(a, use_held)
+        self.dbg["triton_decode_calls"] += 1
+        return out
+
+    def _poll_peek(self, li: int, staged_now: bool) -> bool:
+        """Whether this step attends the held segment (what _poll_use_held will return),
+        without changing any state."""
+        if staged_now or self._staged[li]:
+            return True
+        return bool(self.hold_retrieved and self._held_active[li])
 
     def _retrieval_fires(self, li: int) -> bool:
         """Whether the next maybe_launch_async_retrieval(li) launches a search."""

@@ -189,6 +189,24 @@ int hc_retrieve_ex(const hc_layer* L, const void* q_dense, int64_t qd_seq, int64
                     "retrieve");
 }
 
+int hc_retrieve_decode(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, int n_pool, void* scratch,
+                       size_t scratch_bytes, void* stream) {
+  if (int rc = check_layer(L)) return rc;
+  if (!q_pre) return fail(HC_ERR_ARG, "NULL tensor argument");
+  if (L->max_r <= 0) return fail(HC_ERR_ARG, "lookahead_k is 0");
+  if (L->max_ccap <= 0) return fail(HC_ERR_ARG, "no cold ring");
+  if (n_pool < 0) return fail(HC_ERR_ARG, "n_pool < 0");
+  const size_t need = hc::retrieve_scratch_bytes(*L);
+  if (!scratch || scratch_bytes < need) return fail(HC_ERR_SCRATCH, "scratch %zu < %zu bytes", scratch_bytes, need);
+  const cudaError_t e = hc::launch_retrieve(*L, nullptr, 0, 0, 0, 0, n_pool, nullptr, 0, nullptr, scratch, L->max_ccap,
+                                            reinterpret_cast<cudaStream_t>(stream), q_pre, q_stride_seq);
+  if (e == cudaErrorNotSupported) {
+    (void)cudaGetLastError();
+    return fail(HC_ERR_UNSUPPORTED, "the fused retrieval kernel does not fit this layer");
+  }
+  return check_cuda(e, "retrieve_decode");
+}
+
 int hc_retrieve(const hc_layer* L, const void* q_dense, int64_t qd_seq, int64_t qd_head, int64_t qd_tok, int P,
                 int n_pool, const float* extra_sum, int extra_n, void* scratch, size_t scratch_bytes, void* stream) {
   return hc_retrieve_ex(L, q_dense, qd_seq, qd_head, qd_tok, P, n_pool, extra_sum, extra_n, nullptr, scratch,
@@ -290,6 +308,27 @@ int hc_encode_kmap(void* out, const void* base, int dtype, int64_t rows, int D, 
   return HC_OK;
 }
 
+static int step_checks(const hc_layer* L, int use_held) {
+  if (!hc::step_parts(L->Hk)) return fail(HC_ERR_UNSUPPORTED, "KV heads %d do not divide a 16-CTA cluster", L->Hk);
+  const size_t smem = hc::step_smem_bytes(*L, use_held);
+  if (smem == 0 || smem > 227 * 1024)
+    return fail(HC_ERR_UNSUPPORTED, "fused step needs %zu bytes of shared memory per CTA", smem);
+  if (L->dtype != HC_F32 && !L->kmaps) return fail(HC_ERR_UNSUPPORTED, "16-bit fused step needs hc_layer.kmaps");
+  return HC_OK;
+}
+
+int hc_step_check(const hc_layer* L, int use_held) {
+  if (int rc = check_layer(L)) return rc;
+  if (int rc = step_checks(L, use_held)) return rc;
+  const cudaError_t e = hc::launch_step(*L, nullptr, 0, nullptr, nullptr, 0, nullptr, nullptr, nullptr, use_held, nullptr,
+                                        0, nullptr, true);
+  if (e == cudaErrorNotSupported) {
+    (void)cudaGetLastError();
+    return fail(HC_ERR_UNSUPPORTED, "no resident 16-CTA cluster for this shared memory size");
+  }
+  return check_cuda(e, "step_check");
+}
+
 int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const void* k_pre, const void* v,
             int64_t kv_stride_seq, const void* cos, const void* sin, const int64_t* pos, int use_held, void* out,
             int overflow_nan, void* stream) {
@@ -297,11 +336,7 @@ int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const vo
   if (!q_pre || !k_pre || !v || !pos || !out) return fail(HC_ERR_ARG, "NULL tensor argument");
   if ((cos == nullptr) != (sin == nullptr)) return fail(HC_ERR_ARG, "cos and sin must both be given or both NULL");
   if (!cos && !L->inv_freq) return fail(HC_ERR_ARG, "no cos/sin and no inv_freq");
-  if (!hc::step_parts(L->Hk)) return fail(HC_ERR_UNSUPPORTED, "KV heads %d do not divide a 16-CTA cluster", L->Hk);
-  const size_t smem = hc::step_smem_bytes(*L, use_held);
-  if (smem == 0 || smem > 227 * 1024)
-    return fail(HC_ERR_UNSUPPORTED, "fused step needs %zu bytes of shared memory per CTA", smem);
-  if (L->dtype != HC_F32 && !L->kmaps) return fail(HC_ERR_UNSUPPORTED, "16-bit fused step needs hc_layer.kmaps");
+  if (int rc = step_checks(L, use_held)) return rc;
   const cudaError_t e = hc::launch_step(*L, q_pre, q_stride_seq, k_pre, v, kv_stride_seq, cos, sin, pos, use_held, out,
                                         overflow_nan, reinterpret_cast<cudaStream_t>(stream));
   if (e == cudaErrorNotSupported) {

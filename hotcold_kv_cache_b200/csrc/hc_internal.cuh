@@ -49,7 +49,7 @@ cudaError_t launch_compress(const hc_layer& L, const void* q_obs, int64_t qs0, i
 size_t compress_scratch_bytes(const hc_layer& L, int S_max, int tq);
 cudaError_t launch_retrieve(const hc_layer& L, const void* qd, int64_t q0, int64_t q1, int64_t q2, int P, int n_pool,
                             const float* extra_sum, int extra_n, const float* qvec_in, void* scratch, int max_count,
-                            cudaStream_t stream);
+                            cudaStream_t stream, const void* q_cur = nullptr, int64_t q_cur_ss = 0);
 cudaError_t launch_append_rotated(const hc_layer& L, const void* kpost, const void* kpre, const void* v, int64_t kvss,
                                   const int64_t* pos, cudaStream_t st);
 cudaError_t launch_cold_append(const hc_layer& L, const void* kpre, const void* v, int64_t s0, int64_t s1, int64_t s2,
@@ -57,7 +57,7 @@ cudaError_t launch_cold_append(const hc_layer& L, const void* kpre, const void* 
 size_t retrieve_scratch_bytes(const hc_layer& L);
 cudaError_t launch_step(const hc_layer& L, const void* q, int64_t qss, const void* k, const void* v, int64_t kvss,
                         const void* c, const void* sn, const int64_t* pos, int use_held, void* out, int overflow_nan,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool check_only = false);
 size_t step_smem_bytes(const hc_layer& L, int use_held);
 int step_parts(int Hk);
 

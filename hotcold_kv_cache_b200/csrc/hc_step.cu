@@ -1144,7 +1144,7 @@ static cudaError_t step_prepare(K kern, cudaLaunchConfig_t* cfg) {
 }
 
 template <int DT, int D, int G>
-static cudaError_t step_t(const StepArgs& a, cudaStream_t stream) {
+static cudaError_t step_t(const StepArgs& a, cudaStream_t stream, bool check_only) {
   using T = typename Elem<DT>::T;
   const StepSmem M = step_smem(D, sizeof(T), G, a.L.Hk, a.L.max_r, a.g);
   auto kern = step_kernel<DT, D, G>;
@@ -1163,24 +1163,24 @@ static cudaError_t step_t(const StepArgs& a, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaError_t e = step_prepare(kern, &cfg);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || check_only) return e;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 template <int DT, int D>
-static cudaError_t step_g(const StepArgs& a, cudaStream_t stream) {
+static cudaError_t step_g(const StepArgs& a, cudaStream_t stream, bool check_only) {
   switch (a.L.Hq / a.L.Hk) {
-    case 1: return step_t<DT, D, 1>(a, stream);
-    case 2: return step_t<DT, D, 2>(a, stream);
-    case 4: return step_t<DT, D, 4>(a, stream);
-    case 8: return step_t<DT, D, 8>(a, stream);
+    case 1: return step_t<DT, D, 1>(a, stream, check_only);
+    case 2: return step_t<DT, D, 2>(a, stream, check_only);
+    case 4: return step_t<DT, D, 4>(a, stream, check_only);
+    case 8: return step_t<DT, D, 8>(a, stream, check_only);
   }
   return cudaErrorNotSupported;
 }
 
 cudaError_t launch_step(const hc_layer& L, const void* q, int64_t qss, const void* k, const void* v, int64_t kvss,
                         const void* c, const void* sn, const int64_t* pos, int use_held, void* out, int overflow_nan,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, bool check_only) {
   if (!step_smem_bytes(L, use_held)) return cudaErrorNotSupported;
   StepArgs a{};
   a.L = L;
@@ -1196,12 +1196,12 @@ cudaError_t launch_step(const hc_layer& L, const void* q, int64_t qss, const voi
   a.use_held = use_held;
   a.overflow_nan = overflow_nan;
   a.g = layer_geom(L, use_held);
-  if (L.dtype == HC_F32 && L.D == 128) return step_g<HC_F32, 128>(a, stream);
-  if (L.dtype == HC_F16 && L.D == 128) return step_g<HC_F16, 128>(a, stream);
-  if (L.dtype == HC_BF16 && L.D == 128) return step_g<HC_BF16, 128>(a, stream);
-  if (L.dtype == HC_F32 && L.D == 64) return step_g<HC_F32, 64>(a, stream);
-  if (L.dtype == HC_F16 && L.D == 64) return step_g<HC_F16, 64>(a, stream);
-  if (L.dtype == HC_BF16 && L.D == 64) return step_g<HC_BF16, 64>(a, stream);
+  if (L.dtype == HC_F32 && L.D == 128) return step_g<HC_F32, 128>(a, stream, check_only);
+  if (L.dtype == HC_F16 && L.D == 128) return step_g<HC_F16, 128>(a, stream, check_only);
+  if (L.dtype == HC_BF16 && L.D == 128) return step_g<HC_BF16, 128>(a, stream, check_only);
+  if (L.dtype == HC_F32 && L.D == 64) return step_g<HC_F32, 64>(a, stream, check_only);
+  if (L.dtype == HC_F16 && L.D == 64) return step_g<HC_F16, 64>(a, stream, check_only);
+  if (L.dtype == HC_BF16 && L.D == 64) return step_g<HC_BF16, 64>(a, stream, check_only);
   return cudaErrorNotSupported;
 }
 

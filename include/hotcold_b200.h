@@ -267,6 +267,19 @@ HC_API int hc_attend(const hc_layer* L, const void* q_post, const int64_t* cur_p
               int overflow_nan, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * Decode-step retrieval whose pooled query is this step's pre-RoPE query q_pre
+ * (n_seq, Hq, D) with sequence stride q_stride_seq, taken as the newest pool entry (the mean
+ * over its heads rounded to the dtype, as the query-pool push computes it), followed by the
+ * n_pool newest entries of the query pool: the search of controller.py:314-342 for a step
+ * whose query-pool push happens later in hc_step. Search, gather and re-RoPE into the held
+ * segment as hc_retrieve. No counterpart in the reference (its push precedes the search in
+ * the same Python call). Returns HC_ERR_UNSUPPORTED when the fused retrieval kernel does not
+ * fit the layer.
+ */
+HC_API int hc_retrieve_decode(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, int n_pool, void* scratch,
+                              size_t scratch_bytes, void* stream);
+
+/*
  * TMA tensor map for hc_layer.kmaps, encoded on the host into `out` (128 bytes, copy it to
  * 64-byte aligned device memory): a 2-D map over `rows` rows of D elements of dtype
  * (HC_F16 or HC_BF16) starting at device address `base` (16-byte aligned, rows contiguous),
@@ -275,6 +288,13 @@ HC_API int hc_attend(const hc_layer* L, const void* q_post, const int64_t* cur_p
  * Returns HC_ERR_UNSUPPORTED when the driver offers no tensor-map encoder.
  */
 HC_API int hc_encode_kmap(void* out, const void* base, int dtype, int64_t rows, int D, int box_rows);
+
+/*
+ * Whether hc_step would launch for this layer (HC_OK) or return HC_ERR_UNSUPPORTED, checked
+ * without launching anything. No counterpart in the reference: it lets a caller decide
+ * between the fused step and the split ops before starting a step.
+ */
+HC_API int hc_step_check(const hc_layer* L, int use_held);
 
 /*
  * Fused decode step of one layer: hc_append, hc_compress (decode, slab source)
