@@ -77,7 +77,9 @@ struct CompressArgs {
   int* keep_src;   // [n_seq][S_max]
   int* ev_src;     // [n_seq][S_max]
   int* ev_dst;     // [n_seq][S_max]
+  void* qb;        // [n_seq][Hk][32][D] GQA-mean observation rows in the model dtype (tensor-core path)
   int tqmax;
+  int chunk_len;   // tokens per softmax partial in `part`
 };
 
 template <bool DENSE>
@@ -221,6 +223,164 @@ __global__ void __launch_bounds__(128) score_kernel(CompressArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------
+// SnapKV scoring on the 5th-generation tensor cores (16-bit dtypes, large inputs)
+// ------------------------------------------------------------------------------------------
+// The observation-window x prefix product (scoring.py:71-77) is a dense contraction per KV
+// head: logits[t][r] = k_t . qbar_r * scale for 128-token tiles. snap_qbar_kernel writes the
+// GQA-mean observation rows once; snap_tile_kernel gathers a tile of keys into the 128-byte
+// swizzled K-major layout (cp.async), issues D/16 tcgen05.mma (M = 128 tokens, N = the rows
+// padded to 16/32) into TMEM and reads one token per thread back with tcgen05.ld. Pass 0
+// writes per-warp (32-token) softmax partials of every row; after stats_kernel, pass 1
+// recomputes the tile and writes each token's importance sum_r softmax_r[t] directly, so the
+// [rows][S] logits never go to HBM.
+constexpr int kSnapTile = 128;
+
+template <int DT, int D, bool DENSE>
+__global__ void snap_qbar_kernel(CompressArgs a) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  const int h = blockIdx.x, s = blockIdx.y;
+  const hc_layer& L = a.L;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
+  const int tqu = pl.active ? min(min(pl.nobs, a.tq), 32) : 0;
+  const int G = L.Hq / L.Hk;
+  const T* q = reinterpret_cast<const T*>(a.q_obs) + (size_t)s * a.qs_seq;
+  T* out = reinterpret_cast<T*>(a.qb) + ((size_t)s * L.Hk + h) * 32 * D;
+  for (int i = threadIdx.x; i < 32 * D; i += blockDim.x) {
+    const int r = i / D, dd = i % D;
+    float v = 0.f;
+    if (r < tqu) {
+      const int row = a.tq - tqu + r;
+      float acc = 0.f;
+      for (int g = 0; g < G; ++g) acc += E::to_f(q[(size_t)(h * G + g) * a.qs_head + (size_t)row * a.qs_tok + dd]);
+      v = acc / (float)G;
+    }
+    out[i] = E::from_f(v);  // the dtype rounding of cache.py:60-64 / scoring.py:17-26
+  }
+}
+
+template <int DT, int D, bool DENSE, int PASS>
+__global__ void __launch_bounds__(kSnapTile, 1) snap_tile_kernel(CompressArgs a) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  constexpr int PL = D / 64;  // 128-byte planes of a row
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  unsigned char* sK = smem;                                   // PL x 128 rows x 128 B
+  unsigned char* sQ = smem + PL * kSnapTile * 128;            // PL x 32 rows x 128 B
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sQ + PL * 32 * 128);
+  uint32_t* sT = reinterpret_cast<uint32_t*>(bar + 1);
+  float* sStat = reinterpret_cast<float*>(sT + 4);          // [32][2] row max and sum (pass 1)
+  const int tile = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const hc_layer& L = a.L;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
+  if (!pl.active) return;
+  const int S = pl.S, t0 = tile * kSnapTile;
+  if (t0 >= S) return;
+  const int nt = min(kSnapTile, S - t0);
+  const int tqu = min(min(pl.nobs, a.tq), 32);
+  if (tqu <= 0) return;
+  const int NP = (tqu + 15) & ~15;  // the MMA's N: 16 or 32
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (PASS == 1 && tid < tqu) {
+    const float* st = a.stats + (((size_t)s * L.Hk + h) * a.tqmax + tid) * 2;
+    sStat[2 * tid] = st[0];
+    sStat[2 * tid + 1] = st[1];
+  }
+  // keys of the tile (rows past the sequence read as zeros), 16-byte chunk c of row r at
+  // plane c/8, chunk (c%8) ^ (r%8): the layout of the tensor cores' 128-byte swizzle
+  for (int k = tid; k < kSnapTile * PL * 8; k += kSnapTile) {
+    const int r = k / (PL * 8), c = k % (PL * 8), t = t0 + r;
+    const T* src = reinterpret_cast<const T*>(a.q_obs);
+    int nb = 0;
+    if (r < nt) {
+      if constexpr (DENSE) {
+        src = reinterpret_cast<const T*>(a.src_k) + (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)t * a.ss_tok;
+        nb = 16;
+      } else {
+        const int slot = d.hot_ord[t];
+        if (slot >= 0 && slot < d.cap) {
+          src = reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + slot) * D;
+          nb = 16;
+        } else if ((c & 7) == 0) {
+          set_status(d.st, HC_DEV_INDEX);
+        }
+      }
+    }
+    cp_async16(sK + (size_t)(c >> 3) * kSnapTile * 128 + (size_t)r * 128 + (((c & 7) ^ (r & 7)) << 4),
+               nb ? src + c * 8 : src, nb);
+  }
+  const T* qb = reinterpret_cast<const T*>(a.qb) + ((size_t)s * L.Hk + h) * 32 * D;
+  for (int k = tid; k < NP * PL * 8; k += kSnapTile) {
+    const int n = k / (PL * 8), c = k % (PL * 8);
+    cp_async16(sQ + (size_t)(c >> 3) * NP * 128 + (size_t)n * 128 + (((c & 7) ^ (n & 7)) << 4), qb + (size_t)n * D + c * 8,
+               16);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  fence_proxy_async_smem();  // the tensor cores read what cp.async wrote
+  if (warp == 0) tmem_alloc(sT, 32);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *sT;
+  if (tid == 0) {
+    constexpr uint32_t fmt = DT == HC_BF16 ? 1u : 0u;
+    const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(kSnapTile >> 4) << 24);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const uint32_t pl2 = ks >> 2, kin = ks & 3;
+      const uint32_t aa = smem_u32(sK) + pl2 * kSnapTile * 128u + kin * 32u;
+      const uint32_t bb = smem_u32(sQ) + pl2 * (uint32_t)NP * 128u + kin * 32u;
+      umma_f16(tbase, umma_desc_k_sw128(aa), umma_desc_k_sw128(bb), idesc, ks > 0);
+    }
+    umma_commit(bar);
+  }
+  if (!__syncthreads_and(mbar_wait(bar, 0)) && tid == 0) set_status(d.st, HC_DEV_TIMEOUT);
+  tc_fence_after();
+  float v[32];
+#pragma unroll
+  for (int c = 0; c < 32; c += 8)
+    if (c < NP) tmem_ld_x8(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v + c);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 32);
+  // logits of token t = t0 + tid; observation row r sits at S - tqu + r and masks later keys
+  // (scoring.py:72-74)
+  const int t = t0 + tid;
+#pragma unroll
+  for (int r = 0; r < 32; ++r)
+    v[r] = (r < tqu && tid < nt && t <= S - tqu + r) ? v[r] * L.scale : kNegInf;
+  if constexpr (PASS == 0) {
+    const int chunk = tile * (kSnapTile / 32) + warp;
+    if (chunk * 32 >= S) return;  // the partials cover ceil(S / 32) chunks
+    for (int r = 0; r < tqu; ++r) {
+      const float m = warp_max(v[r]);
+      const float l = warp_sum(v[r] == kNegInf ? 0.f : __expf(v[r] - m));
+      if (lane == 0) {
+        float* p = a.part + ((((size_t)s * L.Hk + h) * a.tqmax + r) * a.max_chunks + chunk) * 2;
+        p[0] = m;
+        p[1] = l;
+      }
+    }
+  } else {
+    if (tid < nt) {
+      float acc = 0.f;
+      for (int r = 0; r < tqu; ++r) acc += (v[r] == kNegInf) ? 0.f : __expf(v[r] - sStat[2 * r]) / sStat[2 * r + 1];
+      a.imp[((size_t)s * L.Hk + h) * a.S_max + t] = acc;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // SnapKV softmax statistics and token scores
 // ------------------------------------------------------------------------------------------
 // Per (head, row): max and sum of exp over the whole sequence from the chunk partials.
@@ -233,7 +393,7 @@ __global__ void stats_kernel(CompressArgs a) {
   const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
   if (!pl.active) return;
   const int tqu = min(pl.nobs, a.tq);
-  const int nch = (pl.S + kScoreCH - 1) / kScoreCH;
+  const int nch = (pl.S + a.chunk_len - 1) / a.chunk_len;
   for (int i = threadIdx.x; i < L.Hk * tqu; i += blockDim.x) {
     const int h = i / tqu, r = i % tqu;
     const float* p = a.part + (((size_t)s * L.Hk + h) * a.tqmax + r) * a.max_chunks * 2;
@@ -709,7 +869,7 @@ cudaError_t launch_cold_append(const hc_layer& L, const void* kpre, const void* 
 // host side
 // ------------------------------------------------------------------------------------------
 struct CompressLayout {
-  size_t hdr, logits, part, stats, imp, tok, sel, keep_src, ev_src, ev_dst, total;
+  size_t hdr, logits, part, stats, imp, tok, sel, keep_src, ev_src, ev_dst, qb, total;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -718,7 +878,7 @@ CompressLayout compress_layout(const hc_layer& L, int S_max, int tq) {
   CompressLayout c{};
   const size_t n = (size_t)L.n_seq, Hk = (size_t)L.Hk, S = (size_t)S_max;
   const size_t tqm = (size_t)(tq > 0 ? tq : 1);
-  const size_t chunks = (S + kScoreCH - 1) / kScoreCH;
+  const size_t chunks = (S + 31) / 32;  // softmax partials of 32 (tensor-core path) or 64 tokens
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
   c.hdr = take(n * 16 * sizeof(int));
@@ -731,6 +891,7 @@ CompressLayout compress_layout(const hc_layer& L, int S_max, int tq) {
   c.keep_src = take(n * S * sizeof(int));
   c.ev_src = take(n * S * sizeof(int));
   c.ev_dst = take(n * S * sizeof(int));
+  c.qb = take(n * Hk * 32 * (size_t)L.D * 2);
   c.total = off;
   return c;
 }
@@ -739,23 +900,43 @@ template <int DT, int D, bool DENSE>
 static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cudaStream_t stream) {
   using T = typename Elem<DT>::T;
   const hc_layer& L = a.L;
-  const size_t smem = sizeof(T) * kScoreCH * D + sizeof(float) * ((size_t)(a.tqmax + 1) * D + (size_t)a.tqmax * kScoreCH) + 64;
-  if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  auto sk = score_kernel<DT, D, DENSE>;
-  cudaError_t e = ensure_smem(sk, 200 * 1024);
-  if (e != cudaSuccess) return e;
-  const int chunks = (S_grid + kScoreCH - 1) / kScoreCH;
-  e = launch_pdl(sk, dim3(chunks, L.Hk, L.n_seq), dim3(128), smem, stream, a);
-  if (e != cudaSuccess) return e;
   // the selection CTA computes the token scores itself when its inputs fit shared memory
   const bool snap = L.policy == HC_POLICY_SNAPKV;
   const size_t rows = (size_t)L.Hk * (snap ? a.tqmax : 1);
   const size_t sel_smem =
       4 * (rows * S_grid + (snap ? (size_t)L.Hk * S_grid : 0) + 2 * rows + (size_t)S_grid) + S_grid + 64;
   const int small = sel_smem <= kSelectSmemMax ? 1 : 0;
+  // large SnapKV inputs of 16-bit layers: the observation x prefix product on the tensor cores
+  const bool tc = snap && !small && DT != HC_F32 && (D % 64) == 0 && min(L.recent, a.tq) <= 32;
+  cudaError_t e = cudaSuccess;
+  if (tc) {
+    a.chunk_len = 32;
+    const int tiles = (S_grid + kSnapTile - 1) / kSnapTile;
+    const size_t tsmem = (size_t)(D / 64) * (kSnapTile + 32) * 128 + 8 + 16 + 256 + 1024;
+    auto k0 = snap_tile_kernel<DT, D, DENSE, 0>;
+    auto k1 = snap_tile_kernel<DT, D, DENSE, 1>;
+    e = ensure_smem(k0, tsmem);
+    if (e == cudaSuccess) e = ensure_smem(k1, tsmem);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(snap_qbar_kernel<DT, D, DENSE>, dim3(L.Hk, L.n_seq), dim3(256), 0, stream, a);
+    if (e == cudaSuccess) e = launch_pdl(k0, dim3(tiles, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a);
+    if (e == cudaSuccess) e = launch_pdl(stats_kernel<DENSE>, dim3(L.n_seq), dim3(256), 0, stream, a);
+    if (e == cudaSuccess) e = launch_pdl(k1, dim3(tiles, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a);
+    if (e != cudaSuccess) return e;
+  } else {
+    const size_t smem =
+        sizeof(T) * kScoreCH * D + sizeof(float) * ((size_t)(a.tqmax + 1) * D + (size_t)a.tqmax * kScoreCH) + 64;
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    auto sk = score_kernel<DT, D, DENSE>;
+    e = ensure_smem(sk, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    const int chunks = (S_grid + kScoreCH - 1) / kScoreCH;
+    e = launch_pdl(sk, dim3(chunks, L.Hk, L.n_seq), dim3(128), smem, stream, a);
+    if (e != cudaSuccess) return e;
+  }
   if (!small) {
     const int blocks = (int)((S_grid + 255) / 256) < 592 ? (S_grid + 255) / 256 : 592;
-    if (L.policy == HC_POLICY_SNAPKV) {
+    if (snap && !tc) {
       e = launch_pdl(stats_kernel<DENSE>, dim3(L.n_seq), dim3(256), 0, stream, a);
       if (e != cudaSuccess) return e;
       const int ib = (int)(((long)L.Hk * S_grid + 255) / 256) < 1184 ? (int)(((long)L.Hk * S_grid + 255) / 256) : 1184;
@@ -801,7 +982,7 @@ cudaError_t launch_compress(const hc_layer& L, const void* q_obs, int64_t qs0, i
   a.tqmax = tq > 0 ? tq : 1;
   a.S_dense = S_dense;
   a.S_max = S_grid;
-  a.max_chunks = (S_grid + kScoreCH - 1) / kScoreCH;
+  a.max_chunks = (S_grid + 31) / 32;
   a.src_k = sk; a.src_v = sv; a.src_kpre = skp;
   a.ss_seq = ss0; a.ss_head = ss1; a.ss_tok = ss2;
   a.src_pos = spos;
@@ -815,6 +996,8 @@ cudaError_t launch_compress(const hc_layer& L, const void* q_obs, int64_t qs0, i
   a.keep_src = reinterpret_cast<int*>(base + lay.keep_src);
   a.ev_src = reinterpret_cast<int*>(base + lay.ev_src);
   a.ev_dst = reinterpret_cast<int*>(base + lay.ev_dst);
+  a.qb = base + lay.qb;
+  a.chunk_len = kScoreCH;
   if (L.dtype == HC_F32 && L.D == 128) return compress_dt<HC_F32, 128>(a, dense, S_grid, n_evict_hint, stream);
   if (L.dtype == HC_F16 && L.D == 128) return compress_dt<HC_F16, 128>(a, dense, S_grid, n_evict_hint, stream);
   if (L.dtype == HC_BF16 && L.D == 128) return compress_dt<HC_BF16, 128>(a, dense, S_grid, n_evict_hint, stream);

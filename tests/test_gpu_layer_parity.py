@@ -149,3 +149,23 @@ def test_cfg0_full_size():
     if steps == 63:
         for k, v in layer.dbg.items():
             assert res["ctrl"].dbg[k] == v, k
+
+
+@pytest.mark.parametrize("dtype,D,recent,T", [("float16", 128, 32, 2048), ("bfloat16", 128, 20, 1537),
+                                              ("float16", 64, 8, 2177), ("bfloat16", 64, 32, 1000)])
+def test_snapkv_prompt_scoring_tensor_cores(dtype, D, recent, T):
+    """Prompt compression of 16-bit layers whose scores exceed one selection CTA: the
+    observation x prefix logits run on the tensor cores (M = 128 tokens, N = 16 or 32 rows)
+    with ragged tails (T not a multiple of 32 or 128). Hot sets after the prompt and three
+    decode steps against the oracle."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import run_cuda_layer
+    c = dict(B=2, Hq=32, Hk=8, D=D, T=T, steps=3, dtype=dtype, policy="snapkv", cap=256, recent=recent,
+             topk_ratio=0.0, pool_kernel=7, ccap=4096, faiss_dim=D, window_size=1 << 20, pool=4, R=16,
+             hold=True, rap=True, theta=500000.0, seed=91 + D + recent)
+    inp = synth.layer_inputs(c["seed"], c["B"], c["Hq"], c["Hk"], D, T, c["steps"], dtype)
+    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], **oracle_kwargs(c))
+    res = run_cuda_layer(c, inp, c["steps"])
+    near = 2e-3 if dtype == "float16" else 2e-2
+    assert _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near) >= 1
+    assert res["ctrl"].device_status() == 0
