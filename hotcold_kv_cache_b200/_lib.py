@@ -74,6 +74,10 @@ SIGNATURES = {
     "hc_attend_scratch_bytes": (c_size_t, [_P]),
     "hc_attend": (c_int, [_P, _P, _P, c_int, _P, c_int, _P, c_size_t, _P]),
     "hc_shard_merge": (c_int, [_P, _P, c_int, c_int, _P, _P, _P]),
+    "hc_cold_topk_scratch_bytes": (c_size_t, [c_int64, c_int]),
+    "hc_cold_topk": (c_int, [_P, c_int64, c_int, c_int64, _P, c_int, _P, _P, _P, c_size_t, _P]),
+    "hc_splice_hits": (c_int, [_P, _P, c_int, _P]),
+    "hc_retrieve_query": (c_int, [_P, _P, c_int64, c_int64, c_int64, c_int, c_int, _P, c_int, _P, _P]),
     "hc_step_check": (c_int, [_P, c_int]),
     "hc_retrieve_decode": (c_int, [_P, _P, _I64, c_int, _P, c_size_t, _P]),
     "hc_encode_kmap": (c_int, [_P, _P, c_int, _I64, c_int, c_int]),

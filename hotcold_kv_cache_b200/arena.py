@@ -256,21 +256,38 @@ class LayerArena:
             raise ValueError("k_post, v and k_pre must share strides with unit stride over head_dim")
         return st[0], st[1], st[2]
 
-    def compress_prompt(self, q_obs, k_post, v, k_pre, pos):
+    def _seq_view(self, s: int):
+        """hc_layer over sequence s alone: the descriptor array and counters from its entry on,
+        n_seq = 1 (every per-sequence buffer is reached through the descriptor)."""
+        L = _lib.HcLayer()
+        ctypes.memmove(ctypes.addressof(L), ctypes.addressof(self.L), ctypes.sizeof(L))
+        L.desc = self.desc.data_ptr() + s * ctypes.sizeof(_lib.HcSeqDesc)
+        L.counters = self.counters.data_ptr() + s * self.Hk * 4
+        L.n_seq = 1
+        L.kmaps = None
+        return L
+
+    def compress_prompt(self, q_obs, k_post, v, k_pre, pos, seq: int | None = None):
         """Prompt of T tokens into an empty slab: sequences with T > budget score, keep and
         evict into the cold ring (cache.py:37-128 on the prompt); the others keep the whole
-        prompt. Tensors (n_seq,Hk,T,D), q_obs (n_seq,Hq,tq,D). Returns evicted counts."""
+        prompt. Tensors (n_seq,Hk,T,D), q_obs (n_seq,Hq,tq,D). With `seq`, the tensors hold
+        that one sequence of a ragged batch (leading dimension 1). Returns evicted counts."""
         T = k_post.shape[2]
-        self.ensure_hot_capacity([min(T, b) + 1 for b in self.budgets])
+        seqs = range(self.n_seq) if seq is None else [int(seq)]
+        need = np.asarray(self.caps, np.int64).copy() if seq is not None else np.zeros(self.n_seq, np.int64)
+        for s in seqs:
+            need[s] = min(T, self.budgets[s]) + 1
+        self.ensure_hot_capacity(need)
+        L = self.L if seq is None else self._seq_view(int(seq))
         tq = q_obs.shape[2]
         qs = q_obs.stride()
-        nbytes = size("hc_compress_scratch_bytes", byref(self.L), T, tq)
+        nbytes = size("hc_compress_scratch_bytes", byref(L), T, tq)
         ws = self.ws.get(nbytes)
         pos = pos.contiguous()
-        call("hc_compress_ex", byref(self.L), ptr(q_obs), qs[0], qs[1], qs[2], tq, T, ptr(k_post), ptr(v), ptr(k_pre),
+        call("hc_compress_ex", byref(L), ptr(q_obs), qs[0], qs[1], qs[2], tq, T, ptr(k_post), ptr(v), ptr(k_pre),
              *self._strides(k_post, v, k_pre), ptr(pos), ptr(ws), ws.numel(), 1 << 30, self._stream())
         ev = np.zeros(self.n_seq, np.int64)
-        for s in range(self.n_seq):
+        for s in seqs:
             p = self.plan(s, T)
             if p is None:
                 self.n_hot[s] = T
@@ -394,6 +411,37 @@ class LayerArena:
         call("hc_retrieve_ex", byref(self.L), ptr(q_dense), qd[0], qd[1], qd[2], P, int(n_pool), ptr(extra_sum),
              int(extra_n), ptr(qvec), ptr(ws), ws.numel(), mc, self._stream())
         self.launches += 1 if self._retr_fused() else (3 if qvec is not None else 4)
+
+    def retrieve_sharded(self, searcher, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0,
+                         qvec=None):
+        """hc_retrieve with the scan divided by token range over the ranks of `searcher` (a
+        shard.ShardedColdSearch): pooled query (hc_retrieve_query), this rank's range of every
+        sequence's cold entries scored and cut to its top R (hc_cold_topk), the all-gather and
+        merge to the global top R, then the same splice on every rank (hc_splice_hits). The
+        rows of a ring that has never wrapped sit in age order from slot 0, so a token range is
+        a contiguous block of slots."""
+        if (self.cold_count >= np.asarray(self.ccaps)).any():
+            raise RuntimeError("sharded search needs cold rings that have never filled")
+        if qvec is None:
+            qvec = torch.empty((self.n_seq, self.F), dtype=torch.float32, device=self.device)
+            qd, P = (0, 0, 0), 0
+            if q_dense is not None:
+                qd, P = q_dense.stride()[:3], q_dense.shape[2]
+            call("hc_retrieve_query", byref(self.L), ptr(q_dense), qd[0], qd[1], qd[2], P, int(n_pool),
+                 ptr(extra_sum), int(extra_n), ptr(qvec), self._stream())
+            self.launches += 1
+        from .shard import token_range
+        rows, n = [], []
+        for s in range(self.n_seq):
+            c = int(self.cold_count[s])
+            lo, hi = token_range(c, searcher.rank, searcher.world)
+            rows.append(self.cold_vec[s, lo:hi])
+            n.append(c)
+        searcher.ws = self.ws
+        k = max(self.r_max, 1)
+        ids = searcher.search(rows, n, qvec, k)
+        call("hc_splice_hits", byref(self.L), ptr(ids), k, self._stream())
+        self.launches += 2 * self.n_seq + self.n_seq + 2
 
     def _retr_fused(self) -> bool:
         """Whether hc_retrieve runs as the one-launch cluster kernel (its shared memory fits)."""

@@ -138,6 +138,14 @@ class KVController:
         self.op_hook = None
         # decode steps without a search run as one fused launch (hc_step) when the layer fits
         self.fused_step = True
+        # ragged batches: per-sequence budgets and cold capacities (set_ragged), else the
+        # scalar settings above apply to every sequence
+        self.seq_budgets = None
+        self.seq_ccaps = None
+        self._tails: List[dict] = []
+        # a shard.ShardedColdSearch: cold searches scan only this rank's token range and merge
+        # the ranks' candidates (every rank runs the same decode); None = search the whole ring
+        self.cold_search = None
         self.dbg = {k: (0.0 if k == "prefetch_copy_ms_sum" else 0) for k in DBG_KEYS}
 
     # ------------------------------------------------------------------ setup
@@ -147,7 +155,10 @@ class KVController:
         if self._inited:
             return
         B, Hk, _, D = k_pre.shape
-        self.B, self.Hk, self.D, self.n_layers = int(B), int(Hk), int(D), int(n_layers)
+        self._init_dims(int(B), int(Hk), int(D), int(n_layers), k_pre.device)
+
+    def _init_dims(self, B: int, Hk: int, D: int, n_layers: int, device):
+        self.B, self.Hk, self.D, self.n_layers = B, Hk, D, n_layers
         L = self.n_layers
         self.step_count = [0] * L
         self.arenas = [None] * L
@@ -156,8 +167,23 @@ class KVController:
         self._staged = [False] * L
         self._held_active = [False] * L
         self._retrieval_ready_cpu = [None] * L
-        self.workspace = Workspace(k_pre.device)
+        self._tails = [dict() for _ in range(L)]
+        self.workspace = Workspace(device)
         self._inited = True
+
+    def set_ragged(self, budgets, ccaps, Hk: int, D: int, n_layers: int, device):
+        """A ragged batch of len(budgets) independent sequences with their own budgets and cold
+        ring capacities. Each sequence's prompt goes through prefill_sequence (any length),
+        then finish_prefill per layer; decode_layer then steps all of them at once."""
+        if self._inited:
+            raise RuntimeError("set_ragged must come before the first forward")
+        if self.query_pool_size >= self.window_size:
+            raise ValueError("ragged prompts need query_pool_size < window_size (prompt queries stay out of the pool)")
+        if len(budgets) != len(ccaps):
+            raise ValueError("one budget and one cold capacity per sequence")
+        self.seq_budgets = [int(b) for b in budgets]
+        self.seq_ccaps = [int(c) for c in ccaps]
+        self._init_dims(len(budgets), int(Hk), int(D), int(n_layers), device)
 
     def set_rotary(self, inv_freq: torch.Tensor, attention_scaling: float = 1.0):
         """Rotary parameters for re-rotating retrieved keys (instead of the active module)."""
@@ -178,12 +204,14 @@ class KVController:
         if a is None:
             inv_freq, sc = self._rotary_params()
             a = LayerArena(n_seq=self.B, Hq=int(Hq), Hk=self.Hk, D=self.D, F=self.faiss_dim, dtype=dtype,
-                           device=device, budgets=self.max_capacity_prompt, r_max=max(self.lookahead_k, 0),
-                           ccap=self.cpu_buffer_size, p_max=max(self.query_pool_size, 1), policy=self.policy,
+                           device=device, budgets=self.seq_budgets or self.max_capacity_prompt,
+                           r_max=max(self.lookahead_k, 0), ccap=self.seq_ccaps or self.cpu_buffer_size,
+                           p_max=max(self.query_pool_size, 1), policy=self.policy,
                            recent=self.recent_size, topk_ratio=self.topk_ratio, pool_kernel=self.pool_kernel,
                            pooling=self.pooling, normalize=self.normalize_for_ip, inv_freq=inv_freq,
                            rope_scaling=sc, workspace=self.workspace,
-                           hot_cap_hint=None if self.max_capacity_prompt < (1 << 16) else 4096)
+                           hot_cap_hint=None if max(self.seq_budgets or [self.max_capacity_prompt]) < (1 << 16)
+                           else 4096)
             self.arenas[li] = a
         return a
 
@@ -197,7 +225,7 @@ class KVController:
         if int(ev.max(initial=0)) > 0:
             self.dbg["compress_calls"] += 1
             self.dbg["evicted_tokens"] += int(ev.sum())
-            self.dbg["faiss_add"] += int(np.minimum(ev, self.cpu_buffer_size).sum())
+            self.dbg["faiss_add"] += int(np.minimum(ev, self.seq_ccaps or self.cpu_buffer_size).sum())
 
     def add_evicted_to_cold_store(self, layer_idx: int, ev: EvictedKV):
         """controller.py:190-238: append evicted tokens (host or device tensors) to the
@@ -213,7 +241,7 @@ class KVController:
         kp = ev.k_pre_cpu.to(device=a.device, dtype=a.dtype)
         vv = ev.v_cpu.to(device=a.device, dtype=a.dtype)
         m = a.cold_append(kp, vv, ev.pos_cpu, ev.evicted_idx)
-        self.dbg["faiss_add"] += int(np.minimum(m, self.cpu_buffer_size).sum())
+        self.dbg["faiss_add"] += int(np.minimum(m, self.seq_ccaps or self.cpu_buffer_size).sum())
 
     @property
     def cpu_kpre_ring(self):
@@ -281,7 +309,10 @@ class KVController:
         return n_pool, (self._prompt_qsum[li] if extra_n else None), extra_n
 
     def _retrieve(self, li: int, **kw):
-        self.arenas[li].retrieve(**kw)
+        if self.cold_search is not None:
+            self.arenas[li].retrieve_sharded(self.cold_search, **kw)
+        else:
+            self.arenas[li].retrieve(**kw)
         self.dbg["retrieval_ready_cpu"] += 1   # some sequence has a non-empty ring: hits are valid
         self.dbg["prefetch_launched"] += 1
         self._staged[li] = True
@@ -337,7 +368,10 @@ class KVController:
             self._retrieval_ready_cpu[li] = None
             self.dbg["retrieval_ready_empty"] += 1
             return
-        a.retrieve(qvec=qv.contiguous())
+        if self.cold_search is not None:
+            a.retrieve_sharded(self.cold_search, qvec=qv.contiguous())
+        else:
+            a.retrieve(qvec=qv.contiguous())
         self._retrieval_ready_cpu[li] = self._held_pack(li)
         self._staged[li] = True
         self.dbg["retrieval_ready_cpu"] += 1
@@ -399,6 +433,34 @@ class KVController:
         if self.retrieve_after_prefill:
             self.launch_retrieval_now(li, q_pre[:, :, -self.query_pool_size:, :])
 
+    def prefill_sequence(self, layer_idx: int, b: int, q_pre, q_post, k_pre, k_post, v, positions):
+        """The prompt forward of sequence b of a ragged batch (set_ragged) in one layer:
+        compression of its prompt into its hot slab with eviction into its cold ring (the
+        per-sequence form of prefill_layer). Tensors (1,H,T_b,D); positions (1,T_b)."""
+        li, b = int(layer_idx), int(b)
+        if self.seq_budgets is None:
+            raise RuntimeError("prefill_sequence needs set_ragged")
+        a = self.arena(li, q_pre.shape[1], k_post.dtype, k_post.device)
+        T = int(k_post.shape[2])
+        r = self.recent_size
+        q_obs = q_post if T <= r else q_post[:, :, -r:, :]
+        ev = a.compress_prompt(q_obs, k_post, v, k_pre, positions.to(k_post.device, torch.int64), seq=b)
+        self._count_eviction(ev)
+        self.dbg["triton_prefill_fallback"] += 1
+        if self.retrieve_after_prefill:
+            self._tails[li][b] = q_pre[:, :, -self.query_pool_size:, :]
+
+    def finish_prefill(self, layer_idx: int):
+        """After every sequence of a ragged batch went through prefill_sequence in this layer:
+        the prompt-end retrieval of all of them in one search (patch.py:232)."""
+        li = int(layer_idx)
+        tails = self._tails[li]
+        if self.retrieve_after_prefill and tails:
+            if len(tails) != self.B or len({t.shape[2] for t in tails.values()}) != 1:
+                raise ValueError("every sequence needs a prompt of at least query_pool_size tokens")
+            self.launch_retrieval_now(li, torch.cat([tails[b] for b in range(self.B)], 0))
+        self._tails[li] = {}
+
     def decode_layer(self, layer_idx: int, q_pre, k_pre, v, cos, sin, pos):
         """One decode step of one layer (patch.py:151-315): RoPE + append + query-pool push,
         scheduled retrieval into the held segment, compression with eviction, and
@@ -436,6 +498,8 @@ class KVController:
         query-pool push happens inside hc_step). Returns None, with nothing launched and no
         counter changed, when the fused kernels do not fit; the caller then runs the split ops."""
         fires = self._retrieval_fires(li)
+        if fires and self.cold_search is not None:
+            return None  # the sharded search runs with the split ops
         if fires:
             pool = list(self._qpool[li]) + [1]
             pool = pool[-(self._qpool[li].maxlen or len(pool)):]

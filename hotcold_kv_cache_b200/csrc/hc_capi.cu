@@ -356,4 +356,41 @@ int hc_shard_merge(const float* cand_score, const int32_t* cand_id, int n_shards
                     "shard_merge");
 }
 
+size_t hc_cold_topk_scratch_bytes(int64_t n_rows, int k) {
+  return n_rows < 0 || k <= 0 ? 0 : hc::cold_topk_scratch_bytes(n_rows, k);
+}
+
+int hc_cold_topk(const float* index, int64_t n_rows, int F, int64_t id_base, const float* qvec, int k,
+                 float* out_score, int32_t* out_id, void* scratch, size_t scratch_bytes, void* stream) {
+  if (!qvec || !out_score || !out_id || !scratch || (n_rows > 0 && !index))
+    return fail(HC_ERR_ARG, "NULL tensor argument");
+  if (n_rows < 0 || F <= 0 || F > 4096 || k <= 0 || k > 256)
+    return fail(HC_ERR_ARG, "n_rows %lld, F %d, k %d: need n_rows >= 0, 1 <= F <= 4096, 1 <= k <= 256",
+                (long long)n_rows, F, k);
+  if (id_base < 0 || id_base + n_rows > 0x7fffffffLL) return fail(HC_ERR_ARG, "ids must fit int32");
+  if ((F & 3) == 0 && F <= 128 && (reinterpret_cast<uintptr_t>(index) & 15))
+    return fail(HC_ERR_ARG, "index rows must be 16-byte aligned");
+  if (scratch_bytes < hc::cold_topk_scratch_bytes(n_rows, k)) return fail(HC_ERR_ARG, "scratch too small");
+  return check_cuda(hc::launch_cold_topk(index, n_rows, F, id_base, qvec, k, out_score, out_id, scratch,
+                                         reinterpret_cast<cudaStream_t>(stream)),
+                    "cold_topk");
+}
+
+int hc_retrieve_query(const hc_layer* L, const void* q_dense, int64_t qd_seq, int64_t qd_head, int64_t qd_tok, int P,
+                      int n_pool, const float* extra_sum, int extra_n, float* out_qvec, void* stream) {
+  if (int rc = check_layer(L)) return rc;
+  if (!out_qvec) return fail(HC_ERR_ARG, "NULL output");
+  if (q_dense && P <= 0) return fail(HC_ERR_ARG, "P must be positive with q_dense");
+  if (!q_dense && (n_pool < 0 || n_pool > 0x7fffffff)) return fail(HC_ERR_ARG, "bad n_pool");
+  return check_cuda(hc::launch_retrieve_query(*L, q_dense, qd_seq, qd_head, qd_tok, P, n_pool, extra_sum, extra_n,
+                                              out_qvec, reinterpret_cast<cudaStream_t>(stream)),
+                    "retrieve_query");
+}
+
+int hc_splice_hits(const hc_layer* L, const int32_t* hit_ids, int k, void* stream) {
+  if (int rc = check_layer(L)) return rc;
+  if (!hit_ids || k < 0) return fail(HC_ERR_ARG, "NULL hit ids or negative k");
+  return check_cuda(hc::launch_splice_hits(*L, hit_ids, k, reinterpret_cast<cudaStream_t>(stream)), "splice_hits");
+}
+
 }  // extern "C"

@@ -327,6 +327,15 @@ __device__ __forceinline__ void block_merge_tree(unsigned long long* lists, int 
   }
 }
 
+__device__ __forceinline__ void block_merge_tree_any(unsigned long long* lists, int m, int RL) {
+  switch (RL) {
+    case 32: block_merge_tree<1>(lists, m); break;
+    case 64: block_merge_tree<2>(lists, m); break;
+    case 128: block_merge_tree<4>(lists, m); break;
+    default: block_merge_tree<8>(lists, m); break;
+  }
+}
+
 __device__ __forceinline__ void block_merge_topr_any(unsigned long long* lists, int m, int RL) {
   switch (RL) {
     case 32: block_merge_tree<1>(lists, m); break;
@@ -610,6 +619,193 @@ __global__ void __launch_bounds__(kRetThreads, 1) retr_kernel(RetrieveArgs a, in
 }
 
 // ------------------------------------------------------------------------------------------
+// Exact inner-product top-k over a block of index rows: the search of IndexFlatIP
+// (controller.py:274) over one token-range shard of the cold index. Rows are scored with the
+// arithmetic of the ring scan above (8 lanes per row, the same xor-tree order), so a row's
+// score does not depend on which shard holds it and the union of the shards' top-k holds the
+// exact global top-k. Ids are id_base + row; ties go to the lower id.
+//   topk_scan_kernel   CTA c scans rows [c*per_cta, (c+1)*per_cta) in batches of 1024: keys
+//                      into shared memory, warp-sorted 32-key runs, a merge tree to the best
+//                      RL, merged into the CTA's running best; writes its list of RL keys;
+//   topk_merge_kernel  CTA b merges lists [32b, 32b+32); the last CTA to finish (an atomic
+//                      ticket, no waiting) merges those results and writes the top k.
+// ------------------------------------------------------------------------------------------
+constexpr int kTopkThreads = 512;
+constexpr int kTopkBatch = 1024;
+constexpr int kTopkFanIn = 32;
+
+struct TopkArgs {
+  const float* index;
+  int64_t n;
+  int F;
+  int64_t id_base;
+  const float* q;
+  int k, RL, per_cta, nA, nB;
+  unsigned long long* lists;   // [nA][RL]
+  unsigned long long* lists2;  // [nB][RL]
+  unsigned int* ticket;
+  float* out_score;
+  int32_t* out_id;
+};
+
+__host__ __device__ inline size_t topk_scan_smem(int F, int RL) {
+  return (size_t)((F + 3) & ~3) * 4 + (size_t)kTopkBatch * 8 + (size_t)(kTopkBatch / 32) * RL * 8 + (size_t)RL * 8;
+}
+
+__device__ __forceinline__ void warp_merge_topr_any(const unsigned long long* A, const unsigned long long* B,
+                                                    unsigned long long* out, int RL) {
+  switch (RL) {
+    case 32: warp_merge_topr<1>(A, B, out); break;
+    case 64: warp_merge_topr<2>(A, B, out); break;
+    case 128: warp_merge_topr<4>(A, B, out); break;
+    default: warp_merge_topr<8>(A, B, out); break;
+  }
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_scan_kernel(TopkArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int F = a.F, RL = a.RL;
+  float* qv = reinterpret_cast<float*>(smem);
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem + (size_t)((F + 3) & ~3) * 4);
+  unsigned long long* runs = keys + kTopkBatch;
+  unsigned long long* best = runs + (size_t)(kTopkBatch / 32) * RL;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = kTopkThreads / 32;
+  pdl_wait();
+  for (int f = tid; f < F; f += kTopkThreads) qv[f] = a.q[f];
+  for (int j = tid; j < RL; j += kTopkThreads) best[j] = 0ull;
+  __syncthreads();
+  const int64_t r0 = (int64_t)blockIdx.x * a.per_cta;
+  const int64_t r1 = min(a.n, r0 + a.per_cta);
+  const bool vec = (F & 3) == 0 && F <= 128;
+  const int nv = F >> 2, sub = lane & 7, rg = lane >> 3;
+  float4 qc[4];
+  if (vec) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+      qc[m] = sub + 8 * m < nv ? reinterpret_cast<const float4*>(qv)[sub + 8 * m] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int64_t b0 = r0; b0 < r1; b0 += kTopkBatch) {
+    const int nb = (int)min((int64_t)kTopkBatch, r1 - b0);
+    if (vec) {
+      constexpr int U = 2;
+      for (int base = warp * 4; base < nb; base += 4 * NW * U) {
+        float4 x[U][4];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * 4 * NW + rg;
+          const float4* row = reinterpret_cast<const float4*>(a.index + (size_t)(b0 + i) * F);
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            x[u][m] = (i < nb && sub + 8 * m < nv) ? row[sub + 8 * m] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * 4 * NW + rg;
+          float pt[4];
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            pt[m] = x[u][m].x * qc[m].x + x[u][m].y * qc[m].y + x[u][m].z * qc[m].z + x[u][m].w * qc[m].w;
+          float v = (pt[0] + pt[2]) + (pt[1] + pt[3]);
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          if (sub == 0 && i < nb)
+            keys[i] = ((unsigned long long)fkey(v) << 32) | (0xffffffffu - (uint32_t)(a.id_base + b0 + i));
+        }
+      }
+    } else {
+      for (int i = warp; i < nb; i += NW) {
+        const float* row = a.index + (size_t)(b0 + i) * F;
+        float acc = 0.f;
+        for (int f = lane; f < F; f += 32) acc = fmaf(row[f], qv[f], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) keys[i] = ((unsigned long long)fkey(acc) << 32) | (0xffffffffu - (uint32_t)(a.id_base + b0 + i));
+      }
+    }
+    __syncthreads();
+    const int nruns = (nb + 31) >> 5;
+    for (int r = warp; r < nruns; r += NW) {
+      const int i = r * 32 + lane;
+      unsigned long long x = i < nb ? keys[i] : 0ull;
+      x = warp_sort_desc_u64(x);
+      __syncwarp();
+      runs[(size_t)r * RL + lane] = x;
+      for (int j = 32 + lane; j < RL; j += 32) runs[(size_t)r * RL + j] = 0ull;
+    }
+    int m = 1;
+    while (m < nruns) m <<= 1;
+    for (int i = nruns * RL + tid; i < m * RL; i += kTopkThreads) runs[i] = 0ull;
+    __syncthreads();
+    block_merge_topr_any(runs, m, RL);
+    if (warp == 0) warp_merge_topr_any(best, runs, best, RL);
+    __syncthreads();
+  }
+  unsigned long long* dst = a.lists + (size_t)blockIdx.x * RL;
+  for (int j = tid; j < RL; j += kTopkThreads) dst[j] = best[j];
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(TopkArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned long long* sl = reinterpret_cast<unsigned long long*>(smem);
+  __shared__ int last;
+  const int RL = a.RL, tid = threadIdx.x, b = blockIdx.x;
+  pdl_wait();
+  for (int i = tid; i < kTopkFanIn * RL; i += kTopkThreads) {
+    const int l = b * kTopkFanIn + i / RL;
+    sl[i] = l < a.nA ? a.lists[(size_t)l * RL + i % RL] : 0ull;
+  }
+  __syncthreads();
+  block_merge_tree_any(sl, kTopkFanIn, RL);
+  for (int j = tid; j < RL; j += kTopkThreads) a.lists2[(size_t)b * RL + j] = sl[j];
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(a.ticket, 1u) == (unsigned)(a.nB - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  int m = 1;
+  while (m < a.nB) m <<= 1;
+  for (int i = tid; i < m * RL; i += kTopkThreads)
+    sl[i] = i / RL < a.nB ? __ldcg(a.lists2 + i) : 0ull;
+  __syncthreads();
+  block_merge_tree_any(sl, m, RL);
+  for (int j = tid; j < a.k; j += kTopkThreads) {
+    const unsigned long long key = sl[j];
+    const bool live = key != 0ull;
+    const uint32_t u = (uint32_t)(key >> 32);
+    const uint32_t bits = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+    a.out_score[j] = live ? __uint_as_float(bits) : kNegInf;
+    a.out_id[j] = live ? (int32_t)(0xffffffffu - (uint32_t)(key & 0xffffffffu)) : -1;
+  }
+  if (tid == 0) *a.ticket = 0u;  // ready for the next call
+}
+
+// Held slots from given hits: hit_ids (n_seq, k) are live cold entries in age order (0 = the
+// oldest), -1 for none; slot j takes hit j (the gather order of controller.py:277-285).
+__global__ void hits_kernel(hc_layer L, const int32_t* hit_ids, int k) {
+  const int s = blockIdx.x;
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  const int count = max(0, min(d.st->cold_count, d.ccap)), head = d.st->cold_head;
+  __shared__ int nh;
+  if (threadIdx.x == 0) nh = 0;
+  __syncthreads();
+  for (int j = threadIdx.x; j < d.r_max; j += blockDim.x) {
+    const int id = j < k ? hit_ids[(size_t)s * k + j] : -1;
+    const bool ok = id >= 0 && id < count;
+    if (id >= count) set_status(d.st, HC_DEV_INDEX);
+    d.held_src[j] = ok ? (int)(((long)head + id) % d.ccap) : -1;
+    if (ok) atomicAdd(&nh, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    d.st->n_hits = nh;
+    d.st->held_len = d.r_max;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // multi-GPU: merge per-shard candidates into the global top-k (ties to the lower id)
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) shard_merge_kernel(const float* cs, const int32_t* cid, int n, int k,
@@ -759,6 +955,83 @@ cudaError_t launch_shard_merge(const float* cs, const int32_t* cid, int n_shards
                                float* out_score, cudaStream_t stream) {
   shard_merge_kernel<<<1, 1024, 0, stream>>>(cs, cid, n_shards * k, k, out_id, out_score);
   return cudaGetLastError();
+}
+
+static int topk_rl(int k) {
+  int RL = 32;
+  while (RL < k) RL <<= 1;
+  return RL;
+}
+static int topk_ctas(int64_t n) {
+  int64_t c = (n + 255) / 256;
+  if (c > 296) c = 296;
+  return c < 1 ? 1 : (int)c;
+}
+size_t cold_topk_scratch_bytes(int64_t n, int k) {
+  const int RL = topk_rl(k), nA = topk_ctas(n), nB = (nA + kTopkFanIn - 1) / kTopkFanIn;
+  return al256((size_t)nA * RL * 8) + al256((size_t)nB * RL * 8) + 256;
+}
+
+cudaError_t launch_cold_topk(const float* index, int64_t n, int F, int64_t id_base, const float* q, int k,
+                             float* out_score, int32_t* out_id, void* scratch, cudaStream_t stream) {
+  TopkArgs a{};
+  a.index = index;
+  a.n = n;
+  a.F = F;
+  a.id_base = id_base;
+  a.q = q;
+  a.k = k;
+  a.RL = topk_rl(k);
+  a.nA = topk_ctas(n);
+  a.per_cta = (int)((n + a.nA - 1) / a.nA);
+  a.nB = (a.nA + kTopkFanIn - 1) / kTopkFanIn;
+  char* base = reinterpret_cast<char*>(scratch);
+  a.lists = reinterpret_cast<unsigned long long*>(base);
+  a.lists2 = reinterpret_cast<unsigned long long*>(base + al256((size_t)a.nA * a.RL * 8));
+  a.ticket = reinterpret_cast<unsigned int*>(base + al256((size_t)a.nA * a.RL * 8) + al256((size_t)a.nB * a.RL * 8));
+  a.out_score = out_score;
+  a.out_id = out_id;
+  cudaError_t e = cudaMemsetAsync(a.ticket, 0, sizeof(unsigned int), stream);
+  if (e != cudaSuccess) return e;
+  const size_t s1 = topk_scan_smem(F, a.RL), s2 = (size_t)kTopkFanIn * a.RL * 8;
+  e = ensure_smem(topk_scan_kernel, s1);
+  if (e == cudaSuccess) e = ensure_smem(topk_merge_kernel, s2);
+  if (e == cudaSuccess) e = launch_pdl(topk_scan_kernel, dim3(a.nA), dim3(kTopkThreads), s1, stream, a);
+  if (e == cudaSuccess) e = launch_pdl(topk_merge_kernel, dim3(a.nB), dim3(kTopkThreads), s2, stream, a);
+  return e;
+}
+
+template <int DT, int D>
+static cudaError_t splice_hits_t(RetrieveArgs a, const int32_t* hit_ids, int k, cudaStream_t stream) {
+  const hc_layer& L = a.L;
+  cudaError_t e = launch_pdl(hits_kernel, dim3(L.n_seq), dim3(256), 0, stream, L, hit_ids, k);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(splice_kernel<DT, D>, dim3((L.max_r + 7) / 8, L.n_seq), dim3(256), 0, stream, a);
+}
+
+template <int DT, int D>
+static cudaError_t query_t(RetrieveArgs a, cudaStream_t stream) {
+  return launch_pdl(query_kernel<DT, D>, dim3(a.L.n_seq), dim3(D), 0, stream, a);
+}
+
+cudaError_t launch_retrieve_query(const hc_layer& L, const void* qd, int64_t q0, int64_t q1, int64_t q2, int P,
+                                  int n_pool, const float* extra_sum, int extra_n, float* qvec, cudaStream_t stream) {
+  RetrieveArgs a{};
+  a.L = L;
+  a.q_dense = qd;
+  a.qd_seq = q0; a.qd_head = q1; a.qd_tok = q2;
+  a.P = P;
+  a.n_pool = n_pool;
+  a.extra_sum = extra_sum;
+  a.extra_n = extra_n;
+  a.qvec = qvec;
+  HC_DISPATCH_DT_D(L.dtype, L.D, query_t, a, stream);
+}
+
+cudaError_t launch_splice_hits(const hc_layer& L, const int32_t* hit_ids, int k, cudaStream_t stream) {
+  RetrieveArgs a{};
+  a.L = L;
+  HC_DISPATCH_DT_D(L.dtype, L.D, splice_hits_t, a, hit_ids, k, stream);
 }
 
 }  // namespace hc

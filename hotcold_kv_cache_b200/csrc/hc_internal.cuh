@@ -64,6 +64,12 @@ int step_parts(int Hk);
 // Set the message hc_last_error() returns on the calling thread.
 void set_last_error(const char* msg);
 
+size_t cold_topk_scratch_bytes(int64_t n, int k);
+cudaError_t launch_cold_topk(const float* index, int64_t n, int F, int64_t id_base, const float* q, int k,
+                             float* out_score, int32_t* out_id, void* scratch, cudaStream_t stream);
+cudaError_t launch_retrieve_query(const hc_layer& L, const void* qd, int64_t q0, int64_t q1, int64_t q2, int P,
+                                  int n_pool, const float* extra_sum, int extra_n, float* qvec, cudaStream_t stream);
+cudaError_t launch_splice_hits(const hc_layer& L, const int32_t* hit_ids, int k, cudaStream_t stream);
 cudaError_t launch_shard_merge(const float* cs, const int32_t* cid, int n_shards, int k, int32_t* out_id,
                                float* out_score, cudaStream_t stream);
 

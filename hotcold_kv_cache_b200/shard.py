@@ -1,0 +1,95 @@
+"""Cold-store search split by token range over ranks (one process per GPU).
+
+The reference searches one CPU FAISS IndexFlatIP per layer (controller.py:250-293). Here a
+layer's cold index can be scanned by `world` ranks at once: rank r scores the entries of its
+token range [r*n/world, (r+1)*n/world) of the cold ring (hc_cold_topk, the same arithmetic
+as the single-device scan), keeps its best k as (score, global id), and one all-gather of
+world*k pairs over NCCL lets every rank merge them (hc_shard_merge) into the exact global
+top k (ties to the lower id, i.e. the older entry), because the global top k is a subset of
+the union of the ranges' top k. Every rank then splices the same hits (hc_splice_hits).
+
+Decode state and payload are the same on every rank (each rank runs the sequence's decode
+on its own copy, so the pooled query needs no broadcast); only the scan is divided.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr, size
+
+
+def token_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Entries [lo, hi) of a cold index of n entries that `rank` of `world` scans."""
+    return rank * n // world, (rank + 1) * n // world
+
+
+def local_topk(index_rows: torch.Tensor, id_base: int, qvec: torch.Tensor, k: int, ws=None):
+    """Exact inner-product top k of index_rows (n, F) fp32 against qvec (F,) fp32, ids
+    id_base + row (hc_cold_topk). Returns (scores (k,) fp32, ids (k,) int32) on the device."""
+    dev = qvec.device
+    n, F = (int(index_rows.shape[0]), int(index_rows.shape[1])) if index_rows.numel() else (0, int(qvec.numel()))
+    if n and (index_rows.stride(1) != 1 or index_rows.stride(0) != F):
+        index_rows = index_rows.contiguous()
+    nbytes = size("hc_cold_topk_scratch_bytes", n, k)
+    scratch = ws.get(nbytes) if ws is not None else torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    sc = torch.empty(k, dtype=torch.float32, device=dev)
+    ids = torch.empty(k, dtype=torch.int32, device=dev)
+    call("hc_cold_topk", ptr(index_rows) if n else None, n, F, int(id_base), ptr(qvec.contiguous()), int(k), ptr(sc),
+         ptr(ids), ptr(scratch), scratch.numel(), _lib.stream_of(dev))
+    return sc, ids
+
+
+def merge_candidates(cand_scores: torch.Tensor, cand_ids: torch.Tensor, n_shards: int, k: int):
+    """Global top k of n_shards lists of k (score, id) candidates (hc_shard_merge)."""
+    dev = cand_scores.device
+    out_id = torch.empty(k, dtype=torch.int32, device=dev)
+    out_sc = torch.empty(k, dtype=torch.float32, device=dev)
+    call("hc_shard_merge", ptr(cand_scores.contiguous()), ptr(cand_ids.contiguous()), int(n_shards), int(k),
+         ptr(out_id), ptr(out_sc), _lib.stream_of(dev))
+    return out_sc, out_id
+
+
+class ShardedColdSearch:
+    """The exchange of a token-range-sharded cold search over a process group.
+
+    search(rows, n, qvecs, k) takes, for each of B sequences, this rank's rows of the cold
+    index (rows[b] covers entries token_range(n[b], rank, world)) and its query vector, and
+    returns the (B, k) global top-k ids on every rank. One all-gather per search, whatever B.
+    `local` and `merge` default to the CUDA kernels; a test may pass host functions with the
+    same contracts to check the exchange without a GPU.
+    """
+
+    def __init__(self, group=None, rank: int | None = None, world: int | None = None, local=None, merge=None):
+        import torch.distributed as dist
+        self.dist = dist if dist.is_available() and dist.is_initialized() else None
+        self.group = group
+        self.rank = rank if rank is not None else (dist.get_rank(group) if self.dist else 0)
+        self.world = world if world is not None else (dist.get_world_size(group) if self.dist else 1)
+        self.local = local or local_topk
+        self.merge = merge or merge_candidates
+        self.ws = None
+
+    def search(self, rows, n, qvecs, k: int) -> torch.Tensor:
+        B = len(rows)
+        dev = qvecs.device
+        sc = torch.empty((B, k), dtype=torch.float32, device=dev)
+        ids = torch.empty((B, k), dtype=torch.int32, device=dev)
+        for b in range(B):
+            lo, _ = token_range(int(n[b]), self.rank, self.world)
+            s, i = self.local(rows[b], lo, qvecs[b], k, self.ws) if self.local is local_topk else \
+                self.local(rows[b], lo, qvecs[b], k)
+            sc[b], ids[b] = s, i
+        if self.world > 1:
+            all_sc = torch.empty((self.world * B, k), dtype=torch.float32, device=dev)
+            all_id = torch.empty((self.world * B, k), dtype=torch.int32, device=dev)
+            self.dist.all_gather_into_tensor(all_sc, sc, group=self.group)
+            self.dist.all_gather_into_tensor(all_id, ids, group=self.group)
+            all_sc, all_id = all_sc.view(self.world, B, k), all_id.view(self.world, B, k)
+        else:
+            all_sc, all_id = sc[None], ids[None]
+        out = torch.empty((B, k), dtype=torch.int32, device=dev)
+        for b in range(B):
+            _, out[b] = self.merge(all_sc[:, b].reshape(-1), all_id[:, b].reshape(-1), self.world, k)
+        return out

@@ -317,6 +317,34 @@ HC_API int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, c
 HC_API int hc_shard_merge(const float* cand_score, const int32_t* cand_id, int n_shards, int k, int32_t* out_id,
                    float* out_score, void* stream);
 
+/*
+ * Exact inner-product top-k over n_rows index vectors (row-major fp32, F per row): the
+ * IndexFlatIP.search of controller.py:274 over one block of the cold index, e.g. the
+ * token-range shard a rank holds. qvec (F) fp32 on the device; writes the k best as
+ * (out_score, out_id) sorted by score, ids id_base + row, ties to the lower id, -1 / -inf
+ * past n_rows. Rows are scored with the ring scan's arithmetic, so a row's score does not
+ * depend on the block it sits in. Scratch from hc_cold_topk_scratch_bytes.
+ */
+HC_API size_t hc_cold_topk_scratch_bytes(int64_t n_rows, int k);
+HC_API int hc_cold_topk(const float* index, int64_t n_rows, int F, int64_t id_base, const float* qvec, int k,
+                        float* out_score, int32_t* out_id, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * The pooled query vector of hc_retrieve alone (_q_to_vecs_np / _pooled_query_np,
+ * controller.py:184-188,243-248; same query sources and rounding), written to out_qvec
+ * (n_seq, F) fp32: the query a sharded search hands to hc_cold_topk.
+ *
+ * Held segment from given hits: hit_ids (n_seq, k) int32 are live cold entries in age order
+ * (0 = the oldest live entry, the numbering of the cold ring's index), -1 for none. Slot j
+ * takes hit j: gather of the payload (controller.py:277-285), RoPE at the original position
+ * (patch.py:94-102) and splice (patch.py:249-256), as the tail of hc_retrieve. Used after a
+ * search done elsewhere (hc_cold_topk on index shards and hc_shard_merge).
+ */
+HC_API int hc_retrieve_query(const hc_layer* L, const void* q_dense, int64_t qd_seq, int64_t qd_head,
+                             int64_t qd_tok, int P, int n_pool, const float* extra_sum, int extra_n, float* out_qvec,
+                             void* stream);
+HC_API int hc_splice_hits(const hc_layer* L, const int32_t* hit_ids, int k, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,3 +78,47 @@ def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused
 def cold_positions(ctrl, li=0):
     a = ctrl.arenas[li]
     return [a.cold_pos[b].index_select(0, a.cold_order(b)).cpu().numpy() for b in range(a.n_seq)]
+
+
+def run_cuda_ragged(case, seq_inputs, budgets, ccaps, n_steps, device="cuda:0", fused=True):
+    """A ragged batch through one controller: sequence b has its own prompt (seq_inputs[b],
+    B=1 arrays of layer_inputs), budget and cold capacity; prompts go in one at a time
+    (prefill_sequence + finish_prefill), decode steps run all sequences at once with their
+    own positions. Returns dict(outs [per-step (n_seq,Hq,D)], hot [per-step list of arrays], ctrl)."""
+    c = case
+    dev = torch.device(device)
+    dt = TORCH_DT[c["dtype"]]
+    Hq, Hk, D = c["Hq"], c["Hk"], c["D"]
+    n = len(seq_inputs)
+
+    def t(x):
+        return torch.from_numpy(np.ascontiguousarray(x).astype(np.float32)).to(device=dev, dtype=dt)
+
+    rot = rotary(Hq, D, c["theta"], dev)
+    ctrl = KVController(**controller_kwargs(c))
+    ctrl.fused_step = fused
+    ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
+    ctrl.set_ragged(budgets, ccaps, Hk, D, 1, dev)
+    Ts = []
+    for b, inp in enumerate(seq_inputs):
+        q_pre, k_pre, v = t(inp["q_pre"]), t(inp["k_pre"]), t(inp["v"])
+        T = q_pre.shape[2]
+        Ts.append(T)
+        pos = torch.arange(T, device=dev).unsqueeze(0)
+        cos, sin = rot(torch.empty(1, dtype=dt, device=dev), pos)
+        q_post, k_post = apply_rotary_pos_emb(q_pre, k_pre, cos, sin)
+        ctrl.prefill_sequence(0, b, q_pre, q_post, k_pre, k_post, v, pos)
+    ctrl.finish_prefill(0)
+    dq = torch.cat([t(inp["dq"]) for inp in seq_inputs], 1)  # (steps, n, Hq, D)
+    dk = torch.cat([t(inp["dk"]) for inp in seq_inputs], 1)
+    dv = torch.cat([t(inp["dv"]) for inp in seq_inputs], 1)
+    outs, hot = [], []
+    for i in range(n_steps):
+        pd = torch.tensor([T + i for T in Ts], device=dev, dtype=torch.long)
+        c1, s1 = rot(torch.empty(1, dtype=dt, device=dev), pd[:, None])
+        o = ctrl.decode_layer(0, dq[i], dk[i], dv[i], c1.reshape(n, D), s1.reshape(n, D), pd)
+        outs.append(o.double().cpu().numpy())
+        a = ctrl.arenas[0]
+        hot.append([a.hot_pos[b].index_select(0, a.logical_order(b)).cpu().numpy() for b in range(n)])
+    torch.cuda.synchronize(dev)
+    return dict(outs=outs, hot=hot, ctrl=ctrl)
