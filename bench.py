@@ -16,7 +16,19 @@ L2 is flushed before each replay, and each replay is bracketed by CUDA events
 on the launching stream. value = device time / layer-steps (us per layer-step,
 lower is better), max over ranks at N > 1 (each rank runs its own replica).
 
+Two more workloads (--workload), measured on request and not part of the default line:
+  ragged      the ragged continuous batch: 64 sequences of lengths
+              uniform in [2048, 32768] with budgets cycling 512/1024/2048, one layer,
+              partitioned over the N ranks by balanced token count, no collective on the
+              decode path; value = us per sequence-layer-step of the whole batch.
+  cold-shard  the long cold store (BASELINE configs[4] shape): a 131072-token prompt per
+              layer compressed to budget 2048 (about 129k cold entries), top-256 retrieval
+              from 8 query states every step, the cold index scanned by token range over the
+              N ranks and the candidates merged after an NCCL all-gather; every rank runs the
+              same decode. value = us per layer-step.
+
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                       [--workload decode|ragged|cold-shard]
 """
 
 from __future__ import annotations
@@ -48,18 +60,20 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--policy", default="snapkv", choices=["snapkv", "hotcold"])
     p.add_argument("--layers", type=int, default=32)
-    p.add_argument("--prompt", type=int, default=8192)
-    p.add_argument("--budget", type=int, default=512)
+    p.add_argument("--prompt", type=int, default=None, help="default 8192 (decode), 131072 (cold-shard)")
+    p.add_argument("--budget", type=int, default=None, help="default 512 (decode), 2048 (cold-shard)")
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--cpu-steps", type=int, default=16)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", default="decode", choices=["decode", "ragged", "cold-shard"])
+    p.add_argument("--seqs", type=int, default=64)
     return p.parse_args()
 
 
 def config(a):
     recent = 32 if a.policy == "snapkv" else 128
-    ratio = 0.0 if a.policy == "snapkv" else max(0.05, 0.75 - recent / a.budget)  # run_baselines.py:86-87
-    return dict(Hq=32, Hk=8, D=128, theta=500000.0, layers=a.layers, prompt=a.prompt, budget=a.budget,
+    ratio = 0.0 if a.policy == "snapkv" else max(0.05, 0.75 - recent / (a.budget or 512))  # run_baselines.py:86-87
+    return dict(Hq=32, Hk=8, D=128, theta=500000.0, layers=a.layers, prompt=a.prompt or 8192, budget=a.budget or 512,
                 policy=a.policy, recent=recent, topk_ratio=ratio, pool_kernel=7, ccap=32768, faiss_dim=128,
                 window_size=16, query_pool_size=4, lookahead_k=64, hold=True, dtype="float16")
 
@@ -483,6 +497,185 @@ def run_e2e(wl, start, n, dev):
 
 
 # ------------------------------------------------------------------------------------------
+# extra workloads: ragged batch over ranks, token-range sharded cold search
+# ------------------------------------------------------------------------------------------
+def _rotary(Hq, Hk, D, theta, dev):
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+    cfg = LlamaConfig(hidden_size=Hq * D, num_attention_heads=Hq, num_key_value_heads=Hk, head_dim=D,
+                      num_hidden_layers=1, rope_theta=theta, vocab_size=16, intermediate_size=16,
+                      max_position_embeddings=1 << 18)
+    return LlamaRotaryEmbedding(cfg).to(dev)
+
+
+def _prefill_inputs(g, Hq, Hk, T, D, dev, rot):
+    import torch
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    dt = torch.float16
+    q = torch.randn((1, Hq, T, D), generator=g, device=dev, dtype=dt)
+    k = torch.randn((1, Hk, T, D), generator=g, device=dev, dtype=dt)
+    v = torch.randn((1, Hk, T, D), generator=g, device=dev, dtype=dt)
+    pos = torch.arange(T, device=dev)[None]
+    cos, sin = rot(torch.empty(1, dtype=dt, device=dev), pos)
+    qp, kp = apply_rotary_pos_emb(q, k, cos, sin)
+    return q, qp, k, kp, v, pos
+
+
+def _timed_graph_steps(step_fn, first, K, dev, world):
+    """Capture each of K steps as a CUDA graph and replay it between CUDA events after an
+    L2 flush; returns (per-step ms, sum of the max over ranks)."""
+    import torch
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+    times = []
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(first, first + K):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                step_fn(i)
+        graph_upload(g, cur)
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        g.replay()
+        e1.record(cur)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+        del g
+    torch.cuda.synchronize(dev)
+    tot = torch.tensor([sum(times)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.MAX)
+    return times, float(tot.item())
+
+
+def run_ragged(a, rank, world):
+    import torch
+    from hotcold_kv_cache_b200 import KVController, synth
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    Hq, Hk, D = 32, 8, 128
+    items = synth.ragged_batch(a.seed, a.seqs)
+    mine = synth.balanced_partition(items, world)[rank]
+    n = len(mine)
+    rot = _rotary(Hq, Hk, D, 500000.0, dev)
+    ctrl = KVController(max_capacity_prompt=2048, topk_ratio=0.0, recent_size=32, cpu_buffer_size=32768,
+                        faiss_dim=128, window_size=1 << 20, query_pool_size=8, lookahead_k=64, hold_retrieved=True,
+                        retrieve_after_prefill=True, policy="snapkv", pool_kernel=7, profile_overlap=False)
+    ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
+    ctrl.set_ragged([items[i][1] for i in mine], [items[i][0] for i in mine], Hk, D, 1, dev)
+    for b, i in enumerate(mine):
+        g = torch.Generator(device=dev).manual_seed(a.seed * 1000 + i)
+        q, qp, k, kp, v, pos = _prefill_inputs(g, Hq, Hk, items[i][0], D, dev, rot)
+        ctrl.prefill_sequence(0, b, q, qp, k, kp, v, pos)
+        del q, qp, k, kp, v
+    ctrl.finish_prefill(0)
+    K, W = a.steps, a.warmup
+    g = torch.Generator(device=dev).manual_seed(a.seed + 7 + rank)
+    dq = torch.randn((W + K, n, Hq, D), generator=g, device=dev, dtype=torch.float16)
+    dk = torch.randn((W + K, n, Hk, D), generator=g, device=dev, dtype=torch.float16)
+    dv = torch.randn((W + K, n, Hk, D), generator=g, device=dev, dtype=torch.float16)
+    lens = torch.tensor([items[i][0] for i in mine], device=dev)
+    pos = torch.stack([lens + i for i in range(W + K)], 0).contiguous()  # (steps, n)
+    cs, sn = rot(torch.empty(1, dtype=torch.float16, device=dev), pos)
+    cs, sn = cs.contiguous(), sn.contiguous()
+
+    def step(i):
+        ctrl.decode_layer(0, dq[i], dk[i], dv[i], cs[i], sn[i], pos[i])
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize(dev)
+    a0 = ctrl.arenas[0]
+    l0 = a0.launches
+    times, max_total = _timed_graph_steps(step, W, K, dev, world)
+    launches = a0.launches - l0
+    if ctrl.device_status():
+        raise RuntimeError("device status word set")
+    units = len(items) * K
+    value = max_total * 1e3 / units
+    # per sequence-layer-step: K/V of the held + hot tokens, the eviction's key scan and payload
+    hot = np.asarray(a0.n_hot, np.float64)
+    byts = float(((hot + a0.r_max) * Hk * D * 2 * 2 + hot * Hk * D * 2 + 2 * Hk * D * 2 * 2).sum())
+    tot_b = torch.tensor([byts], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(tot_b)
+    gbs = float(tot_b.item()) * K / (max_total * 1e-3) / 1e9
+    return {"metric": "ragged batch decode: us per sequence-layer-step (64 seqs, attn+evict)", "value": round(value, 3),
+            "unit": "us/sequence-layer-step", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(max_total / K, 4), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic N(0,1) pre-RoPE q/k/v, seeded per sequence",
+            "config": {"workload": "ragged batch: 64 sequences, lengths U[2048,32768], budgets 512/1024/2048, 1 layer",
+                       "seqs_this_rank": n, "tokens_this_rank": int(sum(items[i][0] for i in mine)),
+                       "partition": "balanced token count (LPT)", "parallelism": f"sequences over {world} ranks",
+                       "l2": "flushed before every timed step"},
+            "aggregate_hbm_gbs": round(gbs, 1), "gpu_launches": int(launches)}
+
+
+def run_cold_shard(a, rank, world):
+    import torch
+    from hotcold_kv_cache_b200 import KVController
+    from hotcold_kv_cache_b200.shard import ShardedColdSearch
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    Hq, Hk, D = 32, 8, 128
+    T, budget, R, layers = a.prompt or 131072, a.budget or 2048, 256, a.layers
+    rot = _rotary(Hq, Hk, D, 500000.0, dev)
+    ctrl = KVController(max_capacity_prompt=budget, topk_ratio=0.0, recent_size=32, cpu_buffer_size=T + 1024,
+                        faiss_dim=128, window_size=1, query_pool_size=8, lookahead_k=R, hold_retrieved=True,
+                        retrieve_after_prefill=False, policy="snapkv", pool_kernel=7, profile_overlap=False)
+    ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
+    ctrl.cold_search = ShardedColdSearch()
+    g = torch.Generator(device=dev).manual_seed(a.seed)  # the same draws on every rank: replicas
+    for li in range(layers):
+        q, qp, k, kp, v, pos = _prefill_inputs(g, Hq, Hk, T, D, dev, rot)
+        if li == 0:
+            ctrl._lazy_init(k, n_layers=layers)
+        ctrl.prefill_layer(li, q, qp, k, kp, v, pos)
+        del q, qp, k, kp, v
+    K, W = a.steps, a.warmup
+    dq = torch.randn((W + K, layers, 1, Hq, D), generator=g, device=dev, dtype=torch.float16)
+    dk = torch.randn((W + K, layers, 1, Hk, D), generator=g, device=dev, dtype=torch.float16)
+    dv = torch.randn((W + K, layers, 1, Hk, D), generator=g, device=dev, dtype=torch.float16)
+    p = torch.arange(T, T + W + K, device=dev)
+    cs, sn = rot(torch.empty(1, dtype=torch.float16, device=dev), p[None])
+    cs, sn = cs[0].contiguous(), sn[0].contiguous()
+    pos = p.view(-1, 1).contiguous()
+
+    def step(i):
+        for li in range(layers):
+            ctrl.decode_layer(li, dq[i, li], dk[i, li], dv[i, li], cs[i:i + 1], sn[i:i + 1], pos[i])
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize(dev)
+    l0 = sum(x.launches for x in ctrl.arenas)
+    times, max_total = _timed_graph_steps(step, W, K, dev, world)
+    launches = sum(x.launches for x in ctrl.arenas) - l0
+    if ctrl.device_status():
+        raise RuntimeError("device status word set")
+    a0 = ctrl.arenas[0]
+    n_cold = int(a0.cold_count[0])
+    value = max_total * 1e3 / (K * layers)
+    return {"metric": "sharded cold store decode: us per layer-step (attn+evict+top-256 search every step)",
+            "value": round(value, 3), "unit": "us/layer-step", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(max_total / K, 4), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic N(0,1) pre-RoPE q/k/v, seeded",
+            "config": {"workload": f"cold-store sharding: {layers} layer(s), {T}-token prompt, budget {budget}, "
+                                   f"top-{R} every step from 8 queries", "cold_entries_per_layer": n_cold,
+                       "index_rows_scanned_per_rank": -(-n_cold // world),
+                       "parallelism": f"cold index by token range over {world} ranks, NCCL all-gather of "
+                                      f"{world}x{R} candidates, decode replicated",
+                       "l2": "flushed before every timed step"},
+            "gpu_launches": int(launches)}
+
+
+# ------------------------------------------------------------------------------------------
 # CPU arm: the oracle port of the reference path on one layer
 # ------------------------------------------------------------------------------------------
 def cpu_port(c, n_steps, seed):
@@ -545,6 +738,15 @@ def main():
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    if a.workload != "decode":
+        res = run_ragged(a, rank, world) if a.workload == "ragged" else run_cold_shard(a, rank, world)
+        if world > 1:
+            import torch
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(res))
+        return 0
     res = run_ours(a, rank, world)
     if rank == 0 and not a.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_obj(config(a), a.cpu_steps, a.seed)

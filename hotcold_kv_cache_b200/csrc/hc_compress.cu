@@ -80,6 +80,7 @@ struct CompressArgs {
   void* qb;        // [n_seq][Hk][32][D] GQA-mean observation rows in the model dtype (tensor-core path)
   int tqmax;
   int chunk_len;   // tokens per softmax partial in `part`
+  int vec_ok;      // source rows and strides allow 16-byte copies (evict_kernel)
 };
 
 template <bool DENSE>
@@ -239,7 +240,7 @@ template <int DT, int D, bool DENSE>
 __global__ void snap_qbar_kernel(CompressArgs a) {
   using E = Elem<DT>;
   using T = typename E::T;
-  const int h = blockIdx.x, s = blockIdx.y;
+  const int h = blockIdx.x, s = blockIdx.z, r0 = blockIdx.y * 2;
   const hc_layer& L = a.L;
   pdl_wait();
   const hc_seq_desc d = L.desc[s];
@@ -248,7 +249,7 @@ __global__ void snap_qbar_kernel(CompressArgs a) {
   const int G = L.Hq / L.Hk;
   const T* q = reinterpret_cast<const T*>(a.q_obs) + (size_t)s * a.qs_seq;
   T* out = reinterpret_cast<T*>(a.qb) + ((size_t)s * L.Hk + h) * 32 * D;
-  for (int i = threadIdx.x; i < 32 * D; i += blockDim.x) {
+  for (int i = r0 * D + threadIdx.x; i < (r0 + 2) * D; i += blockDim.x) {
     const int r = i / D, dd = i % D;
     float v = 0.f;
     if (r < tqu) {
@@ -383,24 +384,32 @@ __global__ void __launch_bounds__(kSnapTile, 1) snap_tile_kernel(CompressArgs a)
 // ------------------------------------------------------------------------------------------
 // SnapKV softmax statistics and token scores
 // ------------------------------------------------------------------------------------------
-// Per (head, row): max and sum of exp over the whole sequence from the chunk partials.
+// Per (head, row): max and sum of exp over the whole sequence from the chunk partials. A warp
+// per row; grid (ceil(Hk * tqmax / 8), n_seq) of 256 threads.
 template <bool DENSE>
 __global__ void stats_kernel(CompressArgs a) {
   const hc_layer& L = a.L;
-  const int s = blockIdx.x;
+  const int s = blockIdx.y, lane = threadIdx.x & 31;
   pdl_wait();
   const hc_seq_desc d = L.desc[s];
   const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
   if (!pl.active) return;
   const int tqu = min(pl.nobs, a.tq);
   const int nch = (pl.S + a.chunk_len - 1) / a.chunk_len;
-  for (int i = threadIdx.x; i < L.Hk * tqu; i += blockDim.x) {
-    const int h = i / tqu, r = i % tqu;
-    const float* p = a.part + (((size_t)s * L.Hk + h) * a.tqmax + r) * a.max_chunks * 2;
-    float M = kNegInf;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, p[2 * c]);
-    float S = 0.f;
-    for (int c = 0; c < nch; ++c) S += (p[2 * c] == kNegInf) ? 0.f : p[2 * c + 1] * __expf(p[2 * c] - M);
+  const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= L.Hk * tqu) return;
+  const int h = i / tqu, r = i % tqu;
+  const float2* p = reinterpret_cast<const float2*>(a.part + (((size_t)s * L.Hk + h) * a.tqmax + r) * a.max_chunks * 2);
+  float M = kNegInf;
+  for (int c = lane; c < nch; c += 32) M = fmaxf(M, p[c].x);
+  M = warp_max(M);
+  float S = 0.f;
+  for (int c = lane; c < nch; c += 32) {
+    const float2 q = p[c];
+    S += (q.x == kNegInf) ? 0.f : q.y * __expf(q.x - M);
+  }
+  S = warp_sum(S);
+  if (lane == 0) {
     float* o = a.stats + (((size_t)s * L.Hk + h) * a.tqmax + r) * 2;
     o[0] = M;
     o[1] = S;
@@ -542,6 +551,87 @@ __device__ void evict_one(const CompressArgs& a, const hc_seq_desc& d, int s, in
   }
   if (lane == 0) d.cold_pos[dst] = DENSE ? a.src_pos[(size_t)s * a.S_dense + src] : d.hot_pos[src];
   // index vector (controller.py:178-182): mean over heads, pad/crop to F, L2-normalise
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    mean[i] = mean[i] / (float)L.Hk;
+    const int dd = lane + 32 * i;
+    if (dd < D && dd < L.F) ss += mean[i] * mean[i];
+  }
+  ss = warp_sum(ss);
+  const float den = fmaxf(sqrtf(ss), 1e-12f);
+  float* vec = d.cold_vec + (size_t)dst * L.F;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int dd = lane + 32 * i;
+    if (dd < D && dd < L.F) vec[dd] = L.normalize ? mean[i] / den : mean[i];
+  }
+  for (int f = D + lane; f < L.F; f += 32) vec[f] = 0.f;
+}
+
+// evict_one with 16-byte copies: the payload moves as uint4 chunks (four per lane in flight),
+// the pre-RoPE key rows are staged in this warp's `stage` (Hk * D elements) so that the index
+// vector is summed over heads in the same order as evict_one.
+template <int DT, int D, bool DENSE>
+__device__ void evict_one_vec(const CompressArgs& a, const hc_seq_desc& d, int s, int src, int dst,
+                              typename Elem<DT>::T* stage) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  const hc_layer& L = a.L;
+  const int lane = threadIdx.x & 31;
+  constexpr int PER = (D + 31) / 32;
+  constexpr int CPR = D * (int)sizeof(T) / 16;  // 16-byte chunks per head row
+  if (dst < 0 || dst >= d.ccap || src < 0 || src >= (DENSE ? a.S_dense : d.cap)) {
+    if (lane == 0) set_status(d.st, HC_DEV_INDEX);
+    return;
+  }
+  const int nq = L.Hk * CPR;
+  uint4* ck = reinterpret_cast<uint4*>(reinterpret_cast<T*>(d.cold_kpre) + (size_t)dst * L.Hk * D);
+  uint4* cv = reinterpret_cast<uint4*>(reinterpret_cast<T*>(d.cold_v) + (size_t)dst * L.Hk * D);
+  uint4* st4 = reinterpret_cast<uint4*>(stage);
+  for (int q0 = 0; q0 < nq; q0 += 128) {
+    uint4 kr[4], vr[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = q0 + u * 32 + lane;
+      if (q < nq) {
+        const int h = q / CPR, c = q % CPR;
+        size_t off;
+        const T* kb;
+        const T* vb;
+        if constexpr (DENSE) {
+          off = (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)src * a.ss_tok;
+          kb = reinterpret_cast<const T*>(a.src_kpre);
+          vb = reinterpret_cast<const T*>(a.src_v);
+        } else {
+          off = ((size_t)h * d.cap + src) * D;
+          kb = reinterpret_cast<const T*>(d.hot_kpre);
+          vb = reinterpret_cast<const T*>(d.hot_v);
+        }
+        kr[u] = reinterpret_cast<const uint4*>(kb + off)[c];
+        vr[u] = reinterpret_cast<const uint4*>(vb + off)[c];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = q0 + u * 32 + lane;
+      if (q < nq) {
+        ck[q] = kr[u];
+        cv[q] = vr[u];
+        st4[q] = kr[u];
+      }
+    }
+  }
+  __syncwarp();
+  float mean[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) mean[i] = 0.f;
+  for (int h = 0; h < L.Hk; ++h)
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (lane + 32 * i < D) mean[i] += E::to_f(stage[(size_t)h * D + lane + 32 * i]);
+  __syncwarp();  // the stage is free for the next token
+  if (lane == 0) d.cold_pos[dst] = DENSE ? a.src_pos[(size_t)s * a.S_dense + src] : d.hot_pos[src];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
@@ -768,6 +858,38 @@ __global__ void __launch_bounds__(256) evict_kernel(CompressArgs a) {
   if (!DENSE && n_ev <= kInlineEvict) return;
   const int lane = threadIdx.x & 31;
   const int w0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+  if (a.vec_ok) {
+    extern __shared__ __align__(16) unsigned char evs[];
+    T* stage = reinterpret_cast<T*>(evs) + (size_t)(threadIdx.x >> 5) * L.Hk * D;
+    constexpr int CPR = D * (int)sizeof(T) / 16;
+    for (int item = w0; item < n_keep + n_ev; item += nw) {
+      if (item < n_keep) {
+        if constexpr (DENSE) {
+          const int t = a.keep_src[(size_t)s * a.S_max + item];
+          for (int q = lane; q < L.Hk * CPR; q += 32) {
+            const int h = q / CPR, c = q % CPR;
+            const size_t src = (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)t * a.ss_tok;
+            const size_t dst = ((size_t)h * d.cap + item) * D;
+            const uint4 kx = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.src_k) + src)[c];
+            const uint4 vx = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.src_v) + src)[c];
+            const uint4 px = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.src_kpre) + src)[c];
+            reinterpret_cast<uint4*>(reinterpret_cast<T*>(d.hot_k) + dst)[c] = kx;
+            reinterpret_cast<uint4*>(reinterpret_cast<T*>(d.hot_v) + dst)[c] = vx;
+            reinterpret_cast<uint4*>(reinterpret_cast<T*>(d.hot_kpre) + dst)[c] = px;
+          }
+          if (lane == 0) {
+            d.hot_pos[item] = a.src_pos[(size_t)s * a.S_dense + t];
+            d.hot_ord[item] = item;
+          }
+        }
+      } else {
+        const int j = item - n_keep;
+        const int dst = a.ev_dst[(size_t)s * a.S_max + j];
+        if (dst >= 0) evict_one_vec<DT, D, DENSE>(a, d, s, a.ev_src[(size_t)s * a.S_max + j], dst, stage);
+      }
+    }
+    return;
+  }
   for (int item = w0; item < n_keep + n_ev; item += nw) {
     if (item < n_keep) {
       if constexpr (DENSE) {
@@ -918,9 +1040,10 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
     e = ensure_smem(k0, tsmem);
     if (e == cudaSuccess) e = ensure_smem(k1, tsmem);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(snap_qbar_kernel<DT, D, DENSE>, dim3(L.Hk, L.n_seq), dim3(256), 0, stream, a);
+    e = launch_pdl(snap_qbar_kernel<DT, D, DENSE>, dim3(L.Hk, 16, L.n_seq), dim3(256), 0, stream, a);
     if (e == cudaSuccess) e = launch_pdl(k0, dim3(tiles, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a);
-    if (e == cudaSuccess) e = launch_pdl(stats_kernel<DENSE>, dim3(L.n_seq), dim3(256), 0, stream, a);
+    if (e == cudaSuccess)
+      e = launch_pdl(stats_kernel<DENSE>, dim3((L.Hk * a.tqmax + 7) / 8, L.n_seq), dim3(256), 0, stream, a);
     if (e == cudaSuccess) e = launch_pdl(k1, dim3(tiles, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a);
     if (e != cudaSuccess) return e;
   } else {
@@ -937,7 +1060,7 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
   if (!small) {
     const int blocks = (int)((S_grid + 255) / 256) < 592 ? (S_grid + 255) / 256 : 592;
     if (snap && !tc) {
-      e = launch_pdl(stats_kernel<DENSE>, dim3(L.n_seq), dim3(256), 0, stream, a);
+      e = launch_pdl(stats_kernel<DENSE>, dim3((L.Hk * a.tqmax + 7) / 8, L.n_seq), dim3(256), 0, stream, a);
       if (e != cudaSuccess) return e;
       const int ib = (int)(((long)L.Hk * S_grid + 255) / 256) < 1184 ? (int)(((long)L.Hk * S_grid + 255) / 256) : 1184;
       e = launch_pdl(imp_kernel<DENSE>, dim3(ib, L.n_seq), dim3(256), 0, stream, a);
@@ -954,9 +1077,16 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
   if (DENSE || n_evict_hint > kInlineEvict) {
     const int items = DENSE ? S_grid : n_evict_hint;
     int blocks = (items + 7) / 8;
-    if (blocks > 296) blocks = 296;
+    if (blocks > 592) blocks = 592;
     if (blocks < 1) blocks = 1;
-    e = launch_pdl(evict_kernel<DT, D, DENSE>, dim3(blocks, L.n_seq), dim3(256), 0, stream, a);
+    const size_t stage = (size_t)8 * L.Hk * D * sizeof(T);
+    if (stage > 96 * 1024) a.vec_ok = 0;
+    auto ek = evict_kernel<DT, D, DENSE>;
+    if (a.vec_ok) {
+      e = ensure_smem(ek, stage);
+      if (e != cudaSuccess) return e;
+    }
+    e = launch_pdl(ek, dim3(blocks, L.n_seq), dim3(256), a.vec_ok ? stage : 0, stream, a);
   }
   return e;
 }
@@ -985,6 +1115,12 @@ cudaError_t launch_compress(const hc_layer& L, const void* q_obs, int64_t qs0, i
   a.max_chunks = (S_grid + 31) / 32;
   a.src_k = sk; a.src_v = sv; a.src_kpre = skp;
   a.ss_seq = ss0; a.ss_head = ss1; a.ss_tok = ss2;
+  {
+    const int esz = L.dtype == HC_F32 ? 4 : 2;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    a.vec_ok = (!dense || (al(sk) && al(sv) && al(skp) && (ss0 * esz) % 16 == 0 && (ss1 * esz) % 16 == 0 &&
+                           (ss2 * esz) % 16 == 0)) ? 1 : 0;
+  }
   a.src_pos = spos;
   a.hdr = reinterpret_cast<int*>(base + lay.hdr);
   a.logits = reinterpret_cast<float*>(base + lay.logits);
