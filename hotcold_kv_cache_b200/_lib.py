@@ -123,7 +123,12 @@ def ptr(t) -> int | None:
 
 
 def stream_of(device) -> int:
+    """The raw handle of the current CUDA stream of `device`."""
     import torch
+    idx = device.index if getattr(device, "index", None) is not None else torch.cuda.current_device()
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 

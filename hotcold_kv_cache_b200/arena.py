@@ -153,6 +153,9 @@ class LayerArena:
         L.rope_scaling = float(self.rope_scaling)
         L.kmaps = self._encode_kmaps()
         self.L = L
+        self._Lref = byref(L)
+        self._caps_np = np.asarray(self.caps, np.int64)
+        self._plan_cache = {}
 
     def _encode_kmaps(self):
         """TMA tensor maps of the hot K slab (all sequences as rows of D, 64-row boxes) and the
@@ -229,6 +232,36 @@ class LayerArena:
     # ------------------------------------------------------------------ helpers
     def _stream(self):
         return _lib.stream_of(self.device)
+
+    def _fast_rows(self, t: torch.Tensor, rows: int):
+        """(tensor, sequence stride) of a (n_seq, rows, D) operand without copies when it is
+        contiguous and 16-byte aligned; else the general _row_major path."""
+        if t.is_contiguous() and t.numel() == self.n_seq * rows * self.D and t.data_ptr() % 16 == 0:
+            return t, rows * self.D
+        return self._row_major(t, rows)
+
+    def _step_plan(self):
+        """Evictions of every sequence when each holds one more token than now (the host
+        mirror of the fused step's compression), cached by the hot lengths: (ev, total,
+        total capped by the cold capacities)."""
+        key = self.n_hot.tobytes()
+        e = self._plan_cache.get(key)
+        if e is None:
+            ev = np.zeros(self.n_seq, np.int64)
+            for s in range(self.n_seq):
+                p = self.plan(s, int(self.n_hot[s]) + 1)
+                if p is not None:
+                    ev[s] = p[0] - p[1]
+            e = (ev, int(ev.sum()), int(np.minimum(ev, np.asarray(self.ccaps)).sum()))
+            if len(self._plan_cache) < 4096:
+                self._plan_cache[key] = e
+        return e
+
+    def _ccaps_arr(self):
+        c = getattr(self, "_ccaps_np", None)
+        if c is None:
+            c = self._ccaps_np = np.asarray(self.ccaps, np.int64)
+        return c
 
     def _row_major(self, t: torch.Tensor, rows: int) -> tuple[torch.Tensor, int]:
         """(n_seq, rows, D) view with contiguous, 16-byte aligned rows; returns (tensor, seq stride)."""
@@ -329,39 +362,41 @@ class LayerArena:
             self._step_ok[key] = ok
         return self._step_ok[key]
 
-    def step(self, q_pre, k_pre, v, cos, sin, pos, use_held: bool, overflow_nan: bool = True):
+    def step(self, q_pre, k_pre, v, cos, sin, pos, use_held: bool, overflow_nan: bool = True, out=None):
         """Fused decode step: append + compression with eviction + attention over [held | hot]
-        in one launch (hc_step). Returns the output (n_seq,Hq,D), or None when the fused
-        kernel does not fit this layer (nothing launched; use append/compress/attend)."""
-        if (self.n_hot + 1 > np.asarray(self.caps)).any() or not self.step_supported(use_held):
+        in one launch (hc_step). Returns (output (n_seq,Hq,D), evicted counts), or None when
+        the fused kernel does not fit this layer (nothing launched; use append/compress/attend).
+        `out`, when given, is a contiguous (n_seq,Hq,D) tensor of the layer dtype to write."""
+        if (self.n_hot >= self._caps_np).any() or not self.step_supported(use_held):
             return None
-        q, qss = self._row_major(q_pre, self.Hq)
-        k, kss = self._row_major(k_pre, self.Hk)
-        vv, vss = self._row_major(v, self.Hk)
+        q, qss = self._fast_rows(q_pre, self.Hq)
+        k, kss = self._fast_rows(k_pre, self.Hk)
+        vv, vss = self._fast_rows(v, self.Hk)
         if vss != kss:
             k, vv = k.contiguous(), vv.contiguous()
             kss = k.stride(0)
-        if cos is not None:
+        if cos is not None and not (cos.is_contiguous() and sin.is_contiguous()
+                                    and cos.numel() == self.n_seq * self.D == sin.numel()):
             cos = cos.reshape(self.n_seq, self.D).contiguous()
             sin = sin.reshape(self.n_seq, self.D).contiguous()
-        rc = _lib.load().hc_step(byref(self.L), ptr(q), qss, ptr(k), ptr(vv), kss, ptr(cos), ptr(sin), ptr(pos),
-                                 1 if use_held else 0, ptr(self.out), 1 if overflow_nan else 0, self._stream())
+        o = self.out if out is None else out
+        rc = _lib.load().hc_step(self._Lref, q.data_ptr(), qss, k.data_ptr(), vv.data_ptr(), kss, ptr(cos), ptr(sin),
+                                 pos.data_ptr(), 1 if use_held else 0, o.data_ptr(), 1 if overflow_nan else 0,
+                                 self._stream())
         if rc == 3:  # HC_ERR_UNSUPPORTED: nothing was launched
             self._step_ok[bool(use_held)] = False
             return None
         if rc != 0:
             raise RuntimeError(f"hc_step failed (code {rc}): {_lib.load().hc_last_error().decode()}")
         self.launches += 1
-        ev = np.zeros(self.n_seq, np.int64)
-        self.n_hot += 1
-        for s in range(self.n_seq):
-            p = self.plan(s, int(self.n_hot[s]))
-            if p is not None:
-                ev[s] = p[0] - p[1]
-        self.n_hot -= ev
-        for s in range(self.n_seq):
-            self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + ev[s])
-        return self.out, ev
+        ev, tot, capped = self._step_plan()
+        self.last_ev = (tot, capped)
+        if tot:
+            self.n_hot += 1 - ev
+            np.minimum(self.cold_count + ev, self._ccaps_arr(), out=self.cold_count)
+        else:
+            self.n_hot += 1
+        return o, ev
 
     def append_rotated(self, k_post, k_pre, v, pos):
         if (self.n_hot + 1 > np.asarray(self.caps)).any():
@@ -480,14 +515,15 @@ class LayerArena:
              self._stream())
         return out
 
-    def attend(self, q_post, cur_pos, use_held: bool, overflow_nan: bool = True):
+    def attend(self, q_post, cur_pos, use_held: bool, overflow_nan: bool = True, out=None):
         nbytes = size("hc_attend_scratch_bytes", byref(self.L))
         ws = self.ws.get(nbytes)
         q = q_post if q_post.is_contiguous() else q_post.contiguous()
-        call("hc_attend", byref(self.L), ptr(q), ptr(cur_pos), 1 if use_held else 0, ptr(self.out),
+        o = self.out if out is None else out
+        call("hc_attend", byref(self.L), ptr(q), ptr(cur_pos), 1 if use_held else 0, ptr(o),
              1 if overflow_nan else 0, ptr(ws), ws.numel(), self._stream())
         self.launches += 1
-        return self.out
+        return o
 
     def cold_append(self, k_pre, v, pos, evicted_idx):
         """Evicted tokens (n_seq,Hk,Te,D) into the cold ring (controller.py:190-238)."""

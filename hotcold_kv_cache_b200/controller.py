@@ -221,7 +221,16 @@ class KVController:
             return 0
         return int(self.arenas[int(layer_idx)].cold_count.sum())
 
-    def _count_eviction(self, ev: np.ndarray):
+    def _count_eviction(self, ev: np.ndarray, totals=None):
+        """dbg counters of one compression; `totals` = (evicted, evicted capped by the cold
+        capacities) when the caller has them."""
+        if totals is not None:
+            tot, capped = totals
+            if tot:
+                self.dbg["compress_calls"] += 1
+                self.dbg["evicted_tokens"] += tot
+                self.dbg["faiss_add"] += capped
+            return
         if int(ev.max(initial=0)) > 0:
             self.dbg["compress_calls"] += 1
             self.dbg["evicted_tokens"] += int(ev.sum())
@@ -461,18 +470,19 @@ class KVController:
             self.launch_retrieval_now(li, torch.cat([tails[b] for b in range(self.B)], 0))
         self._tails[li] = {}
 
-    def decode_layer(self, layer_idx: int, q_pre, k_pre, v, cos, sin, pos):
+    def decode_layer(self, layer_idx: int, q_pre, k_pre, v, cos, sin, pos, out=None):
         """One decode step of one layer (patch.py:151-315): RoPE + append + query-pool push,
         scheduled retrieval into the held segment, compression with eviction, and
         attention over [held | hot]. q_pre (B,Hq,D), k_pre/v (B,Hk,D), cos/sin (B,D) in the
-        model dtype or None, pos (B,) int64 on the device. Returns (B,Hq,D)."""
+        model dtype or None, pos (B,) int64 on the device. Returns (B,Hq,D): `out` when given
+        (a contiguous tensor of that shape and the model dtype), else the layer's own buffer."""
         li = int(layer_idx)
         a = self.arena(li, q_pre.shape[1], k_pre.dtype, k_pre.device)
         hook = self.op_hook or (lambda name, phase: None)
         if self.fused_step:
-            out = self._decode_fused(li, a, hook, q_pre, k_pre, v, cos, sin, pos)
-            if out is not None:
-                return out
+            res = self._decode_fused(li, a, hook, q_pre, k_pre, v, cos, sin, pos, out)
+            if res is not None:
+                return res
         hook("append", "begin")
         q_post = a.append(q_pre, k_pre, v, cos, sin, pos)
         hook("append", "end")
@@ -488,11 +498,11 @@ class KVController:
         self._count_injection(a, use_held)
         self.dbg["triton_decode_calls"] += 1
         hook("attend", "begin")
-        out = a.attend(q_post, pos, use_held, self.overflow_nan)
+        res = a.attend(q_post, pos, use_held, self.overflow_nan, out=out)
         hook("attend", "end")
-        return out
+        return res
 
-    def _decode_fused(self, li, a, hook, q_pre, k_pre, v, cos, sin, pos):
+    def _decode_fused(self, li, a, hook, q_pre, k_pre, v, cos, sin, pos, out=None):
         """The decode step as one hc_step launch, preceded on search steps by one fused
         retrieval launch whose pooled query takes this step's q_pre as the newest entry (its
         query-pool push happens inside hc_step). Returns None, with nothing launched and no
@@ -518,7 +528,7 @@ class KVController:
             self._staged[li] = True
         use_held = self._poll_use_held(li)
         hook("step", "begin")
-        res = a.step(q_pre, k_pre, v, cos, sin, pos, use_held, self.overflow_nan)
+        res = a.step(q_pre, k_pre, v, cos, sin, pos, use_held, self.overflow_nan, out=out)
         hook("step", "end")
         if res is None:
             self._undo_poll(li, use_held)
@@ -528,11 +538,11 @@ class KVController:
         self._qpool[li].append(1)
         if not fires:
             self.maybe_launch_async_retrieval(li)  # counts the call; no search fires here
-        out, ev = res
-        self._count_eviction(ev)
+        o, ev = res
+        self._count_eviction(ev, a.last_ev)
         self._count_injection(a, use_held)
         self.dbg["triton_decode_calls"] += 1
-        return out
+        return o
 
     def _poll_peek(self, li: int, staged_now: bool) -> bool:
         """Whether this step attends the held segment (what _poll_use_held will return),
@@ -553,7 +563,8 @@ class KVController:
     def _poll_use_held(self, li: int) -> bool:
         """patch.py:241-261: attend the retrieved set staged since the last step (and keep it
         when holding), or the held set."""
-        self._poll_undo = (self._staged[li], self._held_active[li], dict(self.dbg))
+        self._poll_undo = (self._staged[li], self._held_active[li], self.dbg["prefetch_ready"],
+                           self.dbg["injection_new"])
         use_held = False
         if self._staged[li]:
             self._staged[li] = False
@@ -569,7 +580,8 @@ class KVController:
         return use_held
 
     def _undo_poll(self, li: int, use_held: bool):
-        self._staged[li], self._held_active[li], self.dbg = self._poll_undo
+        self._staged[li], self._held_active[li], pr, inj = self._poll_undo
+        self.dbg["prefetch_ready"], self.dbg["injection_new"] = pr, inj
 
     def _count_injection(self, a, use_held: bool):
         self.last_injected_len = a.r_max if use_held else 0

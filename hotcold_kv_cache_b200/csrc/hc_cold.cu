@@ -176,47 +176,70 @@ __global__ void __launch_bounds__(1024) pick_kernel(RetrieveArgs a) {
 // Held slot j <- hit j: RoPE of the pre-RoPE key at its position (patch.py:94-102 with HF's
 // LlamaRotaryEmbedding and apply_rotary_pos_emb, rounded in the model dtype), value, position,
 // valid flag; slots past the hits are zero and invalid (controller.py:259-262).
-// Grid (ceil(max_r/8), n_seq), a warp per slot.
+// Grid (max_r, n_seq), one CTA of kSpliceThreads per slot: the hit's D/2 cos/sin pairs once in
+// shared memory, then 16-byte chunks of every head's key (with the rotate-half partner chunk)
+// and value.
+constexpr int kSpliceThreads = 128;
+
 template <int DT, int D>
-__global__ void __launch_bounds__(256) splice_kernel(RetrieveArgs a) {
+__global__ void __launch_bounds__(kSpliceThreads) splice_kernel(RetrieveArgs a) {
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int H = D / 2;
+  constexpr int VEC = 16 / (int)sizeof(T);
+  constexpr int CPR = D / VEC;  // 16-byte chunks per head row
+  __shared__ float scs[2 * H];
   const hc_layer& L = a.L;
-  const int s = blockIdx.y;
+  const int j = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
   pdl_wait();
   const hc_seq_desc d = L.desc[s];
-  const int j = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (j >= d.r_max) return;
   const int phys = d.held_src[j];
-  T* hk = reinterpret_cast<T*>(d.held_k);
-  T* hv = reinterpret_cast<T*>(d.held_v);
+  uint4* hk = reinterpret_cast<uint4*>(d.held_k);
+  uint4* hv = reinterpret_cast<uint4*>(d.held_v);
+  const int nq = L.Hk * CPR;
   if (phys < 0 || phys >= d.ccap) {
-    for (int h = 0; h < L.Hk; ++h)
-      for (int dd = lane; dd < D; dd += 32) {
-        hk[((size_t)h * d.r_max + j) * D + dd] = E::from_f(0.f);
-        hv[((size_t)h * d.r_max + j) * D + dd] = E::from_f(0.f);
-      }
-    if (lane == 0) {
+    for (int q = tid; q < nq; q += kSpliceThreads) {
+      const int h = q / CPR, c = q % CPR;
+      const size_t o = ((size_t)h * d.r_max + j) * CPR + c;
+      hk[o] = make_uint4(0u, 0u, 0u, 0u);
+      hv[o] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (tid == 0) {
       d.held_pos[j] = 0;
       d.held_valid[j] = 0;
     }
     return;
   }
   const int64_t p = d.cold_pos[phys];
-  const T* ck = reinterpret_cast<const T*>(d.cold_kpre) + (size_t)phys * L.Hk * D;
-  const T* cv = reinterpret_cast<const T*>(d.cold_v) + (size_t)phys * L.Hk * D;
-  for (int dd = lane; dd < D; dd += 32) {
+  for (int i = tid; i < H; i += kSpliceThreads) {
     float c, sn;
-    rope_cs<DT>(L.inv_freq[dd % H], p, L.rope_scaling, c, sn);
-    for (int h = 0; h < L.Hk; ++h) {
-      const float x = E::to_f(ck[(size_t)h * D + dd]);
-      const float r = dd < H ? -E::to_f(ck[(size_t)h * D + dd + H]) : E::to_f(ck[(size_t)h * D + dd - H]);
-      hk[((size_t)h * d.r_max + j) * D + dd] = E::from_f(rope_elem<DT>(x, r, c, sn));
-      hv[((size_t)h * d.r_max + j) * D + dd] = cv[(size_t)h * D + dd];
-    }
+    rope_cs<DT>(L.inv_freq[i], p, L.rope_scaling, c, sn);
+    scs[i] = c;
+    scs[H + i] = sn;
   }
-  if (lane == 0) {
+  __syncthreads();
+  const uint4* ck = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(d.cold_kpre) + (size_t)phys * L.Hk * D);
+  const uint4* cv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(d.cold_v) + (size_t)phys * L.Hk * D);
+  for (int q = tid; q < nq; q += kSpliceThreads) {
+    const int h = q / CPR, c = q % CPR;
+    const int cp = c < CPR / 2 ? c + CPR / 2 : c - CPR / 2;  // chunk of the rotate-half partner dims
+    const uint4 xv = ck[(size_t)h * CPR + c], rv = ck[(size_t)h * CPR + cp], vv = cv[(size_t)h * CPR + c];
+    const T* x = reinterpret_cast<const T*>(&xv);
+    const T* r = reinterpret_cast<const T*>(&rv);
+    uint4 ov;
+    T* o = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const int dd = c * VEC + e;
+      const float rot = dd < H ? -E::to_f(r[e]) : E::to_f(r[e]);
+      o[e] = E::from_f(rope_elem<DT>(E::to_f(x[e]), rot, scs[dd % H], scs[H + dd % H]));
+    }
+    const size_t off = ((size_t)h * d.r_max + j) * CPR + c;
+    hk[off] = ov;
+    hv[off] = vv;
+  }
+  if (tid == 0) {
     d.held_pos[j] = p;
     d.held_valid[j] = 1;
   }
@@ -925,7 +948,7 @@ static cudaError_t retrieve_t(RetrieveArgs a, int max_count, cudaStream_t stream
   if (e != cudaSuccess) return e;
   e = launch_pdl(pick_kernel, dim3(L.n_seq), dim3(1024), 0, stream, a);
   if (e != cudaSuccess) return e;
-  return launch_pdl(splice_kernel<DT, D>, dim3((L.max_r + 7) / 8, L.n_seq), dim3(256), 0, stream, a);
+  return launch_pdl(splice_kernel<DT, D>, dim3(max(L.max_r, 1), L.n_seq), dim3(kSpliceThreads), 0, stream, a);
 }
 
 cudaError_t launch_retrieve(const hc_layer& L, const void* qd, int64_t q0, int64_t q1, int64_t q2, int P, int n_pool,
@@ -1006,7 +1029,7 @@ static cudaError_t splice_hits_t(RetrieveArgs a, const int32_t* hit_ids, int k, 
   const hc_layer& L = a.L;
   cudaError_t e = launch_pdl(hits_kernel, dim3(L.n_seq), dim3(256), 0, stream, L, hit_ids, k);
   if (e != cudaSuccess) return e;
-  return launch_pdl(splice_kernel<DT, D>, dim3((L.max_r + 7) / 8, L.n_seq), dim3(256), 0, stream, a);
+  return launch_pdl(splice_kernel<DT, D>, dim3(max(L.max_r, 1), L.n_seq), dim3(kSpliceThreads), 0, stream, a);
 }
 
 template <int DT, int D>

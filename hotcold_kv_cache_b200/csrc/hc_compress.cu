@@ -768,6 +768,73 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
     sel = sSel;
   }
 
+  // one eviction from the slab (the decode steady state): the lowest-scoring prefix token,
+  // the higher index among equal scores (the top-k keeps the lower one), then the order table
+  // shifts down by one past it. Same result as the top-k + compaction below.
+  if (!DENSE && pl.prefix - pl.ntop == 1 && S <= 8 * (int)blockDim.x) {
+    __shared__ unsigned long long s_min[32];
+    unsigned long long m = ~0ull;
+    for (int t = tid; t < pl.prefix; t += blockDim.x) {
+      const unsigned long long k = ((unsigned long long)fkey(tok[t]) << 32) | (0xffffffffu - (uint32_t)t);
+      m = k < m ? k : m;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, m, o);
+      m = y < m ? y : m;
+    }
+    if ((tid & 31) == 0) s_min[tid >> 5] = m;
+    __syncthreads();
+    if (tid < 32) {
+      unsigned long long x = tid < (int)(blockDim.x >> 5) ? s_min[tid] : ~0ull;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long y = __shfl_xor_sync(0xffffffffu, x, o);
+        x = y < x ? y : x;
+      }
+      if (tid == 0) s_min[0] = x;
+    }
+    __syncthreads();
+    const int e = (int)(0xffffffffu - (uint32_t)(s_min[0] & 0xffffffffu));
+    const int phys_e = d.hot_ord[e];
+    int vals[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = e + tid + j * (int)blockDim.x;
+      if (t < S - 1) vals[j] = d.hot_ord[t + 1];
+    }
+    __syncthreads();  // every read of the order table is done
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = e + tid + j * (int)blockDim.x;
+      if (t < S - 1) d.hot_ord[t] = vals[j];
+    }
+    const int ccap = d.ccap, cold_head = st->cold_head, cold_count = st->cold_count, n_free0 = st->n_free;
+    const int dst = (int)(((long)cold_head + cold_count) % ccap);
+    __syncthreads();  // every thread has read the counters before thread 0 updates them
+    if (tid == 0) {
+      a.ev_src[(size_t)s * a.S_max] = phys_e;
+      a.ev_dst[(size_t)s * a.S_max] = dst;
+      if (n_free0 < d.cap) d.hot_free[n_free0] = phys_e;
+      const long total = (long)cold_count + 1;
+      if (total > ccap) {
+        st->cold_head = (int)(((long)cold_head + total - ccap) % ccap);
+        st->cold_count = ccap;
+      } else {
+        st->cold_count = (int)total;
+      }
+      st->n_evict = 1;
+      st->n_hot = S - 1;
+      st->n_free = n_free0 + 1;
+      hdr[0] = S;
+      hdr[4] = 1;
+      hdr[5] = 0;
+      hdr[6] = 1;
+    }
+    if (tid < 32) evict_one<DT, D, false>(a, d, s, phys_e, dst);
+    return;
+  }
+
   // exact top-n_top of the prefix
   block_topk_flags([&](int i) { return tok[i]; }, pl.prefix, pl.ntop, sel, sh);
 

@@ -5,7 +5,11 @@
 // budget + 1 physical slots; a new token takes a slot from the free-slot stack and
 // its logical position is recorded in hot_ord, so an append writes one token.
 
+#include <cooperative_groups.h>
+
 #include "hc_common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace hc {
 
@@ -230,24 +234,58 @@ __global__ void store_prompt_kernel(hc_layer L, int S, const void* sk, const voi
 }
 
 // Sum over prompt positions of the head-mean pre-RoPE query (each mean rounded to the
-// model dtype, as torch's mean over heads returns that dtype), fp32 (n_seq, D).
+// model dtype, as torch's mean over heads returns that dtype), fp32 (n_seq, D). One cluster
+// of kPqsCluster CTAs per sequence; thread group g of CTA r sums positions
+// G, G + NG, G + 2 NG, ... (G = r * groups + g, NG = all groups), then the groups and the CTAs
+// are added in a fixed order (deterministic).
+constexpr int kPqsCluster = 8;
+constexpr int kPqsThreads = 1024;
+
 template <int DT, int D>
-__global__ void prompt_query_sum_kernel(hc_layer L, const void* q_, int64_t qs, int64_t qh, int64_t qt, int P,
-                                        float* out) {
+__global__ void __launch_bounds__(kPqsThreads) prompt_query_sum_kernel(hc_layer L, const void* q_, int64_t qs,
+                                                                       int64_t qh, int64_t qt, int P, float* out) {
   using E = Elem<DT>;
   using T = typename E::T;
-  const int s = blockIdx.x;
+  constexpr int GROUPS = kPqsThreads / D;
+  __shared__ float part[GROUPS][D];
+  __shared__ float cta[D];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int s = blockIdx.y, g = threadIdx.x / D, dd = threadIdx.x % D;
   pdl_wait();
-  for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
-    float tot = 0.f;
-    for (int p = 0; p < P; ++p) {
-      float acc = 0.f;
-      for (int h = 0; h < L.Hq; ++h)
-        acc += E::to_f(reinterpret_cast<const T*>(q_)[(size_t)s * qs + (size_t)h * qh + (size_t)p * qt + dd]);
-      tot += E::round(acc / (float)L.Hq);
+  const T* q = reinterpret_cast<const T*>(q_) + (size_t)s * qs + dd;
+  const int NG = GROUPS * kPqsCluster;
+  float tot = 0.f;
+  for (int p = rank * GROUPS + g; p < P; p += NG) {
+    // heads in groups of 8: the loads of a group are in flight together, the sum keeps the
+    // head order
+    const T* qp = q + (size_t)p * qt;
+    float acc = 0.f;
+    int h = 0;
+    for (; h + 8 <= L.Hq; h += 8) {
+      T x[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x[u] = qp[(size_t)(h + u) * qh];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc += E::to_f(x[u]);
     }
-    out[(size_t)s * D + dd] = tot;
+    for (; h < L.Hq; ++h) acc += E::to_f(qp[(size_t)h * qh]);
+    tot += E::round(acc / (float)L.Hq);
   }
+  part[g][dd] = tot;
+  __syncthreads();
+  if (g == 0) {
+    float t = 0.f;
+    for (int j = 0; j < GROUPS; ++j) t += part[j][dd];
+    cta[dd] = t;
+  }
+  cluster.sync();
+  if (rank == 0 && g == 0) {
+    float t = 0.f;
+    for (int r = 0; r < kPqsCluster; ++r) t += cluster.map_shared_rank(cta, r)[dd];
+    out[(size_t)s * D + dd] = t;
+  }
+  cluster.sync();  // CTA 0 has read every CTA's sum
 }
 
 template <int DT, int D>
@@ -285,7 +323,19 @@ cudaError_t launch_store_prompt(const hc_layer& L, int S, const void* a, const v
 template <int DT, int D>
 static cudaError_t pqs_t(const hc_layer& L, const void* q, int64_t a, int64_t b, int64_t c, int P, float* out,
                          cudaStream_t st) {
-  return launch_pdl(prompt_query_sum_kernel<DT, D>, dim3(L.n_seq), dim3(D), 0, st, L, q, a, b, c, P, out);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kPqsCluster, L.n_seq);
+  cfg.blockDim = dim3(kPqsThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kPqsCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prompt_query_sum_kernel<DT, D>, L, q, a, b, c, P, out);
 }
 cudaError_t launch_prompt_query_sum(const hc_layer& L, const void* q, int64_t a, int64_t b, int64_t c, int P,
                                     float* out, cudaStream_t st) {
