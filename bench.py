@@ -26,9 +26,13 @@ Two more workloads (--workload), measured on request and not part of the default
               from 8 query states every step, the cold index scanned by token range over the
               N ranks and the candidates merged after an NCCL all-gather; every rank runs the
               same decode. value = us per layer-step.
+  prefill     SnapKV compression of one layer's prompt (window 32, max-pool 7, budget 512,
+              fp16, 32/8 heads) with eviction of the rest into the cold ring: the prompt-side
+              use of the scoring kernels (tcgen05 observation x prefix product). value = us per
+              prompt-layer; also the scoring's algorithmic TFLOP/s.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                       [--workload decode|ragged|cold-shard]
+                       [--workload decode|ragged|cold-shard|prefill]
 """
 
 from __future__ import annotations
@@ -65,7 +69,7 @@ def parse():
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--cpu-steps", type=int, default=16)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="decode", choices=["decode", "ragged", "cold-shard"])
+    p.add_argument("--workload", default="decode", choices=["decode", "ragged", "cold-shard", "prefill"])
     p.add_argument("--seqs", type=int, default=64)
     return p.parse_args()
 
@@ -391,13 +395,12 @@ def run_ours(a, rank, world):
     return res
 
 
-def per_op_live(wl, start, n, dev):
+def op_times(ctrl, step_fn, start, n, dev):
     """Device time of each op of a layer-step inside captured decode steps: event nodes
     (cudaEventRecordExternal) bracket every op of every layer, the graph is uploaded, L2 is
-    flushed, the step is replayed once. Returns per-op medians over the layer-steps where the
-    op launched kernels, with the op's algorithmic bytes and GB/s."""
+    flushed, the step is replayed once. Returns {op: [us of each layer-step where the op
+    launched kernels]}."""
     import torch
-    ctrl, c = wl.ctrl, wl.c
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.Stream(dev)
     cur = torch.cuda.current_stream(dev)
@@ -422,7 +425,7 @@ def per_op_live(wl, start, n, dev):
         try:
             with torch.cuda.stream(stream):
                 with torch.cuda.graph(g, stream=stream):
-                    wl.step(i)
+                    step_fn(i)
         finally:
             ctrl.op_hook = None
         graph_upload(g, cur)
@@ -434,6 +437,17 @@ def per_op_live(wl, start, n, dev):
                 rec[name].append(pool.elapsed_us(a, b))
         pool.close()
         del g
+    return rec
+
+
+def ops_median(rec):
+    return {k: round(float(np.median(v)), 3) for k, v in rec.items() if v}
+
+
+def per_op_live(wl, start, n, dev):
+    """op_times over the decode workload, with each op's algorithmic bytes and GB/s."""
+    ctrl, c = wl.ctrl, wl.c
+    rec = op_times(ctrl, wl.step, start, n, dev)
     Hk, D, R, Hq = c["Hk"], c["D"], c["lookahead_k"], c["Hq"]
     a = ctrl.arenas[0]
     n_hot, n_cold = int(a.n_hot[0]), int(a.cold_count[0])
@@ -600,6 +614,7 @@ def run_ragged(a, rank, world):
     l0 = a0.launches
     times, max_total = _timed_graph_steps(step, W, K, dev, world)
     launches = a0.launches - l0
+    ops = ops_median(op_times(ctrl, step, W + K - 2, 2, dev)) if K >= 2 else {}
     if ctrl.device_status():
         raise RuntimeError("device status word set")
     units = len(items) * K
@@ -619,7 +634,7 @@ def run_ragged(a, rank, world):
                        "seqs_this_rank": n, "tokens_this_rank": int(sum(items[i][0] for i in mine)),
                        "partition": "balanced token count (LPT)", "parallelism": f"sequences over {world} ranks",
                        "l2": "flushed before every timed step"},
-            "aggregate_hbm_gbs": round(gbs, 1), "gpu_launches": int(launches)}
+            "aggregate_hbm_gbs": round(gbs, 1), "gpu_launches": int(launches), "ops_us_per_step": ops}
 
 
 def run_cold_shard(a, rank, world):
@@ -662,6 +677,7 @@ def run_cold_shard(a, rank, world):
     l0 = sum(x.launches for x in ctrl.arenas)
     times, max_total = _timed_graph_steps(step, W, K, dev, world)
     launches = sum(x.launches for x in ctrl.arenas) - l0
+    ops = ops_median(op_times(ctrl, step, W + K - 2, 2, dev)) if K >= 2 else {}
     if ctrl.device_status():
         raise RuntimeError("device status word set")
     a0 = ctrl.arenas[0]
@@ -677,7 +693,50 @@ def run_cold_shard(a, rank, world):
                        "parallelism": f"cold index by token range over {world} ranks, NCCL all-gather of "
                                       f"{world}x{R} candidates, decode replicated",
                        "l2": "flushed before every timed step"},
-            "gpu_launches": int(launches)}
+            "gpu_launches": int(launches), "ops_us_per_layer_step": ops}
+
+
+def run_prefill(a, rank, world):
+    import torch
+    from hotcold_kv_cache_b200 import KVController
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    Hq, Hk, D, W = 32, 8, 128, 32
+    T, budget = a.prompt or 8192, a.budget or 512
+    rot = _rotary(Hq, Hk, D, 500000.0, dev)
+    ctrl = KVController(max_capacity_prompt=budget, topk_ratio=0.0, recent_size=W, cpu_buffer_size=T,
+                        faiss_dim=128, window_size=1 << 20, query_pool_size=8, lookahead_k=64, hold_retrieved=True,
+                        retrieve_after_prefill=False, policy="snapkv", pool_kernel=7, profile_overlap=False)
+    ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
+    g = torch.Generator(device=dev).manual_seed(a.seed + rank)
+    q, qp, k, kp, v, pos = _prefill_inputs(g, Hq, Hk, T, D, dev, rot)
+    ctrl._lazy_init(k, n_layers=1)
+    ctrl.prefill_layer(0, q, qp, k, kp, v, pos)
+    ar = ctrl.arenas[0]
+    q_obs = qp[:, :, -W:, :]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    l0 = ar.launches
+    times = []
+    for i in range(a.warmup + a.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ar.compress_prompt(q_obs, kp, v, k, pos)  # the whole prompt again, from an empty slab
+        e1.record()
+        e1.synchronize()
+        if i >= a.warmup:
+            times.append(e0.elapsed_time(e1) * 1e3)
+    us = float(statistics.median(times))
+    flops = 2.0 * Hk * W * T * D
+    kv_bytes = 3.0 * Hk * T * D * 2  # k_post scored, k_pre and v of every token copied once
+    return {"metric": "SnapKV prompt compression: us per prompt-layer (score + pool + top-k + evict)",
+            "value": round(us, 2), "unit": "us/prompt-layer", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic N(0,1) pre-RoPE q/k/v, seeded",
+            "config": {"workload": f"{T}-token prompt, 32/8 heads, D 128, window {W}, max-pool 7, budget {budget}",
+                       "l2": "flushed before every timed call"},
+            "scoring_tflops": round(flops / (us * 1e-6) / 1e12, 3),
+            "hbm_gbs": round(kv_bytes / (us * 1e-6) / 1e9, 1)}
 
 
 # ------------------------------------------------------------------------------------------
@@ -744,7 +803,8 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     if a.workload != "decode":
-        res = run_ragged(a, rank, world) if a.workload == "ragged" else run_cold_shard(a, rank, world)
+        run = {"ragged": run_ragged, "cold-shard": run_cold_shard, "prefill": run_prefill}[a.workload]
+        res = run(a, rank, world)
         if world > 1:
             import torch
             torch.distributed.barrier()

@@ -289,6 +289,25 @@ class LayerArena:
             raise ValueError("k_post, v and k_pre must share strides with unit stride over head_dim")
         return st[0], st[1], st[2]
 
+    def hot_dense(self):
+        """The hot tokens of every sequence in logical order as dense (n_seq, Hk, n_hot, D)
+        tensors (k_post, v, k_pre) and positions (n_seq, n_hot); all sequences must hold the
+        same number of tokens. Device gathers, no host synchronisation."""
+        n = int(self.n_hot[0])
+        if (self.n_hot != n).any():
+            raise ValueError("hot_dense needs equal hot lengths")
+        outs = []
+        for name in ("hot_k", "hot_v", "hot_kpre"):
+            t = getattr(self, name)
+            rows = []
+            for s in range(self.n_seq):
+                c = self.caps[s]
+                slab = t[s].reshape(-1)[: self.Hk * c * self.D].view(self.Hk, c, self.D)
+                rows.append(slab.index_select(1, self.hot_ord[s, :n].long()))
+            outs.append(torch.stack(rows, 0))
+        pos = torch.stack([self.hot_pos[s].index_select(0, self.hot_ord[s, :n].long()) for s in range(self.n_seq)], 0)
+        return outs[0], outs[1], outs[2], pos
+
     def _seq_view(self, s: int):
         """hc_layer over sequence s alone: the descriptor array and counters from its entry on,
         n_seq = 1 (every per-sequence buffer is reached through the descriptor)."""
@@ -476,7 +495,7 @@ class LayerArena:
         k = max(self.r_max, 1)
         ids = searcher.search(rows, n, qvec, k)
         call("hc_splice_hits", byref(self.L), ptr(ids), k, self._stream())
-        self.launches += 2 * self.n_seq + self.n_seq + 2
+        self.launches += 2 * self.n_seq + (self.n_seq if searcher.world > 1 else 0) + 2
 
     def _retr_fused(self) -> bool:
         """Whether hc_retrieve runs as the one-launch cluster kernel (its shared memory fits)."""
@@ -542,6 +561,46 @@ class LayerArena:
         return m
 
     # ------------------------------------------------------------------ views (API, not the hot path)
+    # ------------------------------------------------------------------ persistence
+    _STATE_TENSORS = ("hot_k", "hot_v", "hot_kpre", "hot_pos", "hot_ord", "hot_free", "held_k", "held_v",
+                      "held_pos", "held_valid", "held_src", "cold_vec", "cold_kpre", "cold_v", "cold_pos", "qwin",
+                      "st", "counters")
+
+    def state_dict(self, pin: bool = True) -> dict:
+        """The arena's HBM contents and host mirrors, copied to host memory (page-locked when
+        `pin`): the hot slab with its order table and free stack, the held segment, the cold
+        ring (payload, index vectors, positions), the query pool and the device counters.
+        Synchronises the current stream."""
+        out = {"geometry": dict(n_seq=self.n_seq, Hq=self.Hq, Hk=self.Hk, D=self.D, F=self.F,
+                                dtype=str(self.dtype), budgets=list(self.budgets), ccaps=list(self.ccaps),
+                                r_max=self.r_max, p_max=self.p_max, policy=self.policy, recent=self.recent),
+               "caps": list(self.caps), "n_hot": self.n_hot.copy(), "cold_count": self.cold_count.copy()}
+        for name in self._STATE_TENSORS:
+            t = getattr(self, name)
+            h = torch.empty(t.shape, dtype=t.dtype, pin_memory=pin)
+            h.copy_(t, non_blocking=pin)
+            out[name] = h
+        torch.cuda.current_stream(self.device).synchronize()
+        return out
+
+    def load_state_dict(self, sd: dict) -> None:
+        """Restore a state_dict() into this arena (same geometry; the hot slab grows to the
+        saved capacity first). Host-to-device copies on the current stream."""
+        g = sd["geometry"]
+        mine = dict(n_seq=self.n_seq, Hq=self.Hq, Hk=self.Hk, D=self.D, F=self.F, dtype=str(self.dtype),
+                    budgets=list(self.budgets), ccaps=list(self.ccaps), r_max=self.r_max, p_max=self.p_max,
+                    policy=self.policy, recent=self.recent)
+        if g != mine:
+            raise ValueError(f"arena geometry differs: saved {g}, here {mine}")
+        self.ensure_hot_capacity(sd["caps"])
+        if list(self.caps) != list(sd["caps"]):
+            raise ValueError("hot slab capacity differs from the saved one")
+        for name in self._STATE_TENSORS:
+            getattr(self, name).copy_(sd[name], non_blocking=True)
+        self.n_hot[:] = sd["n_hot"]
+        self.cold_count[:] = sd["cold_count"]
+        self._plan_cache = {}
+
     def logical_order(self, s: int) -> torch.Tensor:
         return self.hot_ord[s, : int(self.n_hot[s])].long()
 

@@ -442,6 +442,43 @@ class KVController:
         if self.retrieve_after_prefill:
             self.launch_retrieval_now(li, q_pre[:, :, -self.query_pool_size:, :])
 
+    def prefill_chunk(self, layer_idx: int, q_pre, q_post, k_pre, k_post, v, positions, last: bool):
+        """One chunk of a prompt forwarded in pieces (the reference rejects chunked prefill,
+        patch.py:325-329). The chunk's tokens join the hot tier after the ones already kept;
+        when the tier exceeds the budget it is compressed with the chunk's last recent_size
+        post-RoPE queries as the observation window, evicting into the cold ring. The whole
+        prompt counts as one forward for the retrieval schedule; after the `last` chunk the
+        prompt-end retrieval uses the prompt's last query_pool_size queries. Needs
+        query_pool_size < window_size. A single chunk is prefill_layer. Tensors (B,H,T_c,D);
+        positions (B,T_c)."""
+        li = int(layer_idx)
+        if self.query_pool_size >= self.window_size:
+            raise ValueError("chunked prefill needs query_pool_size < window_size")
+        a = self.arena(li, q_pre.shape[1], k_post.dtype, k_post.device)
+        first = int(a.n_hot.max()) == 0 and int(a.cold_count.max()) == 0
+        if first:
+            self.maybe_launch_async_retrieval(li)  # the prompt's forward, counted once
+        r = self.recent_size
+        T = int(k_post.shape[2])
+        q_obs = q_post if T <= r else q_post[:, :, -r:, :]
+        pos = positions.to(k_post.device, torch.int64)
+        if first:
+            ev = a.compress_prompt(q_obs, k_post, v, k_pre, pos)
+        else:
+            hk, hv, hp, hpos = a.hot_dense()
+            ev = a.compress_prompt(q_obs, torch.cat([hk, k_post], 2), torch.cat([hv, v], 2),
+                                   torch.cat([hp, k_pre], 2), torch.cat([hpos, pos], 1))
+        self._count_eviction(ev)
+        self.dbg["triton_prefill_fallback"] += 1
+        P = self.query_pool_size
+        tail = self._tails[li].get("chunk")
+        tail = q_pre if tail is None else torch.cat([tail, q_pre], 2)
+        self._tails[li]["chunk"] = tail[:, :, -P:, :] if P > 0 else tail[:, :, :0, :]
+        if last:
+            q_tail = self._tails[li].pop("chunk")
+            if self.retrieve_after_prefill:
+                self.launch_retrieval_now(li, q_tail)
+
     def prefill_sequence(self, layer_idx: int, b: int, q_pre, q_post, k_pre, k_post, v, positions):
         """The prompt forward of sequence b of a ragged batch (set_ragged) in one layer:
         compression of its prompt into its hot slab with eviction into its cold ring (the
@@ -587,6 +624,50 @@ class KVController:
         self.last_injected_len = a.r_max if use_held else 0
         if use_held:
             self.dbg["injection_used"] += 1
+
+    # ------------------------------------------------------------------ persistence
+    def state_dict(self, pin: bool = True) -> dict:
+        """Everything a later process needs to continue decoding from this point: every
+        layer's arena (LayerArena.state_dict, host copies) and the host schedule (step
+        counts, query-pool entries, staged/held flags, the prompt query sums, dbg counters).
+        The result can go through torch.save. Synchronises."""
+        if not self._inited:
+            raise RuntimeError("KVController not initialized")
+        return {
+            "dims": dict(B=self.B, Hk=self.Hk, D=self.D, n_layers=self.n_layers),
+            "seq_budgets": self.seq_budgets, "seq_ccaps": self.seq_ccaps,
+            "arenas": [None if a is None else a.state_dict(pin) for a in self.arenas],
+            "arena_meta": [None if a is None else (a.Hq, str(a.dtype)) for a in self.arenas],
+            "step_count": list(self.step_count),
+            "qpool": [list(q) for q in self._qpool],
+            "prompt_qsum": [None if t is None else t.cpu() for t in self._prompt_qsum],
+            "staged": list(self._staged), "held_active": list(self._held_active),
+            "dbg": dict(self.dbg), "last_injected_len": self.last_injected_len,
+        }
+
+    def load_state_dict(self, sd: dict, device) -> None:
+        """Restore a state_dict() into a controller built with the same settings (and the
+        same rotary parameters) before its first forward."""
+        if self._inited:
+            raise RuntimeError("load_state_dict must come before the first forward")
+        dm = sd["dims"]
+        self.seq_budgets, self.seq_ccaps = sd["seq_budgets"], sd["seq_ccaps"]
+        self._init_dims(dm["B"], dm["Hk"], dm["D"], dm["n_layers"], torch.device(device))
+        dtypes = {str(t): t for t in (torch.float32, torch.float16, torch.bfloat16)}
+        for li, (st, meta) in enumerate(zip(sd["arenas"], sd["arena_meta"])):
+            if st is None:
+                continue
+            a = self.arena(li, meta[0], dtypes[meta[1]], torch.device(device))
+            a.load_state_dict(st)
+        self.step_count = list(sd["step_count"])
+        for li, entries in enumerate(sd["qpool"]):
+            self._qpool[li].clear()
+            self._qpool[li].extend(tuple(e) if isinstance(e, (tuple, list)) else e for e in entries)
+        self._prompt_qsum = [None if t is None else t.to(device) for t in sd["prompt_qsum"]]
+        self._staged = list(sd["staged"])
+        self._held_active = list(sd["held_active"])
+        self.dbg = dict(sd["dbg"])
+        self.last_injected_len = sd["last_injected_len"]
 
     def device_status(self) -> int:
         """OR of the device status words of every layer (synchronises): HC_DEV_* bits."""

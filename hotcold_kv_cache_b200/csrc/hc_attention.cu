@@ -263,17 +263,45 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   __threadfence();
   if (tid == 0) a.counters[(size_t)s * a.Hk + h] = 0;
 
+  // per query head: the overall max and sum from the chunks' (max, sum), a warp per head with
+  // its lanes over the chunks; then every output column as a weighted sum of the partials,
+  // eight chunks' loads in flight per thread
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    float M = kNegInf;
+    for (int cc = lane; cc < n_chunks; cc += 32) M = fmaxf(M, __ldcg(pbase + (size_t)cc * PSTRIDE + G * D + g));
+    M = warp_max(M);
+    float L = 0.f;
+    for (int cc = lane; cc < n_chunks; cc += 32) {
+      const float* pc = pbase + (size_t)cc * PSTRIDE;
+      L = fmaf(__ldcg(pc + G * D + G + g), __expf(__ldcg(pc + G * D + g) - M), L);
+    }
+    L = warp_sum(L);
+    if (lane == 0) {
+      sML[g] = M;
+      sML[G + g] = L;
+    }
+  }
+  __syncthreads();
   if (tid < D) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float M = kNegInf;
-      for (int cc = 0; cc < n_chunks; ++cc) M = fmaxf(M, pbase[(size_t)cc * PSTRIDE + G * D + g]);
-      float L = 0.f, O = 0.f;
-      for (int cc = 0; cc < n_chunks; ++cc) {
+      const float M = sML[g], L = sML[G + g];
+      float O = 0.f;
+      int cc = 0;
+      for (; cc + 8 <= n_chunks; cc += 8) {
+        float x[8], m[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float* pc = pbase + (size_t)(cc + u) * PSTRIDE;
+          x[u] = __ldcg(pc + g * D + tid);
+          m[u] = __ldcg(pc + G * D + g);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) O = fmaf(x[u], __expf(m[u] - M), O);
+      }
+      for (; cc < n_chunks; ++cc) {
         const float* pc = pbase + (size_t)cc * PSTRIDE;
-        const float w = __expf(pc[G * D + g] - M);
-        L = fmaf(pc[G * D + G + g], w, L);
-        O = fmaf(pc[g * D + tid], w, O);
+        O = fmaf(__ldcg(pc + g * D + tid), __expf(__ldcg(pc + G * D + g) - M), O);
       }
       float r = O / L;
       if (a.overflow_nan && M >= kExpOverflow) r = __int_as_float(0x7fc00000);

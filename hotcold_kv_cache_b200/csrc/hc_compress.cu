@@ -702,10 +702,10 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
     float* sStat = sImp + (snap ? (size_t)L.Hk * S : 0);  // rows * 2
     float* sTok = sStat + 2 * rows;        // S
     uint8_t* sSel = reinterpret_cast<uint8_t*>(sTok + S);
-    for (int i = tid; i < rows * S; i += blockDim.x) {
-      const int row = i / S, t = i % S;
+    for (int row = 0; row < rows; ++row) {  // row by row: no division per element
       const size_t g = snap ? (((size_t)s * L.Hk + row / tqu) * a.tqmax + row % tqu) : ((size_t)s * L.Hk + row);
-      sLg[i] = a.logits[g * a.S_max + t];
+      const float* src = a.logits + g * a.S_max;
+      for (int t = tid; t < S; t += blockDim.x) sLg[(size_t)row * S + t] = src[t];
     }
     __syncthreads();
     if (snap) {
@@ -724,16 +724,16 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
         }
       }
       __syncthreads();
-      for (int i = tid; i < L.Hk * S; i += blockDim.x) {
-        const int h = i / S, t = i % S;
-        float acc = 0.f;
-        for (int r = 0; r < tqu; ++r) {
-          const int row = h * tqu + r;
-          const float x = sLg[(size_t)row * S + t];
-          acc += (x == kNegInf) ? 0.f : __expf(x - sStat[2 * row]) / sStat[2 * row + 1];
+      for (int h = 0; h < L.Hk; ++h)
+        for (int t = tid; t < S; t += blockDim.x) {
+          float acc = 0.f;
+          for (int r = 0; r < tqu; ++r) {
+            const int row = h * tqu + r;
+            const float x = sLg[(size_t)row * S + t];
+            acc += (x == kNegInf) ? 0.f : __expf(x - sStat[2 * row]) / sStat[2 * row + 1];
+          }
+          sImp[(size_t)h * S + t] = acc;
         }
-        sImp[i] = acc;
-      }
       __syncthreads();
       const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
       for (int t = tid; t < S; t += blockDim.x) {

@@ -25,26 +25,29 @@ def token_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return rank * n // world, (rank + 1) * n // world
 
 
-def local_topk(index_rows: torch.Tensor, id_base: int, qvec: torch.Tensor, k: int, ws=None):
+def local_topk(index_rows: torch.Tensor, id_base: int, qvec: torch.Tensor, k: int, ws=None, out=None):
     """Exact inner-product top k of index_rows (n, F) fp32 against qvec (F,) fp32, ids
-    id_base + row (hc_cold_topk). Returns (scores (k,) fp32, ids (k,) int32) on the device."""
+    id_base + row (hc_cold_topk). Returns (scores (k,) fp32, ids (k,) int32) on the device,
+    written into `out` = (scores, ids) when given (contiguous views)."""
     dev = qvec.device
     n, F = (int(index_rows.shape[0]), int(index_rows.shape[1])) if index_rows.numel() else (0, int(qvec.numel()))
     if n and (index_rows.stride(1) != 1 or index_rows.stride(0) != F):
         index_rows = index_rows.contiguous()
     nbytes = size("hc_cold_topk_scratch_bytes", n, k)
     scratch = ws.get(nbytes) if ws is not None else torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    sc = torch.empty(k, dtype=torch.float32, device=dev)
-    ids = torch.empty(k, dtype=torch.int32, device=dev)
+    sc, ids = out if out is not None else (torch.empty(k, dtype=torch.float32, device=dev),
+                                           torch.empty(k, dtype=torch.int32, device=dev))
     call("hc_cold_topk", ptr(index_rows) if n else None, n, F, int(id_base), ptr(qvec.contiguous()), int(k), ptr(sc),
          ptr(ids), ptr(scratch), scratch.numel(), _lib.stream_of(dev))
     return sc, ids
 
 
-def merge_candidates(cand_scores: torch.Tensor, cand_ids: torch.Tensor, n_shards: int, k: int):
-    """Global top k of n_shards lists of k (score, id) candidates (hc_shard_merge)."""
+def merge_candidates(cand_scores: torch.Tensor, cand_ids: torch.Tensor, n_shards: int, k: int, out_id=None):
+    """Global top k of n_shards lists of k (score, id) candidates (hc_shard_merge); the ids
+    go to `out_id` (a contiguous (k,) int32 view) when given."""
     dev = cand_scores.device
-    out_id = torch.empty(k, dtype=torch.int32, device=dev)
+    if out_id is None:
+        out_id = torch.empty(k, dtype=torch.int32, device=dev)
     out_sc = torch.empty(k, dtype=torch.float32, device=dev)
     call("hc_shard_merge", ptr(cand_scores.contiguous()), ptr(cand_ids.contiguous()), int(n_shards), int(k),
          ptr(out_id), ptr(out_sc), _lib.stream_of(dev))
@@ -78,9 +81,13 @@ class ShardedColdSearch:
         ids = torch.empty((B, k), dtype=torch.int32, device=dev)
         for b in range(B):
             lo, _ = token_range(int(n[b]), self.rank, self.world)
-            s, i = self.local(rows[b], lo, qvecs[b], k, self.ws) if self.local is local_topk else \
-                self.local(rows[b], lo, qvecs[b], k)
-            sc[b], ids[b] = s, i
+            if self.local is local_topk:
+                local_topk(rows[b], lo, qvecs[b], k, self.ws, out=(sc[b], ids[b]))
+            else:
+                s, i = self.local(rows[b], lo, qvecs[b], k)
+                sc[b], ids[b] = s, i
+        if self.world == 1:
+            return ids  # one range: its top k, sorted with ties to the lower id, is the answer
         if self.world > 1:
             all_sc = torch.empty((self.world * B, k), dtype=torch.float32, device=dev)
             all_id = torch.empty((self.world * B, k), dtype=torch.int32, device=dev)
@@ -91,5 +98,8 @@ class ShardedColdSearch:
             all_sc, all_id = sc[None], ids[None]
         out = torch.empty((B, k), dtype=torch.int32, device=dev)
         for b in range(B):
-            _, out[b] = self.merge(all_sc[:, b].reshape(-1), all_id[:, b].reshape(-1), self.world, k)
+            if self.merge is merge_candidates:
+                merge_candidates(all_sc[:, b].reshape(-1), all_id[:, b].reshape(-1), self.world, k, out_id=out[b])
+            else:
+                _, out[b] = self.merge(all_sc[:, b].reshape(-1), all_id[:, b].reshape(-1), self.world, k)
         return out

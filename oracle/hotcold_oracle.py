@@ -484,6 +484,51 @@ class OracleLayer:
                 self.dbg["retrieval_launched"] += 1
                 self.dbg["retrieval_launched_prefill"] += 1
 
+    def prefill_chunks(self, q_pre, k_pre, v, bounds):
+        """A prompt forwarded in chunks [bounds[i], bounds[i+1]) (the reference rejects chunked
+        prefill, patch.py:325-329; this is the semantics the CUDA path implements): each
+        chunk's tokens join the hot tier after the ones already kept, and when the hot tier
+        exceeds the budget it is compressed (cache.py:37-128 / the SnapKV composition) with the
+        last recent_size post-RoPE queries of that chunk as the observation window. The whole
+        prompt counts as one forward for the retrieval schedule; the prompt-end retrieval uses
+        the last query_pool_size queries of the prompt. Needs query_pool_size < window_size
+        (prompt queries stay out of the query pool). One chunk equals prefill()."""
+        assert self.query_pool_size < self.window_size
+        q_pre = np.asarray(q_pre, np.float64)
+        k_pre = np.asarray(k_pre, np.float64)
+        v = np.asarray(v, np.float64)
+        B, Hq, T, D = q_pre.shape
+        self.B = B
+        self.cold = [ColdRing(self.ccap) for _ in range(B)]
+        if self.lookahead_k > 0:
+            self.step_count += 1
+            if self.step_count % self.window_size == 0:
+                self.dbg["retrieval_skipped_no_cold"] += 1
+        r = self.pol.recent
+        for c0, c1 in zip(bounds[:-1], bounds[1:]):
+            pos = np.arange(c0, c1, dtype=np.int64)
+            cos, sin = rope_cos_sin(pos, self.inv_freq, self.att_scale, self.dt)
+            q_post = apply_rope(q_pre[:, :, c0:c1], cos, sin, self.dt)
+            k_post = apply_rope(k_pre[:, :, c0:c1], cos, sin, self.dt)
+            if c0 == 0:
+                self.K, self.V, self.Kpre = k_post, v[:, :, c0:c1], k_pre[:, :, c0:c1]
+                self.P = np.broadcast_to(pos, (B, c1 - c0)).copy()
+            else:
+                self.K = np.concatenate([self.K, k_post], 2)
+                self.V = np.concatenate([self.V, v[:, :, c0:c1]], 2)
+                self.Kpre = np.concatenate([self.Kpre, k_pre[:, :, c0:c1]], 2)
+                self.P = np.concatenate([self.P, np.broadcast_to(pos, (B, c1 - c0))], 1)
+            q_obs = q_post if c1 - c0 <= r else q_post[:, :, -r:]
+            self._compress(q_obs, step=0)
+            self.dbg["triton_prefill_fallback"] += 1
+        if self.retrieve_after_prefill and self.lookahead_k > 0:
+            if self.cold_size() == 0:
+                self.dbg["retrieval_skipped_no_cold"] += 1
+            else:
+                self._retrieve(q_pre[:, :, -self.query_pool_size:], step=0)
+                self.dbg["retrieval_launched"] += 1
+                self.dbg["retrieval_launched_prefill"] += 1
+
     def decode(self, q_pre, k_pre, v, step):
         """One decode step (q_len = 1): patch.py:151-315. q_pre (B,Hq,D),
         k_pre/v (B,Hk,D). `step` is 1-based; the position is T-1+step.
@@ -552,11 +597,14 @@ class OracleLayer:
         return [np.array(list(c.pos), np.int64) for c in self.cold]
 
 
-def run_layer(inputs: dict, n_steps: int, **kw):
-    """Drive OracleLayer over `inputs` (synth.layer_inputs layout). Returns
-    (layer, outs (n,B,Hq,D), hot_pos list per step)."""
+def run_layer(inputs: dict, n_steps: int, chunks=None, **kw):
+    """Drive OracleLayer over `inputs` (synth.layer_inputs layout), the prompt whole or in
+    chunks with the given boundaries. Returns (layer, outs (n,B,Hq,D), hot_pos list per step)."""
     layer = OracleLayer(**kw)
-    layer.prefill(inputs["q_pre"], inputs["k_pre"], inputs["v"])
+    if chunks is None:
+        layer.prefill(inputs["q_pre"], inputs["k_pre"], inputs["v"])
+    else:
+        layer.prefill_chunks(inputs["q_pre"], inputs["k_pre"], inputs["v"], chunks)
     T = inputs["q_pre"].shape[2]
     layer.start_decode(T)
     outs, hot = [], []

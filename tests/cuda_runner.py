@@ -30,7 +30,7 @@ def controller_kwargs(case):
                 pool_kernel=c.get("pool_kernel", 7))
 
 
-def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused=True):
+def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused=True, chunks=None):
     """Returns dict(outs (n,B,Hq,D) float64, hot [per-step (B,S) int64], held {step: (pos, valid, k)},
     ctrl). model_cos=True passes HF's cos/sin tables to the append kernel (what the patched
     forward does); False lets the kernel compute them from inv_freq."""
@@ -51,7 +51,12 @@ def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused
     pos = torch.arange(T, device=dev).unsqueeze(0).expand(B, T)
     cos, sin = rot(torch.empty(1, dtype=dt, device=dev), pos)
     q_post, k_post = apply_rotary_pos_emb(q_pre, k_pre, cos, sin)
-    ctrl.prefill_layer(0, q_pre, q_post, k_pre, k_post, v, pos)
+    if chunks is None:
+        ctrl.prefill_layer(0, q_pre, q_post, k_pre, k_post, v, pos)
+    else:
+        for c0, c1 in zip(chunks[:-1], chunks[1:]):
+            ctrl.prefill_chunk(0, q_pre[:, :, c0:c1], q_post[:, :, c0:c1], k_pre[:, :, c0:c1], k_post[:, :, c0:c1],
+                               v[:, :, c0:c1], pos[:, c0:c1], last=c1 == chunks[-1])
     outs, hot, held = [], [], {}
     dq, dk, dv = t(inputs["dq"]), t(inputs["dk"]), t(inputs["dv"])
     for i in range(n_steps):

@@ -169,3 +169,83 @@ def test_snapkv_prompt_scoring_tensor_cores(dtype, D, recent, T):
     near = 2e-3 if dtype == "float16" else 2e-2
     assert _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near) >= 1
     assert res["ctrl"].device_status() == 0
+
+
+def _continue(ctrl, c, inp, i0, n):
+    """Decode steps i0..i0+n-1 of `inp` on an existing controller (as run_cuda_layer does)."""
+    from cuda_runner import TORCH_DT, rotary
+    dev = torch.device("cuda", 0)
+    dt = TORCH_DT[c["dtype"]]
+    rot = rotary(c["Hq"], c["D"], c["theta"], dev)
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x).astype(np.float32)).to(device=dev, dtype=dt)
+    dq, dk, dv = t(inp["dq"]), t(inp["dk"]), t(inp["dv"])
+    outs, hot = [], []
+    for i in range(i0, i0 + n):
+        pd = torch.full((c["B"],), c["T"] + i, device=dev, dtype=torch.long)
+        c1, s1 = rot(torch.empty(1, dtype=dt, device=dev), pd[:, None])
+        o = ctrl.decode_layer(0, dq[i], dk[i], dv[i], c1.reshape(c["B"], c["D"]), s1.reshape(c["B"], c["D"]), pd)
+        outs.append(o.double().cpu().numpy())
+        hot.append(ctrl.arenas[0].hot_positions().cpu().numpy())
+    return outs, hot
+
+
+@pytest.mark.parametrize("dtype", ["float16", "float32"])
+def test_state_dict_resume(dtype, tmp_path):
+    """Save the arena and the schedule mid-decode (through torch.save), restore them into a
+    new controller, and continue: outputs, hot sets and counters match the run that never
+    stopped, bit for bit (retrievals every 3 steps and held segments included)."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import controller_kwargs, rotary, run_cuda_layer
+    from hotcold_kv_cache_b200.controller import KVController
+    c = dict(B=2, Hq=8, Hk=2, D=128, T=400, steps=12, dtype=dtype, policy="snapkv", cap=64, recent=16,
+             topk_ratio=0.0, pool_kernel=7, ccap=500, faiss_dim=128, window_size=3, pool=4, R=12, hold=True,
+             rap=True, theta=500000.0, seed=77)
+    inp = synth.layer_inputs(c["seed"], 2, 8, 2, 128, c["T"], c["steps"], dtype)
+    res = run_cuda_layer(c, inp, 5)
+    ctrl = res["ctrl"]
+    sd = ctrl.state_dict()
+    path = tmp_path / "arena.pt"
+    torch.save(sd, path)
+    outs_a, hot_a = _continue(ctrl, c, inp, 5, 7)
+    dev = torch.device("cuda", 0)
+    ctrl2 = KVController(**controller_kwargs(c))
+    rot = rotary(c["Hq"], c["D"], c["theta"], dev)
+    ctrl2.set_rotary(rot.inv_freq, rot.attention_scaling)
+    ctrl2.load_state_dict(torch.load(path, weights_only=False), dev)
+    outs_b, hot_b = _continue(ctrl2, c, inp, 5, 7)
+    for i in range(7):
+        assert np.array_equal(outs_a[i], outs_b[i]), f"output, step {6 + i}"
+        assert np.array_equal(hot_a[i], hot_b[i]), f"hot set, step {6 + i}"
+    assert ctrl.dbg == ctrl2.dbg
+    assert ctrl2.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype,policy,chunks", [
+    ("float16", "snapkv", [0, 300, 301, 700, 1200]),
+    ("float32", "hotcold", [0, 64, 500, 1200]),
+    ("bfloat16", "snapkv", [0, 1200]),
+])
+def test_chunked_prefill_vs_oracle(dtype, policy, chunks):
+    """A prompt forwarded in chunks (ragged sizes, a one-token chunk, a chunk within the
+    budget): hot sets, cold rings and the decode steps after it against the oracle's chunked
+    prefill; one chunk is the plain prefill."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import cold_positions, run_cuda_layer
+    c = dict(B=2, Hq=8, Hk=2, D=128, T=1200, steps=6, dtype=dtype, policy=policy, cap=128,
+             recent=16 if policy == "snapkv" else 32, topk_ratio=0.0 if policy == "snapkv" else 0.5, pool_kernel=7,
+             ccap=2000, faiss_dim=128, window_size=1 << 20, pool=8, R=16, hold=True, rap=True, theta=500000.0,
+             seed=515)
+    inp = synth.layer_inputs(c["seed"], 2, 8, 2, 128, c["T"], c["steps"], dtype)
+    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], chunks=chunks, **oracle_kwargs(c))
+    res = run_cuda_layer(c, inp, c["steps"], chunks=chunks)
+    near = 1e-4 if dtype == "float32" else 2e-3 if dtype == "float16" else 2e-2
+    steps = _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near)
+    assert steps >= 1
+    if steps == c["steps"]:
+        got = cold_positions(res["ctrl"])
+        want = layer.cold_positions()
+        for b in range(2):
+            assert np.array_equal(np.sort(got[b]), np.sort(want[b])), f"cold ring of sequence {b}"
+        for k, v in layer.dbg.items():
+            assert res["ctrl"].dbg[k] == v, k
+    assert res["ctrl"].device_status() == 0

@@ -54,3 +54,19 @@ def test_balanced_partition():
         assert sorted(i for p in parts for i in p) == list(range(64))
         loads = [sum(items[i][0] + items[i][1] for i in p) for p in parts]
         assert max(loads) - min(loads) <= max(L + b for L, b in items)
+
+
+def test_oracle_chunked_prefill_one_chunk_is_prefill():
+    """The oracle's chunked prefill with one chunk equals its plain prefill."""
+    from oracle import hotcold_oracle as O
+    from golden_cases import oracle_kwargs
+    c = dict(B=1, Hq=4, Hk=2, D=64, T=200, dtype="float32", policy="snapkv", cap=48, recent=8, topk_ratio=0.0,
+             pool_kernel=7, ccap=400, faiss_dim=64, window_size=1 << 20, pool=4, R=8, hold=True, rap=True,
+             theta=500000.0)
+    inp = synth.layer_inputs(3, 1, 4, 2, 64, 200, 3, "float32")
+    a, oa, ha = O.run_layer(inp, 3, **oracle_kwargs(c))
+    b, ob, hb = O.run_layer(inp, 3, chunks=[0, 200], **oracle_kwargs(c))
+    assert np.array_equal(oa, ob) and all(np.array_equal(x, y) for x, y in zip(ha, hb))
+    assert a.dbg == b.dbg
+    d, od, hd = O.run_layer(inp, 3, chunks=[0, 50, 120, 200], **oracle_kwargs(c))
+    assert d.P.shape[1] == a.P.shape[1]  # the same budget is kept either way
