@@ -25,6 +25,8 @@ namespace hc {
 
 
 constexpr int kAttnThreads = 128;
+constexpr int kPipeCH = 64;   // rows per chunk of attn_pipe_kernel
+constexpr int kPipeSub = 4;   // chunks per CTA of attn_pipe_kernel
 
 template <int DT, int D, int G, int CH>
 struct AttnSmem {
@@ -315,6 +317,288 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   pdl_launch_dependents();
 }
 
+// Slab attention for large batches: CTA (c, h, s) covers NSUB consecutive chunks of CH rows
+// ([held | hot] order) with two buffers, so the bulk copies of chunk j + 1 land while chunk j is
+// scored; the softmax is carried across the chunks online (running max, sum and a rescale of
+// the partial output), then the CTA's partial is merged as in attn_kernel.
+template <int DT, int D, int G, int CH>
+struct PipeSmem {
+  using T = typename Elem<DT>::T;
+  static constexpr size_t kOff = 0;                                    // [2][CH][D]
+  static constexpr size_t vOff = kOff + 2 * sizeof(T) * CH * D;        // [2][CH][D]
+  static constexpr size_t qOff = vOff + 2 * sizeof(T) * CH * D;        // [G][D] fp32
+  static constexpr size_t sOff = qOff + sizeof(float) * G * D;         // [G][CH] scores, then p
+  static constexpr size_t mlOff = sOff + sizeof(float) * G * CH;       // running max [G], sum [G], rescale [G]
+  static constexpr size_t validOff = mlOff + sizeof(float) * 3 * G;    // [2][CH]
+  static constexpr size_t barOff = (validOff + sizeof(int) * 2 * CH + 15) & ~size_t(15);  // 4 mbarriers
+  static constexpr size_t miscOff = barOff + 32;
+  static constexpr size_t bytes = miscOff + 16;
+};
+
+template <int DT, int D, int G, int CH, int NSUB>
+__global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  using SM = PipeSmem<DT, D, G, CH>;
+  constexpr int ROWB = D * sizeof(T);
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int NJ = D / (8 * VEC);
+  constexpr int SPAN = CH * NSUB;
+  extern __shared__ __align__(128) unsigned char smem[];
+  T* sK = reinterpret_cast<T*>(smem + SM::kOff);
+  T* sV = reinterpret_cast<T*>(smem + SM::vOff);
+  float* sQ = reinterpret_cast<float*>(smem + SM::qOff);
+  float* sS = reinterpret_cast<float*>(smem + SM::sOff);
+  float* sML = reinterpret_cast<float*>(smem + SM::mlOff);
+  int* sValid = reinterpret_cast<int*>(smem + SM::validOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::barOff);
+  int* sMisc = reinterpret_cast<int*>(smem + SM::miscOff);
+
+  const int c = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  const hc_seq_desc d = a.desc[s];
+  hc_seq_state* st = d.st;
+  const int n_held = a.use_held ? max(0, min(st->held_len, d.r_max)) : 0;
+  const int n_tok = n_held + max(0, min(st->n_hot, d.cap));
+  const int n_chunks = (n_tok + SPAN - 1) / SPAN;
+  if (c >= n_chunks) return;
+  const int base0 = c * SPAN;
+  const int nsub = min(NSUB, (n_tok - base0 + CH - 1) / CH);
+  if (tid == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  if (tid < G) {
+    sML[tid] = kNegInf;
+    sML[G + tid] = 0.f;
+  }
+  __syncthreads();
+
+  // rows of chunk j into buffer j & 1 (an out-of-range slot is reported and read as zeros)
+  auto stage = [&](int j) {
+    const int buf = j & 1;
+    const int t0 = base0 + j * CH, nt = min(CH, n_tok - t0);
+    T* bk = sK + (size_t)buf * CH * D;
+    T* bv = sV + (size_t)buf * CH * D;
+    const T* krow = nullptr;
+    const T* vrow = nullptr;
+    bool copy = false;
+    if (tid < nt) {
+      const int t = t0 + tid;
+      int valid = 1;
+      if (t < n_held) {
+        const size_t off = ((size_t)h * d.r_max + t) * D;
+        krow = reinterpret_cast<const T*>(d.held_k) + off;
+        vrow = reinterpret_cast<const T*>(d.held_v) + off;
+        valid = d.held_valid[t] != 0 && d.held_pos[t] <= a.cur_pos[s];
+        copy = true;
+      } else {
+        const int slot = d.hot_ord[t - n_held];
+        if (slot >= 0 && slot < d.cap) {
+          const size_t off = ((size_t)h * d.cap + slot) * D;
+          krow = reinterpret_cast<const T*>(d.hot_k) + off;
+          vrow = reinterpret_cast<const T*>(d.hot_v) + off;
+          copy = true;
+        } else {
+          valid = 0;
+          set_status(st, HC_DEV_INDEX);
+        }
+      }
+      sValid[buf * CH + tid] = valid;
+    }
+    const int n_copy = __syncthreads_count(copy);
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&bars[2 * buf], (uint32_t)(n_copy * ROWB));
+      mbar_arrive_expect_tx(&bars[2 * buf + 1], (uint32_t)(n_copy * ROWB));
+    }
+    if (copy) {
+      fence_proxy_async_smem();  // this buffer was last read by the generic proxy
+      bulk_g2s(bk + (size_t)tid * D, krow, ROWB, &bars[2 * buf]);
+      bulk_g2s(bv + (size_t)tid * D, vrow, ROWB, &bars[2 * buf + 1]);
+    } else if (tid < nt) {
+      for (int i = 0; i < D; ++i) {
+        bk[(size_t)tid * D + i] = E::from_f(0.f);
+        bv[(size_t)tid * D + i] = E::from_f(0.f);
+      }
+    }
+  };
+  // on a timed-out wait: give every copy still in flight a last bounded wait, then leave
+  auto drain = [&](int j) {
+    if (tid == 0) set_status(st, HC_DEV_TIMEOUT);
+    for (int jj = j; jj < min(nsub, j + 2); ++jj) {
+      const uint32_t ph = (uint32_t)(jj >> 1) & 1u;
+      mbar_wait(&bars[2 * (jj & 1)], ph);
+      mbar_wait(&bars[2 * (jj & 1) + 1], ph);
+    }
+  };
+
+  stage(0);
+  if (nsub > 1) stage(1);
+  const T* qg = reinterpret_cast<const T*>(a.q) + ((size_t)s * a.Hq + (size_t)h * G) * D;
+  for (int i = tid; i < G * D; i += kAttnThreads) sQ[i] = E::to_f(qg[i]);
+  __syncthreads();
+  const int sub = lane & 7, tk = lane >> 3;
+  float qr[G][NJ * VEC];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) qr[g][j * VEC + e] = sQ[g * D + j * 8 * VEC + sub * VEC + e];
+  float o[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) o[g] = 0.f;
+
+  for (int j = 0; j < nsub; ++j) {
+    const int buf = j & 1;
+    const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+    const int nt = min(CH, n_tok - (base0 + j * CH));
+    const T* bk = sK + (size_t)buf * CH * D;
+    const T* bv = sV + (size_t)buf * CH * D;
+    const int* bval = sValid + buf * CH;
+    if (!__syncthreads_and(mbar_wait(&bars[2 * buf], ph))) {
+      drain(j);
+      return;
+    }
+    for (int b4 = warp * 4; b4 < nt; b4 += 16) {
+      const int t = b4 + tk;
+      float acc[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = 0.f;
+      if (t < nt) {
+        const T* row = bk + (size_t)t * D;
+#pragma unroll
+        for (int jj = 0; jj < NJ; ++jj) {
+          uint4 u = *reinterpret_cast<const uint4*>(row + jj * 8 * VEC + sub * VEC);
+          float kf[VEC];
+          unpack16<DT>(u, kf);
+#pragma unroll
+          for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[g] = fmaf(qr[g][jj * VEC + e], kf[e], acc[g]);
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 4);
+        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 2);
+        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
+      }
+      if (sub == 0 && t < nt) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) sS[g * CH + t] = bval[t] ? acc[g] * a.scale : kNegInf;
+      }
+    }
+    __syncthreads();
+    // online softmax: the chunk's probabilities against the running max, and the factor that
+    // rescales what was accumulated before
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+      float mc = kNegInf;
+      for (int t = lane; t < nt; t += 32) mc = fmaxf(mc, sS[g * CH + t]);
+      mc = warp_max(mc);
+      const float m_old = sML[g];
+      const float m_new = fmaxf(m_old, mc);
+      float l = 0.f;
+      for (int t = lane; t < nt; t += 32) {
+        const float x = sS[g * CH + t];
+        const float pr = (x == kNegInf) ? 0.f : __expf(x - m_new);
+        sS[g * CH + t] = pr;
+        l += pr;
+      }
+      l = warp_sum(l);
+      __syncwarp();
+      if (lane == 0) {
+        const float alpha = (m_old == kNegInf) ? 0.f : __expf(m_old - m_new);
+        sML[g] = m_new;
+        sML[G + g] = sML[G + g] * alpha + l;
+        sML[2 * G + g] = alpha;
+      }
+    }
+    if (!__syncthreads_and(mbar_wait(&bars[2 * buf + 1], ph))) {
+      drain(j);
+      return;
+    }
+    if (tid < D) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) o[g] *= sML[2 * G + g];
+      for (int t = 0; t < nt; ++t) {
+        const float vv = E::to_f(bv[(size_t)t * D + tid]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) o[g] = fmaf(sS[g * CH + t], vv, o[g]);
+      }
+    }
+    __syncthreads();  // buffer `buf` and the scores are free
+    if (j + 2 < nsub) stage(j + 2);
+  }
+
+  const size_t head0 = (size_t)s * a.Hq + (size_t)h * G;
+  T* outp = reinterpret_cast<T*>(a.out);
+  if (n_chunks == 1) {
+    if (tid < D) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float r = o[g] / sML[G + g];
+        if (a.overflow_nan && sML[g] >= kExpOverflow) r = __int_as_float(0x7fc00000);
+        outp[(head0 + g) * D + tid] = E::from_f(r);
+      }
+    }
+    pdl_launch_dependents();
+    return;
+  }
+  constexpr int PSTRIDE = G * D + 2 * G;
+  float* pbase = a.part + ((size_t)s * a.Hk + h) * (size_t)a.max_chunks * PSTRIDE;
+  float* mine = pbase + (size_t)c * PSTRIDE;
+  if (tid < D) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) mine[g * D + tid] = o[g];
+  }
+  if (tid < 2 * G) mine[G * D + tid] = sML[tid];
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(&a.counters[(size_t)s * a.Hk + h], 1);
+    sMisc[0] = (prev == n_chunks - 1);
+  }
+  __syncthreads();
+  if (!sMisc[0]) return;
+  __threadfence();
+  if (tid == 0) a.counters[(size_t)s * a.Hk + h] = 0;
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    float M = kNegInf;
+    for (int cc = lane; cc < n_chunks; cc += 32) M = fmaxf(M, __ldcg(pbase + (size_t)cc * PSTRIDE + G * D + g));
+    M = warp_max(M);
+    float L = 0.f;
+    for (int cc = lane; cc < n_chunks; cc += 32) {
+      const float* pc = pbase + (size_t)cc * PSTRIDE;
+      L = fmaf(__ldcg(pc + G * D + G + g), __expf(__ldcg(pc + G * D + g) - M), L);
+    }
+    L = warp_sum(L);
+    __syncwarp();
+    if (lane == 0) {
+      sML[g] = M;
+      sML[G + g] = L;
+    }
+  }
+  __syncthreads();
+  if (tid < D) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float M = sML[g], L = sML[G + g];
+      float O = 0.f;
+      for (int cc = 0; cc < n_chunks; ++cc) {
+        const float* pc = pbase + (size_t)cc * PSTRIDE;
+        O = fmaf(__ldcg(pc + g * D + tid), __expf(__ldcg(pc + G * D + g) - M), O);
+      }
+      float r = O / L;
+      if (a.overflow_nan && M >= kExpOverflow) r = __int_as_float(0x7fc00000);
+      outp[(head0 + g) * D + tid] = E::from_f(r);
+    }
+  }
+  pdl_launch_dependents();
+}
+
 // Second output of the dense drop-in (kernels.py:103,134-137): per token the mean over query
 // heads of softmax probability times sum_d |v_d| / D, rounded to the input dtype; masked
 // tokens contribute exactly 0 (the reference's exp(-1e35)).
@@ -439,9 +723,50 @@ int attn_chunk(int n_seq, int Hk, int max_tokens) {
   return ctas64 < 296 ? 32 : 64;
 }
 
+template <int DT, int D, int G>
+cudaError_t launch_pipe_t(const AttnArgs& a, int n_seq, cudaStream_t stream) {
+  using SM = PipeSmem<DT, D, G, kPipeCH>;
+  auto kern = attn_pipe_kernel<DT, D, G, kPipeCH, kPipeSub>;
+  cudaError_t e = ensure_smem(kern, SM::bytes);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.max_chunks, a.Hk, n_seq);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = SM::bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <int DT, int D>
+cudaError_t launch_pipe_g(const AttnArgs& a, int G, int n_seq, cudaStream_t stream) {
+  switch (G) {
+    case 1: return launch_pipe_t<DT, D, 1>(a, n_seq, stream);
+    case 2: return launch_pipe_t<DT, D, 2>(a, n_seq, stream);
+    case 4: return launch_pipe_t<DT, D, 4>(a, n_seq, stream);
+    case 8: return launch_pipe_t<DT, D, 8>(a, n_seq, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_attention(const AttnArgs& a0, int dtype, int D, int G, int n_seq, int max_tokens, bool dense,
                              cudaStream_t stream) {
   AttnArgs a = a0;
+  const long pipe_ctas = (long)n_seq * a.Hk * ((max_tokens + kPipeCH * kPipeSub - 1) / (kPipeCH * kPipeSub));
+  if (!dense && pipe_ctas >= 2 * 148 && max_tokens > kPipeCH * kPipeSub) {
+    // large slab batches: four chunks per CTA, copies of the next chunk overlapping the math
+    a.max_chunks = (max_tokens + kPipeCH * kPipeSub - 1) / (kPipeCH * kPipeSub);
+#define HC_PIPE(DTV, DV) \
+    if (dtype == DTV && D == DV) return launch_pipe_g<DTV, DV>(a, G, n_seq, stream);
+    HC_PIPE(HC_F32, 128) HC_PIPE(HC_F16, 128) HC_PIPE(HC_BF16, 128)
+    HC_PIPE(HC_F32, 64) HC_PIPE(HC_F16, 64) HC_PIPE(HC_BF16, 64)
+#undef HC_PIPE
+    return cudaErrorInvalidValue;
+  }
   const int CH = attn_chunk(n_seq, a.Hk, max_tokens);
   a.max_chunks = (max_tokens + CH - 1) / CH;
   if (a.max_chunks < 1) a.max_chunks = 1;

@@ -262,28 +262,42 @@ __global__ void snap_qbar_kernel(CompressArgs a) {
   }
 }
 
+// CTA (x, h, s) takes `tpc` consecutive tiles; the keys of tile i + 1 are gathered (cp.async,
+// second buffer) while tile i is multiplied and its epilogue runs. Shared memory, 1024-aligned:
+// two key buffers of PL planes x 128 rows x 128 B, the observation rows (PL x 32 x 128 B), a
+// [128][33] fp32 transpose of the logits (pass 0), the MMA barrier, the TMEM address and the
+// row statistics (pass 1).
+template <int D>
+constexpr size_t snap_tile_smem() {
+  return (size_t)2 * (D / 64) * kSnapTile * 128 + (size_t)(D / 64) * 32 * 128 + (size_t)kSnapTile * 33 * 4 + 8 +
+         16 + 256 + 1024;
+}
+
 template <int DT, int D, bool DENSE, int PASS>
-__global__ void __launch_bounds__(kSnapTile, 1) snap_tile_kernel(CompressArgs a) {
+__global__ void __launch_bounds__(kSnapTile, 1) snap_tile_kernel(CompressArgs a, int tpc) {
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int PL = D / 64;  // 128-byte planes of a row
+  constexpr uint32_t KBUF = PL * kSnapTile * 128;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  unsigned char* sK = smem;                                   // PL x 128 rows x 128 B
-  unsigned char* sQ = smem + PL * kSnapTile * 128;            // PL x 32 rows x 128 B
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sQ + PL * 32 * 128);
+  unsigned char* sK = smem;                       // 2 buffers of PL x 128 rows x 128 B
+  unsigned char* sQ = smem + 2 * KBUF;            // PL x 32 rows x 128 B
+  float* sX = reinterpret_cast<float*>(sQ + PL * 32 * 128);  // [128][33]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sX + kSnapTile * 33);
   uint32_t* sT = reinterpret_cast<uint32_t*>(bar + 1);
-  float* sStat = reinterpret_cast<float*>(sT + 4);          // [32][2] row max and sum (pass 1)
-  const int tile = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  float* sStat = reinterpret_cast<float*>(sT + 4);  // [32][2] row max and sum (pass 1)
+  const int h = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const hc_layer& L = a.L;
   pdl_wait();
   const hc_seq_desc d = L.desc[s];
   const Plan pl = make_plan(L, d.budget, min(seq_len<DENSE>(a, d), a.S_max));
   if (!pl.active) return;
-  const int S = pl.S, t0 = tile * kSnapTile;
-  if (t0 >= S) return;
-  const int nt = min(kSnapTile, S - t0);
+  const int S = pl.S;
+  const int tile0 = blockIdx.x * tpc;
+  if (tile0 * kSnapTile >= S) return;
+  const int ntile = min(tpc, (S - tile0 * kSnapTile + kSnapTile - 1) / kSnapTile);
   const int tqu = min(min(pl.nobs, a.tq), 32);
   if (tqu <= 0) return;
   const int NP = (tqu + 15) & ~15;  // the MMA's N: 16 or 32
@@ -296,89 +310,115 @@ __global__ void __launch_bounds__(kSnapTile, 1) snap_tile_kernel(CompressArgs a)
     sStat[2 * tid] = st[0];
     sStat[2 * tid + 1] = st[1];
   }
-  // keys of the tile (rows past the sequence read as zeros), 16-byte chunk c of row r at
-  // plane c/8, chunk (c%8) ^ (r%8): the layout of the tensor cores' 128-byte swizzle
-  for (int k = tid; k < kSnapTile * PL * 8; k += kSnapTile) {
-    const int r = k / (PL * 8), c = k % (PL * 8), t = t0 + r;
-    const T* src = reinterpret_cast<const T*>(a.q_obs);
-    int nb = 0;
-    if (r < nt) {
-      if constexpr (DENSE) {
-        src = reinterpret_cast<const T*>(a.src_k) + (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)t * a.ss_tok;
-        nb = 16;
-      } else {
-        const int slot = d.hot_ord[t];
-        if (slot >= 0 && slot < d.cap) {
-          src = reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + slot) * D;
+  // keys of tile `tile0 + i` into buffer i & 1 (rows past the sequence read as zeros); 16-byte
+  // chunk c of row r at plane c/8, chunk (c%8) ^ (r%8): the tensor cores' 128-byte swizzle
+  auto load_tile = [&](int i) {
+    unsigned char* buf = sK + (i & 1) * KBUF;
+    const int t0 = (tile0 + i) * kSnapTile, nt = min(kSnapTile, S - t0);
+    for (int k = tid; k < kSnapTile * PL * 8; k += kSnapTile) {
+      const int r = k / (PL * 8), c = k % (PL * 8), t = t0 + r;
+      const T* src = reinterpret_cast<const T*>(a.q_obs);
+      int nb = 0;
+      if (r < nt) {
+        if constexpr (DENSE) {
+          src = reinterpret_cast<const T*>(a.src_k) + (size_t)s * a.ss_seq + (size_t)h * a.ss_head + (size_t)t * a.ss_tok;
           nb = 16;
-        } else if ((c & 7) == 0) {
-          set_status(d.st, HC_DEV_INDEX);
+        } else {
+          const int slot = d.hot_ord[t];
+          if (slot >= 0 && slot < d.cap) {
+            src = reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + slot) * D;
+            nb = 16;
+          } else if ((c & 7) == 0) {
+            set_status(d.st, HC_DEV_INDEX);
+          }
         }
       }
+      cp_async16(buf + (size_t)(c >> 3) * kSnapTile * 128 + (size_t)r * 128 + (((c & 7) ^ (r & 7)) << 4),
+                 nb ? src + c * 8 : src, nb);
     }
-    cp_async16(sK + (size_t)(c >> 3) * kSnapTile * 128 + (size_t)r * 128 + (((c & 7) ^ (r & 7)) << 4),
-               nb ? src + c * 8 : src, nb);
-  }
+    cp_async_commit();
+  };
   const T* qb = reinterpret_cast<const T*>(a.qb) + ((size_t)s * L.Hk + h) * 32 * D;
   for (int k = tid; k < NP * PL * 8; k += kSnapTile) {
     const int n = k / (PL * 8), c = k % (PL * 8);
     cp_async16(sQ + (size_t)(c >> 3) * NP * 128 + (size_t)n * 128 + (((c & 7) ^ (n & 7)) << 4), qb + (size_t)n * D + c * 8,
                16);
   }
-  cp_async_commit();
-  cp_async_wait<0>();
-  fence_proxy_async_smem();  // the tensor cores read what cp.async wrote
+  load_tile(0);  // one group with the observation rows
   if (warp == 0) tmem_alloc(sT, 32);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *sT;
-  if (tid == 0) {
-    constexpr uint32_t fmt = DT == HC_BF16 ? 1u : 0u;
-    const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(kSnapTile >> 4) << 24);
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const uint32_t pl2 = ks >> 2, kin = ks & 3;
-      const uint32_t aa = smem_u32(sK) + pl2 * kSnapTile * 128u + kin * 32u;
-      const uint32_t bb = smem_u32(sQ) + pl2 * (uint32_t)NP * 128u + kin * 32u;
-      umma_f16(tbase, umma_desc_k_sw128(aa), umma_desc_k_sw128(bb), idesc, ks > 0);
+  constexpr uint32_t fmt = DT == HC_BF16 ? 1u : 0u;
+  const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(NP >> 3) << 17) |
+                         ((uint32_t)(kSnapTile >> 4) << 24);
+  for (int i = 0; i < ntile; ++i) {
+    if (i + 1 < ntile) {
+      load_tile(i + 1);  // lands while tile i is multiplied
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    umma_commit(bar);
-  }
-  if (!__syncthreads_and(mbar_wait(bar, 0)) && tid == 0) set_status(d.st, HC_DEV_TIMEOUT);
-  tc_fence_after();
-  float v[32];
+    fence_proxy_async_smem();  // the tensor cores read what cp.async wrote
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      const uint32_t kb = smem_u32(sK) + (uint32_t)(i & 1) * KBUF;
 #pragma unroll
-  for (int c = 0; c < 32; c += 8)
-    if (c < NP) tmem_ld_x8(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v + c);
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, 32);
-  // logits of token t = t0 + tid; observation row r sits at S - tqu + r and masks later keys
-  // (scoring.py:72-74)
-  const int t = t0 + tid;
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint32_t pl2 = ks >> 2, kin = ks & 3;
+        const uint32_t aa = kb + pl2 * kSnapTile * 128u + kin * 32u;
+        const uint32_t bb = smem_u32(sQ) + pl2 * (uint32_t)NP * 128u + kin * 32u;
+        umma_f16(tbase, umma_desc_k_sw128(aa), umma_desc_k_sw128(bb), idesc, ks > 0);
+      }
+      umma_commit(bar);
+    }
+    if (!__syncthreads_and(mbar_wait(bar, (uint32_t)(i & 1))) && tid == 0) set_status(d.st, HC_DEV_TIMEOUT);
+    tc_fence_after();
+    float v[32];
 #pragma unroll
-  for (int r = 0; r < 32; ++r)
-    v[r] = (r < tqu && tid < nt && t <= S - tqu + r) ? v[r] * L.scale : kNegInf;
-  if constexpr (PASS == 0) {
-    const int chunk = tile * (kSnapTile / 32) + warp;
-    if (chunk * 32 >= S) return;  // the partials cover ceil(S / 32) chunks
-    for (int r = 0; r < tqu; ++r) {
-      const float m = warp_max(v[r]);
-      const float l = warp_sum(v[r] == kNegInf ? 0.f : __expf(v[r] - m));
-      if (lane == 0) {
-        float* p = a.part + ((((size_t)s * L.Hk + h) * a.tqmax + r) * a.max_chunks + chunk) * 2;
-        p[0] = m;
-        p[1] = l;
+    for (int c = 0; c < 32; c += 8)
+      if (c < NP) tmem_ld_x8(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v + c);
+    tc_fence_before();
+    // logits of token t = t0 + tid; observation row r sits at S - tqu + r and masks later keys
+    // (scoring.py:72-74)
+    const int t0 = (tile0 + i) * kSnapTile, nt = min(kSnapTile, S - t0), t = t0 + tid;
+#pragma unroll
+    for (int r = 0; r < 32; ++r)
+      v[r] = (r < tqu && tid < nt && t <= S - tqu + r) ? v[r] * L.scale : kNegInf;
+    if constexpr (PASS == 0) {
+      // per-warp (32-token) partials of every row: the logits go through shared memory so that
+      // lane r of warp w reduces row r over the warp's tokens without shuffles
+#pragma unroll
+      for (int r = 0; r < 32; ++r) sX[tid * 33 + r] = v[r];
+      __syncthreads();
+      const int chunk = (tile0 + i) * (kSnapTile / 32) + warp;
+      if (lane < tqu && chunk * 32 < S) {  // the partials cover ceil(S / 32) chunks
+        const float* col = sX + (size_t)warp * 32 * 33 + lane;
+        float m = kNegInf;
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) m = fmaxf(m, col[j * 33]);
+        float l = 0.f;
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
+          const float x = col[j * 33];
+          l += (x == kNegInf) ? 0.f : __expf(x - m);
+        }
+        float* pp = a.part + ((((size_t)s * L.Hk + h) * a.tqmax + lane) * a.max_chunks + chunk) * 2;
+        pp[0] = m;
+        pp[1] = l;
+      }
+    } else {
+      if (tid < nt) {
+        float acc = 0.f;
+        for (int r = 0; r < tqu; ++r) acc += (v[r] == kNegInf) ? 0.f : __expf(v[r] - sStat[2 * r]) / sStat[2 * r + 1];
+        a.imp[((size_t)s * L.Hk + h) * a.S_max + t] = acc;
       }
     }
-  } else {
-    if (tid < nt) {
-      float acc = 0.f;
-      for (int r = 0; r < tqu; ++r) acc += (v[r] == kNegInf) ? 0.f : __expf(v[r] - sStat[2 * r]) / sStat[2 * r + 1];
-      a.imp[((size_t)s * L.Hk + h) * a.S_max + t] = acc;
-    }
+    __syncthreads();  // TMEM and the transpose are free for the next tile
   }
+  if (warp == 0) tmem_dealloc(tbase, 32);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -1101,17 +1141,22 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
   if (tc) {
     a.chunk_len = 32;
     const int tiles = (S_grid + kSnapTile - 1) / kSnapTile;
-    const size_t tsmem = (size_t)(D / 64) * (kSnapTile + 32) * 128 + 8 + 16 + 256 + 1024;
+    // tiles per CTA: about two CTAs per SM over the whole grid
+    const long all_tiles = (long)tiles * L.Hk * L.n_seq;
+    int tpc = (int)((all_tiles + 295) / 296);
+    tpc = tpc < 1 ? 1 : tpc > 16 ? 16 : tpc;
+    const int gx = (tiles + tpc - 1) / tpc;
+    const size_t tsmem = snap_tile_smem<D>();
     auto k0 = snap_tile_kernel<DT, D, DENSE, 0>;
     auto k1 = snap_tile_kernel<DT, D, DENSE, 1>;
     e = ensure_smem(k0, tsmem);
     if (e == cudaSuccess) e = ensure_smem(k1, tsmem);
     if (e != cudaSuccess) return e;
     e = launch_pdl(snap_qbar_kernel<DT, D, DENSE>, dim3(L.Hk, 16, L.n_seq), dim3(256), 0, stream, a);
-    if (e == cudaSuccess) e = launch_pdl(k0, dim3(tiles, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a);
+    if (e == cudaSuccess) e = launch_pdl(k0, dim3(gx, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a, tpc);
     if (e == cudaSuccess)
       e = launch_pdl(stats_kernel<DENSE>, dim3((L.Hk * a.tqmax + 7) / 8, L.n_seq), dim3(256), 0, stream, a);
-    if (e == cudaSuccess) e = launch_pdl(k1, dim3(tiles, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a);
+    if (e == cudaSuccess) e = launch_pdl(k1, dim3(gx, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a, tpc);
     if (e != cudaSuccess) return e;
   } else {
     const size_t smem =

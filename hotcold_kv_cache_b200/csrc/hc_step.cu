@@ -331,6 +331,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   // that kernel writes.
   {
     const int nl_ord = (d.cap * 4 + 127) / 128, nl_pos = (d.r_max * 8 + 127) / 128;
+    if (MMA && tid == 32) {
+      prefetch_tensormap(L.kmaps);  // both maps: the hot K slab and the held K rows
+      prefetch_tensormap(reinterpret_cast<const char*>(L.kmaps) + 128);
+    }
     if (tid == 0) {
       prefetch_l2(d.st);
       if (d.held_valid) prefetch_l2(d.held_valid);
@@ -349,12 +353,105 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       prefetch_l2(reinterpret_cast<const char*>(d.hot_free) + (size_t)(tid - 1) * 128);
     } else if (a.use_held && d.held_pos && tid <= nl_ord + nl_pos) {
       prefetch_l2(reinterpret_cast<const char*>(d.held_pos) + (size_t)(tid - 1 - nl_ord) * 128);
+    } else if (tid >= 64) {
+      // this step's inputs (the query rows of this head group, or all of them for the CTA that
+      // pushes the query pool; the new key, value, cos/sin and position): written by the
+      // preceding kernel in a model, so only warmed here, read after the wait
+      const int lt = tid - 64;
+      const int rb = D * ESZ;  // bytes of one head row
+      const bool all_q = rank == ncta - 1;
+      const int nq = ((all_q ? L.Hq : G) * rb + 127) / 128, nr = (rb + 127) / 128;
+      const char* qrow = reinterpret_cast<const char*>(a.q_pre) + (size_t)s * a.qss * ESZ + (all_q ? 0 : (size_t)h * G * rb);
+      if (lt < nq) {
+        prefetch_l2(qrow + (size_t)lt * 128);
+      } else if (lt < nq + nr) {
+        prefetch_l2(reinterpret_cast<const char*>(a.k_pre) + ((size_t)s * a.kvss + (size_t)h * D) * ESZ +
+                    (size_t)(lt - nq) * 128);
+      } else if (lt < nq + 2 * nr) {
+        prefetch_l2(reinterpret_cast<const char*>(a.v) + ((size_t)s * a.kvss + (size_t)h * D) * ESZ +
+                    (size_t)(lt - nq - nr) * 128);
+      } else if (a.cos && lt < nq + 3 * nr) {
+        prefetch_l2(reinterpret_cast<const char*>(a.cos) + (size_t)s * rb + (size_t)(lt - nq - 2 * nr) * 128);
+      } else if (a.sin && lt < nq + 4 * nr) {
+        prefetch_l2(reinterpret_cast<const char*>(a.sin) + (size_t)s * rb + (size_t)(lt - nq - 3 * nr) * 128);
+      } else if (lt == nq + 4 * nr) {
+        prefetch_l2(a.pos + s);
+      }
     }
   }
   pdl_wait();
 
+  // ---- one round trip: counters, logical order, free stack, held flags, new token inputs ----
+  hc_seq_state* st = d.st;
+  const int n_hot = st->n_hot, n_free = st->n_free, held_len = st->held_len;
+  const int qwin_head = st->qwin_head, cold_head = st->cold_head, cold_count = st->cold_count;
+  const int64_t cur_pos = a.pos[s];
+  const int cap = d.cap;
+  const T* __restrict__ qp = reinterpret_cast<const T*>(a.q_pre) + (size_t)s * a.qss;
+  const T* __restrict__ kp = reinterpret_cast<const T*>(a.k_pre) + (size_t)s * a.kvss + (size_t)h * D;
+  const T* __restrict__ vp = reinterpret_cast<const T*>(a.v) + (size_t)s * a.kvss + (size_t)h * D;
+  // raw loads first (all in flight together), conversions after
+  T xr[RP][2], cr[RP][2], sr[RP][2];
+  float rx[RP][2], rc[RP][2], rs[RP][2];
+  const bool have_cs = a.cos != nullptr;
+#pragma unroll
+  for (int j = 0; j < RP; ++j) {
+    const int k = tid + j * kStepThreads;
+    if (k < (G + 1) * H) {
+      const int g = k / H, i = k % H;
+      const T* x = g < G ? qp + (size_t)(h * G + g) * D : kp;
+      xr[j][0] = x[i];
+      xr[j][1] = x[i + H];
+      if (have_cs) {
+        const T* cs = reinterpret_cast<const T*>(a.cos) + (size_t)s * D;
+        const T* sn = reinterpret_cast<const T*>(a.sin) + (size_t)s * D;
+        cr[j][0] = cs[i];
+        cr[j][1] = cs[i + H];
+        sr[j][0] = sn[i];
+        sr[j][1] = sn[i + H];
+      } else {
+        rc[j][0] = L.inv_freq[i];
+      }
+    }
+  }
+  const T vnew = tid < D ? vp[tid] : E::from_f(0.f);
+  // the last CTA stages the query rows for the query-pool push
+  const bool qpush = rank == ncta - 1 && d.p_max > 0;
+  constexpr int kQP = 16;
+  T tq[kQP];
+  if (qpush)
+#pragma unroll
+    for (int j = 0; j < kQP; ++j)
+      if (tid + j * kStepThreads < L.Hq * D) tq[j] = qp[tid + j * kStepThreads];
+  // all loads first, then the stores: one round trip for up to kPre entries per thread
+  constexpr int kPre = 4;
+  int ov[kPre], fv[kPre];
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int i = tid + j * kStepThreads;
+    if (i < cap) {
+      ov[j] = d.hot_ord[i];
+      fv[j] = d.hot_free[i];
+    }
+  }
+  const bool hv_ok = a.use_held && tid < d.r_max;
+  const uint8_t hval = hv_ok ? d.held_valid[tid] : 0;
+  const int64_t hpos = hv_ok ? d.held_pos[tid] : 0;
+#pragma unroll
+  for (int j = 0; j < RP; ++j) {
+    if (tid + j * kStepThreads < (G + 1) * H) {
+      rx[j][0] = E::to_f(xr[j][0]);
+      rx[j][1] = E::to_f(xr[j][1]);
+      if (have_cs) {
+        rc[j][0] = E::to_f(cr[j][0]);
+        rc[j][1] = E::to_f(cr[j][1]);
+        rs[j][0] = E::to_f(sr[j][0]);
+        rs[j][1] = E::to_f(sr[j][1]);
+      }
+    }
+  }
   // ---- this part's K rows (TMA tensor boxes into the swizzled MMA layout for 16-bit types,
-  //      else bulk copies) and V rows (bulk copies, at most two); lanes of warp 0 issue them ----
+  //      else bulk copies); lanes of warp 0 issue them while the loads above are in flight ----
   if (warp == 0) {
     const uint32_t vbytes = (uint32_t)((nhr + ns) * ROWB);
     const int nhb = nh >> 3, nsb = (ns + 63) >> 6;  // 8-row held boxes, 64-row slot boxes
@@ -387,67 +484,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         bulk_g2s(sK + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + sb) * D,
                  (uint32_t)(ns * ROWB), &bars[0]);
     }
-    if (lane == 3 && nhr > 0)
-      bulk_g2s(sV, reinterpret_cast<const T*>(d.held_v) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
-               &bars[1]);
-    if (lane == 4 && ns > 0)
-      bulk_g2s(sV + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_v) + ((size_t)h * d.cap + sb) * D,
-               (uint32_t)(ns * ROWB), &bars[1]);
   }
 
-  // ---- one round trip: counters, logical order, free stack, held flags, new token inputs ----
-  hc_seq_state* st = d.st;
-  const int n_hot = st->n_hot, n_free = st->n_free, held_len = st->held_len;
-  const int qwin_head = st->qwin_head, cold_head = st->cold_head, cold_count = st->cold_count;
-  const int64_t cur_pos = a.pos[s];
-  const int cap = d.cap;
-  const T* __restrict__ qp = reinterpret_cast<const T*>(a.q_pre) + (size_t)s * a.qss;
-  const T* __restrict__ kp = reinterpret_cast<const T*>(a.k_pre) + (size_t)s * a.kvss + (size_t)h * D;
-  const T* __restrict__ vp = reinterpret_cast<const T*>(a.v) + (size_t)s * a.kvss + (size_t)h * D;
-  float rx[RP][2], rc[RP][2], rs[RP][2];
-#pragma unroll
-  for (int j = 0; j < RP; ++j) {
-    const int k = tid + j * kStepThreads;
-    if (k < (G + 1) * H) {
-      const int g = k / H, i = k % H;
-      const T* x = g < G ? qp + (size_t)(h * G + g) * D : kp;
-      rx[j][0] = E::to_f(x[i]);
-      rx[j][1] = E::to_f(x[i + H]);
-      if (a.cos) {
-        const T* cs = reinterpret_cast<const T*>(a.cos) + (size_t)s * D;
-        const T* sn = reinterpret_cast<const T*>(a.sin) + (size_t)s * D;
-        rc[j][0] = E::to_f(cs[i]);
-        rc[j][1] = E::to_f(cs[i + H]);
-        rs[j][0] = E::to_f(sn[i]);
-        rs[j][1] = E::to_f(sn[i + H]);
-      } else {
-        rc[j][0] = L.inv_freq[i];
-      }
-    }
-  }
-  const T vnew = tid < D ? vp[tid] : E::from_f(0.f);
-  // the last CTA stages the query rows for the query-pool push
-  const bool qpush = rank == ncta - 1 && d.p_max > 0;
-  constexpr int kQP = 16;
-  T tq[kQP];
-  if (qpush)
-#pragma unroll
-    for (int j = 0; j < kQP; ++j)
-      if (tid + j * kStepThreads < L.Hq * D) tq[j] = qp[tid + j * kStepThreads];
-  // all loads first, then the stores: one round trip for up to kPre entries per thread
-  constexpr int kPre = 4;
-  int ov[kPre], fv[kPre];
-#pragma unroll
-  for (int j = 0; j < kPre; ++j) {
-    const int i = tid + j * kStepThreads;
-    if (i < cap) {
-      ov[j] = d.hot_ord[i];
-      fv[j] = d.hot_free[i];
-    }
-  }
-  const bool hv_ok = a.use_held && tid < d.r_max;
-  const uint8_t hval = hv_ok ? d.held_valid[tid] : 0;
-  const int64_t hpos = hv_ok ? d.held_pos[tid] : 0;
 #pragma unroll
   for (int j = 0; j < kPre; ++j) {
     const int i = tid + j * kStepThreads;
@@ -487,8 +525,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   // uniform exit, after this CTA's bulk copies have landed
   if (n_hot < 0 || S > cap || S > gm.s_cap || new_slot < 0 || new_slot >= cap) {
     if (rank == 0 && tid == 0) set_status(st, HC_DEV_CAPACITY);
-    mbar_wait(&bars[0], 0);
-    mbar_wait(&bars[1], 0);
+    mbar_wait(&bars[0], 0);  // the V rows are not requested yet
     cluster_wait();
     return;
   }
@@ -569,6 +606,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   }
   // K rows landed: the new key replaces the stale copy of its slot
   if (!__syncthreads_and(mbar_wait(&bars[0], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
+  // V rows only now: K alone shares the cluster's L2 bandwidth (one GPC) until it has landed;
+  // V arrives during scoring and policy, long before P.V needs it
+  if (warp == 0) {
+    if (lane == 3 && nhr > 0)
+      bulk_g2s(sV, reinterpret_cast<const T*>(d.held_v) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
+               &bars[1]);
+    if (lane == 4 && ns > 0)
+      bulk_g2s(sV + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_v) + ((size_t)h * d.cap + sb) * D,
+               (uint32_t)(ns * ROWB), &bars[1]);
+  }
   if (i_new >= 0)
     for (int i = tid; i < D; i += kStepThreads) {
       if constexpr (MMA) {

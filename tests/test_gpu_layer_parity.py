@@ -249,3 +249,21 @@ def test_chunked_prefill_vs_oracle(dtype, policy, chunks):
         for k, v in layer.dbg.items():
             assert res["ctrl"].dbg[k] == v, k
     assert res["ctrl"].device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", ["float16", "float32"])
+def test_split_attention_large_batch_vs_oracle(dtype):
+    """The split-path attention for batches that fill the GPU (16 sequences x 8 KV heads x
+    3 blocks of 256 rows): four double-buffered chunks per CTA with an online softmax. Against
+    the oracle, with retrieval and a held segment."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import run_cuda_layer
+    c = dict(B=16, Hq=32, Hk=8, D=128, T=700, steps=3, dtype=dtype, policy="snapkv", cap=512, recent=32,
+             topk_ratio=0.0, pool_kernel=7, ccap=1000, faiss_dim=128, window_size=2, pool=1, R=16, hold=True,
+             rap=True, theta=500000.0, seed=2024)
+    inp = synth.layer_inputs(c["seed"], 16, 32, 8, 128, c["T"], c["steps"], dtype)
+    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], **oracle_kwargs(c))
+    res = run_cuda_layer(c, inp, c["steps"], fused=False)
+    near = 1e-4 if dtype == "float32" else 2e-3
+    assert _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near) >= 1
+    assert res["ctrl"].device_status() == 0
