@@ -330,8 +330,8 @@ struct PipeSmem {
   static constexpr size_t sOff = qOff + sizeof(float) * G * D;         // [G][CH] scores, then p
   static constexpr size_t mlOff = sOff + sizeof(float) * G * CH;       // running max [G], sum [G], rescale [G]
   static constexpr size_t validOff = mlOff + sizeof(float) * 3 * G;    // [2][CH]
-  static constexpr size_t barOff = (validOff + sizeof(int) * 2 * CH + 15) & ~size_t(15);  // 4 mbarriers
-  static constexpr size_t miscOff = barOff + 32;
+  static constexpr size_t rowOff = (validOff + sizeof(int) * 2 * CH + 15) & ~size_t(15);  // [2][2][CH] row pointers
+  static constexpr size_t miscOff = rowOff + 2 * 2 * CH * sizeof(void*);
   static constexpr size_t bytes = miscOff + 16;
 };
 
@@ -340,9 +340,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
   using E = Elem<DT>;
   using T = typename E::T;
   using SM = PipeSmem<DT, D, G, CH>;
-  constexpr int ROWB = D * sizeof(T);
   constexpr int VEC = 16 / sizeof(T);
   constexpr int NJ = D / (8 * VEC);
+  constexpr int CPR = D / VEC;  // 16-byte chunks per row
   constexpr int SPAN = CH * NSUB;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sK = reinterpret_cast<T*>(smem + SM::kOff);
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
   float* sS = reinterpret_cast<float*>(smem + SM::sOff);
   float* sML = reinterpret_cast<float*>(smem + SM::mlOff);
   int* sValid = reinterpret_cast<int*>(smem + SM::validOff);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::barOff);
+  const T** sRow = reinterpret_cast<const T**>(smem + SM::rowOff);  // [buf][K|V][CH]
   int* sMisc = reinterpret_cast<int*>(smem + SM::miscOff);
 
   const int c = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
@@ -365,73 +365,57 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
   if (c >= n_chunks) return;
   const int base0 = c * SPAN;
   const int nsub = min(NSUB, (n_tok - base0 + CH - 1) / CH);
-  if (tid == 0) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
-    fence_mbar_init();
-  }
   if (tid < G) {
     sML[tid] = kNegInf;
     sML[G + tid] = 0.f;
   }
-  __syncthreads();
 
-  // rows of chunk j into buffer j & 1 (an out-of-range slot is reported and read as zeros)
+  // rows of chunk j into buffer j & 1 with 16-byte cp.async gathers (one commit group per chunk);
+  // an out-of-range slot is reported and its row reads as zeros
   auto stage = [&](int j) {
     const int buf = j & 1;
     const int t0 = base0 + j * CH, nt = min(CH, n_tok - t0);
     T* bk = sK + (size_t)buf * CH * D;
     T* bv = sV + (size_t)buf * CH * D;
-    const T* krow = nullptr;
-    const T* vrow = nullptr;
-    bool copy = false;
-    if (tid < nt) {
-      const int t = t0 + tid;
-      int valid = 1;
-      if (t < n_held) {
-        const size_t off = ((size_t)h * d.r_max + t) * D;
-        krow = reinterpret_cast<const T*>(d.held_k) + off;
-        vrow = reinterpret_cast<const T*>(d.held_v) + off;
-        valid = d.held_valid[t] != 0 && d.held_pos[t] <= a.cur_pos[s];
-        copy = true;
-      } else {
-        const int slot = d.hot_ord[t - n_held];
-        if (slot >= 0 && slot < d.cap) {
-          const size_t off = ((size_t)h * d.cap + slot) * D;
-          krow = reinterpret_cast<const T*>(d.hot_k) + off;
-          vrow = reinterpret_cast<const T*>(d.hot_v) + off;
-          copy = true;
+    const T** rk = sRow + (size_t)buf * 2 * CH;
+    const T** rv = rk + CH;
+    if (tid < CH) {
+      const T* krow = nullptr;
+      const T* vrow = nullptr;
+      int valid = 0;
+      if (tid < nt) {
+        const int t = t0 + tid;
+        valid = 1;
+        if (t < n_held) {
+          const size_t off = ((size_t)h * d.r_max + t) * D;
+          krow = reinterpret_cast<const T*>(d.held_k) + off;
+          vrow = reinterpret_cast<const T*>(d.held_v) + off;
+          valid = d.held_valid[t] != 0 && d.held_pos[t] <= a.cur_pos[s];
         } else {
-          valid = 0;
-          set_status(st, HC_DEV_INDEX);
+          const int slot = d.hot_ord[t - n_held];
+          if (slot >= 0 && slot < d.cap) {
+            const size_t off = ((size_t)h * d.cap + slot) * D;
+            krow = reinterpret_cast<const T*>(d.hot_k) + off;
+            vrow = reinterpret_cast<const T*>(d.hot_v) + off;
+          } else {
+            valid = 0;
+            set_status(st, HC_DEV_INDEX);
+          }
         }
       }
+      rk[tid] = krow;
+      rv[tid] = vrow;
       sValid[buf * CH + tid] = valid;
     }
-    const int n_copy = __syncthreads_count(copy);
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&bars[2 * buf], (uint32_t)(n_copy * ROWB));
-      mbar_arrive_expect_tx(&bars[2 * buf + 1], (uint32_t)(n_copy * ROWB));
+    __syncthreads();
+    for (int k = tid; k < CH * CPR; k += kAttnThreads) {
+      const int r = k / CPR, q = k % CPR;
+      const T* kr = rk[r];
+      const T* vr = rv[r];
+      cp_async16(bk + (size_t)r * D + q * VEC, kr ? kr + q * VEC : reinterpret_cast<const T*>(a.q), kr ? 16 : 0);
+      cp_async16(bv + (size_t)r * D + q * VEC, vr ? vr + q * VEC : reinterpret_cast<const T*>(a.q), vr ? 16 : 0);
     }
-    if (copy) {
-      fence_proxy_async_smem();  // this buffer was last read by the generic proxy
-      bulk_g2s(bk + (size_t)tid * D, krow, ROWB, &bars[2 * buf]);
-      bulk_g2s(bv + (size_t)tid * D, vrow, ROWB, &bars[2 * buf + 1]);
-    } else if (tid < nt) {
-      for (int i = 0; i < D; ++i) {
-        bk[(size_t)tid * D + i] = E::from_f(0.f);
-        bv[(size_t)tid * D + i] = E::from_f(0.f);
-      }
-    }
-  };
-  // on a timed-out wait: give every copy still in flight a last bounded wait, then leave
-  auto drain = [&](int j) {
-    if (tid == 0) set_status(st, HC_DEV_TIMEOUT);
-    for (int jj = j; jj < min(nsub, j + 2); ++jj) {
-      const uint32_t ph = (uint32_t)(jj >> 1) & 1u;
-      mbar_wait(&bars[2 * (jj & 1)], ph);
-      mbar_wait(&bars[2 * (jj & 1) + 1], ph);
-    }
+    cp_async_commit();
   };
 
   stage(0);
@@ -447,21 +431,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
     for (int j = 0; j < NJ; ++j)
 #pragma unroll
       for (int e = 0; e < VEC; ++e) qr[g][j * VEC + e] = sQ[g * D + j * 8 * VEC + sub * VEC + e];
-  float o[G];
+  // P.V: thread (row group grp, column chunk cc) accumulates 16-byte column chunk cc of every
+  // query head over rows grp, grp + NGRP, ... (packed fp32 FMAs); the groups are added at the end
+  constexpr int KCH = D / VEC;               // 16-byte column chunks per row
+  constexpr int NGRP = kAttnThreads / KCH;   // row groups
+  const int cch = tid % KCH, grp = tid / KCH;
+  float2 o2[G][VEC / 2];
 #pragma unroll
-  for (int g = 0; g < G; ++g) o[g] = 0.f;
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int e = 0; e < VEC / 2; ++e) o2[g][e] = make_float2(0.f, 0.f);
 
   for (int j = 0; j < nsub; ++j) {
     const int buf = j & 1;
-    const uint32_t ph = (uint32_t)(j >> 1) & 1u;
     const int nt = min(CH, n_tok - (base0 + j * CH));
     const T* bk = sK + (size_t)buf * CH * D;
     const T* bv = sV + (size_t)buf * CH * D;
     const int* bval = sValid + buf * CH;
-    if (!__syncthreads_and(mbar_wait(&bars[2 * buf], ph))) {
-      drain(j);
-      return;
-    }
+    if (j + 1 < nsub) cp_async_wait<1>();  // chunk j landed, chunk j + 1 may still be in flight
+    else cp_async_wait<0>();
+    __syncthreads();
     for (int b4 = warp * 4; b4 < nt; b4 += 16) {
       const int t = b4 + tk;
       float acc[G];
@@ -516,23 +505,47 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
         sML[2 * G + g] = alpha;
       }
     }
-    if (!__syncthreads_and(mbar_wait(&bars[2 * buf + 1], ph))) {
-      drain(j);
-      return;
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float al = sML[2 * G + g];
+      const float2 a2 = make_float2(al, al);
+#pragma unroll
+      for (int e = 0; e < VEC / 2; ++e) o2[g][e] = __fmul2_rn(o2[g][e], a2);
     }
-    if (tid < D) {
+    for (int t = grp; t < nt; t += NGRP) {
+      float vf[VEC];
+      unpack16<DT>(*reinterpret_cast<const uint4*>(bv + (size_t)t * D + cch * VEC), vf);
 #pragma unroll
-      for (int g = 0; g < G; ++g) o[g] *= sML[2 * G + g];
-      for (int t = 0; t < nt; ++t) {
-        const float vv = E::to_f(bv[(size_t)t * D + tid]);
+      for (int g = 0; g < G; ++g) {
+        const float pr = sS[g * CH + t];
+        const float2 p2 = make_float2(pr, pr);
 #pragma unroll
-        for (int g = 0; g < G; ++g) o[g] = fmaf(sS[g * CH + t], vv, o[g]);
+        for (int e = 0; e < VEC / 2; ++e) o2[g][e] = __ffma2_rn(p2, make_float2(vf[2 * e], vf[2 * e + 1]), o2[g][e]);
       }
     }
     __syncthreads();  // buffer `buf` and the scores are free
     if (j + 2 < nsub) stage(j + 2);
   }
 
+  // the row groups' column chunks, added per column (the key and value buffers, contiguous, are
+  // free: no copy is in flight after the last chunk)
+  float* red = reinterpret_cast<float*>(sK);  // [NGRP][G][D] fp32 over the key and value buffers
+  static_assert((size_t)NGRP * G * D * 4 <= 4 * sizeof(T) * CH * D, "reduction buffer");
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int e = 0; e < VEC / 2; ++e)
+      *reinterpret_cast<float2*>(red + ((size_t)grp * G + g) * D + cch * VEC + 2 * e) = o2[g][e];
+  __syncthreads();
+  float o[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    o[g] = 0.f;
+    if (tid < D)
+#pragma unroll
+      for (int q = 0; q < NGRP; ++q) o[g] += red[((size_t)q * G + g) * D + tid];
+  }
   const size_t head0 = (size_t)s * a.Hq + (size_t)h * G;
   T* outp = reinterpret_cast<T*>(a.out);
   if (n_chunks == 1) {
