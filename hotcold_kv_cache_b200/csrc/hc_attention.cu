@@ -37,8 +37,8 @@ struct AttnSmem {
   static constexpr size_t sOff = qOff + sizeof(float) * G * D;
   static constexpr size_t mlOff = sOff + sizeof(float) * G * CH;
   static constexpr size_t validOff = mlOff + sizeof(float) * 2 * G;
-  static constexpr size_t barOff = (validOff + sizeof(int) * CH + 15) & ~size_t(15);
-  static constexpr size_t miscOff = barOff + 16;
+  static constexpr size_t rowOff = (validOff + sizeof(int) * CH + 15) & ~size_t(15);  // [K|V][CH] row pointers
+  static constexpr size_t miscOff = rowOff + 2 * CH * sizeof(void*);
   static constexpr size_t bytes = miscOff + 16;
 };
 
@@ -59,8 +59,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   float* sS = reinterpret_cast<float*>(smem + SM::sOff);
   float* sML = reinterpret_cast<float*>(smem + SM::mlOff);
   int* sValid = reinterpret_cast<int*>(smem + SM::validOff);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::barOff);
+  const T** sRow = reinterpret_cast<const T**>(smem + SM::rowOff);
   int* sMisc = reinterpret_cast<int*>(smem + SM::miscOff);
+  constexpr int CPR = D / VEC;  // 16-byte chunks per row
 
   const int c = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -84,13 +85,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   const int t0 = c * CH;
   const int nt = min(CH, n_tok - t0);
 
-  if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    fence_mbar_init();
-  }
-
-  // ---- resolve rows and issue the bulk copies -------------------------------------------
+  // ---- resolve rows, then gather them with 16-byte cp.async (K and V in two groups) --------
   const T* krow = nullptr;
   const T* vrow = nullptr;
   bool copy = false;
@@ -123,20 +118,24 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
     }
     sValid[tid] = valid;
   }
-  const int n_copy = __syncthreads_count(copy);
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bars[0], (uint32_t)(n_copy * ROWB));
-    mbar_arrive_expect_tx(&bars[1], (uint32_t)(n_copy * ROWB));
+  if (tid < CH) {
+    sRow[tid] = copy ? krow : nullptr;
+    sRow[CH + tid] = copy ? vrow : nullptr;
   }
-  if (copy) {
-    bulk_g2s(sK + (size_t)tid * D, krow, ROWB, &bars[0]);
-    bulk_g2s(sV + (size_t)tid * D, vrow, ROWB, &bars[1]);
-  } else if (tid < nt) {
-    for (int i = 0; i < D; ++i) {
-      sK[(size_t)tid * D + i] = E::from_f(0.f);
-      sV[(size_t)tid * D + i] = E::from_f(0.f);
-    }
+  __syncthreads();
+  // rows without a source (and rows past the chunk) read as zeros
+  for (int k = tid; k < nt * CPR; k += kAttnThreads) {
+    const int r = k / CPR, q = k % CPR;
+    const T* kr = sRow[r];
+    cp_async16(sK + (size_t)r * D + q * VEC, kr ? kr + q * VEC : reinterpret_cast<const T*>(a.q), kr ? 16 : 0);
   }
+  cp_async_commit();
+  for (int k = tid; k < nt * CPR; k += kAttnThreads) {
+    const int r = k / CPR, q = k % CPR;
+    const T* vr = sRow[CH + r];
+    cp_async16(sV + (size_t)r * D + q * VEC, vr ? vr + q * VEC : reinterpret_cast<const T*>(a.q), vr ? 16 : 0);
+  }
+  cp_async_commit();
   // query heads of this KV head -> shared (float), while the rows are in flight
   const T* qg = reinterpret_cast<const T*>(a.q) + ((size_t)s * a.Hq + (size_t)h * G) * D;
   for (int i = tid; i < G * D; i += kAttnThreads) sQ[i] = E::to_f(qg[i]);
@@ -151,12 +150,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
 #pragma unroll
       for (int e = 0; e < VEC; ++e) qr[g][j * VEC + e] = sQ[g * D + j * 8 * VEC + sub * VEC + e];
 
-  if (!__syncthreads_and(mbar_wait(&bars[0], 0))) {
-    if (tid == 0) set_status(st, HC_DEV_TIMEOUT);
-    mbar_wait(&bars[1], 0);  // bounded: give copies in flight a last chance to land
-    mbar_wait(&bars[0], 0);
-    return;
-  }
+  cp_async_wait<1>();  // K rows landed (V may still be in flight)
+  __syncthreads();
 
   // ---- scores: 4 tokens per warp per pass, 8 lanes per token ----------------------------
   for (int base = warp * 4; base < nt; base += 16) {
@@ -208,11 +203,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
       sML[G + g] = l;
     }
   }
-  if (!__syncthreads_and(mbar_wait(&bars[1], 0))) {
-    if (tid == 0) set_status(st, HC_DEV_TIMEOUT);
-    mbar_wait(&bars[1], 0);
-    return;
-  }
+  cp_async_wait<0>();  // V rows landed
+  __syncthreads();
 
   // ---- P.V: thread d owns output column d for every query head ----------------------------
   float o[G];
