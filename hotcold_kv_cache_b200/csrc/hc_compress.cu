@@ -104,7 +104,8 @@ __global__ void __launch_bounds__(128) score_kernel(CompressArgs a) {
   T* sK = reinterpret_cast<T*>(smem);
   float* sQ = reinterpret_cast<float*>(smem + sizeof(T) * CH * D);      // [tqmax + 1][D]
   float* sL = sQ + (size_t)(a.tqmax + 1) * D;                             // [tqmax][CH]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sL + (size_t)a.tqmax * CH + 4);
+  const T** sRowp = reinterpret_cast<const T**>(sL + (size_t)a.tqmax * CH + 4);  // [CH] row sources
+  constexpr int CPR = D / VEC;  // 16-byte chunks per row
 
   const int c = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -119,12 +120,8 @@ __global__ void __launch_bounds__(128) score_kernel(CompressArgs a) {
   const int tqu = min(pl.nobs, a.tq);
   const int G = L.Hq / L.Hk;
 
-  if (tid == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  // key rows of this chunk (an out-of-range slot is reported and read as zeros)
+  // key rows of this chunk, gathered with 16-byte cp.async (an out-of-range slot is reported
+  // and read as zeros)
   const T* row = nullptr;
   if (tid < nt) {
     const int t = t0 + tid;
@@ -136,11 +133,14 @@ __global__ void __launch_bounds__(128) score_kernel(CompressArgs a) {
       else set_status(d.st, HC_DEV_INDEX);
     }
   }
-  const int n_copy = __syncthreads_count(row != nullptr);
-  if (tid == 0) mbar_arrive_expect_tx(bar, (uint32_t)(n_copy * ROWB));
-  if (row) bulk_g2s(sK + (size_t)tid * D, row, ROWB, bar);
-  else if (tid < nt)
-    for (int i = 0; i < D; ++i) sK[(size_t)tid * D + i] = E::from_f(0.f);
+  if (tid < CH) sRowp[tid] = row;
+  __syncthreads();
+  for (int k = tid; k < nt * CPR; k += 128) {
+    const int r = k / CPR, q = k % CPR;
+    const T* src = sRowp[r];
+    cp_async16(sK + (size_t)r * D + q * VEC, src ? src + q * VEC : reinterpret_cast<const T*>(a.q_obs), src ? 16 : 0);
+  }
+  cp_async_commit();
   // GQA-mean observation rows (cache.py:60-64 / scoring.py:17-26), rounded to the dtype
   const T* q = reinterpret_cast<const T*>(a.q_obs) + (size_t)s * a.qs_seq;
   for (int i = tid; i < tqu * D; i += 128) {
@@ -158,11 +158,8 @@ __global__ void __launch_bounds__(128) score_kernel(CompressArgs a) {
     for (int r = 0; r < tqu; ++r) acc += sQ[r * D + tid];
     sQ[(size_t)a.tqmax * D + tid] = acc;  // the extra row holds the sum
   }
-  if (!__syncthreads_and(mbar_wait(bar, 0))) {
-    if (tid == 0) set_status(d.st, HC_DEV_TIMEOUT);
-    mbar_wait(bar, 0);
-    return;
-  }
+  cp_async_wait<0>();
+  __syncthreads();
 
   const int sub = lane & 7, tk = lane >> 3;
   const int nrows = hotcold ? 1 : tqu;
@@ -1159,8 +1156,9 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
     if (e == cudaSuccess) e = launch_pdl(k1, dim3(gx, L.Hk, L.n_seq), dim3(kSnapTile), tsmem, stream, a, tpc);
     if (e != cudaSuccess) return e;
   } else {
-    const size_t smem =
-        sizeof(T) * kScoreCH * D + sizeof(float) * ((size_t)(a.tqmax + 1) * D + (size_t)a.tqmax * kScoreCH) + 64;
+    const size_t smem = sizeof(T) * kScoreCH * D +
+                        sizeof(float) * ((size_t)(a.tqmax + 1) * D + (size_t)a.tqmax * kScoreCH) + 64 +
+                        sizeof(void*) * kScoreCH;
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     auto sk = score_kernel<DT, D, DENSE>;
     e = ensure_smem(sk, 200 * 1024);
