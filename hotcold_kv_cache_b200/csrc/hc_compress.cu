@@ -745,7 +745,49 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
       for (int t = tid; t < S; t += blockDim.x) sLg[(size_t)row * S + t] = src[t];
     }
     __syncthreads();
-    if (snap) {
+    if (snap && tqu == 1) {
+      // one observation row (decode): each head's softmax statistics from the score kernel's
+      // chunk partials, and the max-pooled probability of a window as exp(max logit - M) / L
+      // (exp and the division are monotone, so this is the pool of the probabilities)
+      const int warp = tid >> 5, lane = tid & 31;
+      const int nch = (S + a.chunk_len - 1) / a.chunk_len;
+      for (int hh = warp; hh < L.Hk; hh += blockDim.x >> 5) {
+        const float* pp = a.part + ((size_t)s * L.Hk + hh) * a.tqmax * a.max_chunks * 2;
+        float M = kNegInf;
+        for (int c2 = lane; c2 < nch; c2 += 32) M = fmaxf(M, pp[2 * c2]);
+        M = warp_max(M);
+        float Ls = 0.f;
+        for (int c2 = lane; c2 < nch; c2 += 32) Ls += (pp[2 * c2] == kNegInf) ? 0.f : pp[2 * c2 + 1] * __expf(pp[2 * c2] - M);
+        Ls = warp_sum(Ls);
+        if (lane == 0) {
+          sStat[2 * hh] = M;
+          sStat[2 * hh + 1] = Ls;
+        }
+      }
+      __syncthreads();
+      const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
+      const bool pmax = L.pooling == HC_POOL_MAX;
+      for (int t = tid; t < S; t += blockDim.x) {
+        float tot = 0.f;
+        for (int hh = 0; hh < L.Hk; ++hh) {
+          const float* lg = sLg + (size_t)hh * S;
+          const float M = sStat[2 * hh], Ls = sStat[2 * hh + 1];
+          float v;
+          if (pad == 0 || pmax) {
+            float mx = kNegInf;
+            for (int u = max(0, t - pad); u <= min(S - 1, t + pad); ++u) mx = fmaxf(mx, lg[u]);
+            v = (mx == kNegInf) ? 0.f : __expf(mx - M) / Ls;
+          } else {
+            v = 0.f;
+            for (int u = max(0, t - pad); u <= min(S - 1, t + pad); ++u)
+              v += (lg[u] == kNegInf) ? 0.f : __expf(lg[u] - M) / Ls;
+            v /= (float)L.pool_kernel;
+          }
+          tot += v;
+        }
+        sTok[t] = tot / (float)L.Hk;
+      }
+    } else if (snap) {
       const int warp = tid >> 5, lane = tid & 31;
       for (int r = warp; r < rows; r += blockDim.x >> 5) {
         const float* lg = sLg + (size_t)r * S;
