@@ -558,6 +558,11 @@ def _timed_graph_steps(step_fn, first, K, dev, world):
                 step_fn(i)
         graph_upload(g, cur)
         flush.zero_()
+        if world > 1:
+            # ranks capture at different host speeds: line them up outside the timed region so a
+            # collective inside the step does not time the other rank's capture
+            torch.cuda.synchronize(dev)
+            torch.distributed.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(cur)
         g.replay()
