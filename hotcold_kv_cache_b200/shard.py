@@ -59,7 +59,8 @@ class ShardedColdSearch:
 
     search(rows, n, qvecs, k) takes, for each of B sequences, this rank's rows of the cold
     index (rows[b] covers entries token_range(n[b], rank, world)) and its query vector, and
-    returns the (B, k) global top-k ids on every rank. One all-gather per search, whatever B.
+    returns the (B, k) global top-k ids on every rank. One all-gather per search, whatever B
+    (scores and ids travel together in one int32 buffer).
     `local` and `merge` default to the CUDA kernels; a test may pass host functions with the
     same contracts to check the exchange without a GPU.
     """
@@ -77,8 +78,9 @@ class ShardedColdSearch:
     def search(self, rows, n, qvecs, k: int) -> torch.Tensor:
         B = len(rows)
         dev = qvecs.device
-        sc = torch.empty((B, k), dtype=torch.float32, device=dev)
-        ids = torch.empty((B, k), dtype=torch.int32, device=dev)
+        # one buffer of (scores | ids) per sequence, so that a single all-gather exchanges both
+        packed = torch.empty((B, 2 * k), dtype=torch.int32, device=dev)
+        sc, ids = packed.view(torch.float32)[:, :k], packed[:, k:]
         for b in range(B):
             lo, _ = token_range(int(n[b]), self.rank, self.world)
             if self.local is local_topk:
@@ -87,15 +89,11 @@ class ShardedColdSearch:
                 s, i = self.local(rows[b], lo, qvecs[b], k)
                 sc[b], ids[b] = s, i
         if self.world == 1:
-            return ids  # one range: its top k, sorted with ties to the lower id, is the answer
-        if self.world > 1:
-            all_sc = torch.empty((self.world * B, k), dtype=torch.float32, device=dev)
-            all_id = torch.empty((self.world * B, k), dtype=torch.int32, device=dev)
-            self.dist.all_gather_into_tensor(all_sc, sc, group=self.group)
-            self.dist.all_gather_into_tensor(all_id, ids, group=self.group)
-            all_sc, all_id = all_sc.view(self.world, B, k), all_id.view(self.world, B, k)
-        else:
-            all_sc, all_id = sc[None], ids[None]
+            return ids.contiguous()  # one range: its top k (sorted, ties to the lower id) is the answer
+        allp = torch.empty((self.world * B, 2 * k), dtype=torch.int32, device=dev)
+        self.dist.all_gather_into_tensor(allp, packed, group=self.group)
+        allp = allp.view(self.world, B, 2 * k)
+        all_sc, all_id = allp.view(torch.float32)[:, :, :k], allp[:, :, k:]
         out = torch.empty((B, k), dtype=torch.int32, device=dev)
         for b in range(B):
             if self.merge is merge_candidates:
