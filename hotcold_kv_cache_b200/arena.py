@@ -106,9 +106,11 @@ class LayerArena:
         self._step_ok: dict = {}
         self.launches = 0  # kernels launched by the decode-path ops (append/compress/retrieve/attend/step)
         self._build_descriptors()
-        # host mirrors
+        # host mirrors: hot and cold lengths, and the entries ever appended to each cold ring (the
+        # ring's oldest live entry sits at slot (cold_pushed - cold_count) % ccap)
         self.n_hot = np.zeros(n_seq, np.int64)
         self.cold_count = np.zeros(n_seq, np.int64)
+        self.cold_pushed = np.zeros(n_seq, np.int64)
 
     def _build_descriptors(self):
         n_seq, caps, budgets, ccaps = self.n_seq, self.caps, self.budgets, self.ccaps
@@ -347,7 +349,7 @@ class LayerArena:
             prefix, ntop = p
             ev[s] = prefix - ntop
             self.n_hot[s] = T - ev[s]
-            self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + ev[s])
+        self._cold_push(ev)
         return ev
 
     def append(self, q_pre, k_pre, v, cos, sin, pos):
@@ -412,6 +414,7 @@ class LayerArena:
         self.last_ev = (tot, capped)
         if tot:
             self.n_hot += 1 - ev
+            self.cold_pushed += ev
             np.minimum(self.cold_count + ev, self._ccaps_arr(), out=self.cold_count)
         else:
             self.n_hot += 1
@@ -448,8 +451,7 @@ class LayerArena:
              ptr(ws), ws.numel(), int(ev.max()), self._stream())
         self.launches += 2 + (1 if int(ev.max()) > 32 else 0)
         self.n_hot -= ev
-        for s in range(self.n_seq):
-            self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + ev[s])
+        self._cold_push(ev)
         return ev
 
     def retrieve(self, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0, qvec=None):
@@ -471,11 +473,10 @@ class LayerArena:
         """hc_retrieve with the scan divided by token range over the ranks of `searcher` (a
         shard.ShardedColdSearch): pooled query (hc_retrieve_query), this rank's range of every
         sequence's cold entries scored and cut to its top R (hc_cold_topk), the all-gather and
-        merge to the global top R, then the same splice on every rank (hc_splice_hits). The
-        rows of a ring that has never wrapped sit in age order from slot 0, so a token range is
-        a contiguous block of slots."""
-        if (self.cold_count >= np.asarray(self.ccaps)).any():
-            raise RuntimeError("sharded search needs cold rings that have never filled")
+        merge to the global top R, then the same splice on every rank (hc_splice_hits). A
+        token range is a range of ages (0 = the oldest live entry); on a ring that has wrapped
+        it covers at most two runs of contiguous slots (shard.age_runs), searched separately
+        and merged on this rank before the exchange."""
         if qvec is None:
             qvec = torch.empty((self.n_seq, self.F), dtype=torch.float32, device=self.device)
             qd, P = (0, 0, 0), 0
@@ -484,18 +485,22 @@ class LayerArena:
             call("hc_retrieve_query", byref(self.L), ptr(q_dense), qd[0], qd[1], qd[2], P, int(n_pool),
                  ptr(extra_sum), int(extra_n), ptr(qvec), self._stream())
             self.launches += 1
-        from .shard import token_range
-        rows, n = [], []
+        from .shard import age_runs, token_range
+        runs, n = [], []
+        heads = self.cold_head()
         for s in range(self.n_seq):
             c = int(self.cold_count[s])
             lo, hi = token_range(c, searcher.rank, searcher.world)
-            rows.append(self.cold_vec[s, lo:hi])
+            runs.append([(self.cold_vec[s, s0:s0 + cnt], age0)
+                         for s0, cnt, age0 in age_runs(int(heads[s]), self.ccaps[s], lo, hi)])
             n.append(c)
         searcher.ws = self.ws
         k = max(self.r_max, 1)
-        ids = searcher.search(rows, n, qvec, k)
+        ids = searcher.search(runs, n, qvec, k)
         call("hc_splice_hits", byref(self.L), ptr(ids), k, self._stream())
-        self.launches += 2 * self.n_seq + (self.n_seq if searcher.world > 1 else 0) + 2
+        # per sequence: scan + merge per run, a merge of two runs, the merge of the ranks; one splice
+        self.launches += sum(2 * max(len(r), 1) + (len(r) == 2) for r in runs) + \
+            (self.n_seq if searcher.world > 1 else 0) + 1
 
     def _retr_fused(self) -> bool:
         """Whether hc_retrieve runs as the one-launch cluster kernel (its shared memory fits)."""
@@ -556,9 +561,19 @@ class LayerArena:
         call("hc_cold_append", byref(self.L), ptr(k_pre), ptr(v), st[0], st[1], st[2],
              ptr(pos.to(device=self.device, dtype=torch.int64).contiguous()), ptr(idx), Te, self._stream())
         m = (evicted_idx >= 0).sum(dim=1).cpu().numpy()
-        for s in range(self.n_seq):
-            self.cold_count[s] = min(self.ccaps[s], self.cold_count[s] + int(m[s]))
+        self._cold_push(m)
         return m
+
+    def _cold_push(self, ev):
+        """Host mirror of ev[s] entries appended to each cold ring (the device ring keeps the
+        newest ccap: hc_seq_state cold_head/cold_count)."""
+        ev = np.asarray(ev, np.int64)
+        self.cold_pushed += ev
+        np.minimum(self.cold_count + ev, self._ccaps_arr(), out=self.cold_count)
+
+    def cold_head(self) -> np.ndarray:
+        """Physical slot of each ring's oldest live entry (host mirror, no synchronisation)."""
+        return (self.cold_pushed - self.cold_count) % np.maximum(self._ccaps_arr(), 1)
 
     # ------------------------------------------------------------------ views (API, not the hot path)
     # ------------------------------------------------------------------ persistence
@@ -599,6 +614,8 @@ class LayerArena:
             getattr(self, name).copy_(sd[name], non_blocking=True)
         self.n_hot[:] = sd["n_hot"]
         self.cold_count[:] = sd["cold_count"]
+        # entries ever appended, up to a multiple of the ring size: head + count
+        self.cold_pushed[:] = sd["st"][:, 2].numpy().astype(np.int64) + self.cold_count
         self._plan_cache = {}
 
     def logical_order(self, s: int) -> torch.Tensor:

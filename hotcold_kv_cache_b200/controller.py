@@ -145,8 +145,20 @@ class KVController:
         self._tails: List[dict] = []
         # a shard.ShardedColdSearch: cold searches scan only this rank's token range and merge
         # the ranks' candidates (every rank runs the same decode); None = search the whole ring
-        self.cold_search = None
+        self._cold_search = None
         self.dbg = {k: (0.0 if k == "prefetch_copy_ms_sum" else 0) for k in DBG_KEYS}
+
+    @property
+    def cold_search(self):
+        return self._cold_search
+
+    @cold_search.setter
+    def cold_search(self, searcher):
+        """Attach a shard.ShardedColdSearch (or None). Its limits on the top k are checked here,
+        against lookahead_k, instead of at the first retrieval deep in a decode."""
+        if searcher is not None and self.lookahead_k > 0:
+            searcher.check_k(self.lookahead_k)
+        self._cold_search = searcher
 
     # ------------------------------------------------------------------ setup
     def _lazy_init(self, k_pre: torch.Tensor, n_layers: int):

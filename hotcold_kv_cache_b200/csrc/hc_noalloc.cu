@@ -12,11 +12,14 @@
 // two host threads) race and must not be issued concurrently. The arrays keep the last call's
 // contents; the counters, which must start at zero, are cleared by every call.
 //
-// Set-up: the first call on a device (with that device current) resolves the arrays' device
-// addresses with cudaGetSymbolAddress; make that first call before any stream capture.
+// Set-up: every call resolves the arrays' device addresses on the current device with
+// cudaGetSymbolAddress (cheap, and never stale: a device reset reloads the module and may move
+// them). Under CUDA's lazy module loading (the 12.x default) the arrays are committed on a device
+// when the first call there loads the module, so make that first call before the caller's own
+// pool reserves the device's memory, and before any stream capture; or run the process with
+// CUDA_MODULE_LOADING=EAGER, which commits them when the library is loaded.
 
 #include <cstdio>
-#include <mutex>
 
 #include "hc_internal.cuh"
 
@@ -35,28 +38,16 @@ struct DevicePtrs {
   int32_t* counters = nullptr;
 };
 
-std::mutex g_mu;
-DevicePtrs g_ptrs[64];
-
-// The arrays' device addresses on the current device, resolved once per device.
+// The arrays' device addresses on the current device, resolved on every call.
 cudaError_t device_ptrs(DevicePtrs& out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  void* s = nullptr;
+  void* c = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&s, g_scratch);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(g_mu);
-  DevicePtrs& p = g_ptrs[dev];
-  if (!p.scratch) {
-    void* s = nullptr;
-    void* c = nullptr;
-    e = cudaGetSymbolAddress(&s, g_scratch);
-    if (e != cudaSuccess) return e;
-    e = cudaGetSymbolAddress(&c, g_counters);
-    if (e != cudaSuccess) return e;
-    p.scratch = s;
-    p.counters = static_cast<int32_t*>(c);
-  }
-  out = p;
+  e = cudaGetSymbolAddress(&c, g_counters);
+  if (e != cudaSuccess) return e;
+  out.scratch = s;
+  out.counters = static_cast<int32_t*>(c);
   return cudaSuccess;
 }
 

@@ -143,8 +143,11 @@ HC_API int hc_attention_dense(const void* q, const void* k, const void* v, const
  * reserved by its own pool. Scratch and counters live in static device arrays
  * of the library (8 MiB + 4096 counters, held on every GPU that loads it until
  * exit); shapes needing more are rejected with HC_ERR_UNSUPPORTED. Calls share
- * those arrays, so calls that overlap on the GPU race. The first call on a
- * device resolves the arrays' addresses; make it before any stream capture.
+ * those arrays, so calls that overlap on the GPU race. Every call resolves the
+ * arrays' addresses on the current device. Under lazy module loading (the CUDA
+ * 12.x default) the arrays are committed when the first call on a device loads
+ * the module: make that call before the caller's pool reserves the device's
+ * memory and before any stream capture, or set CUDA_MODULE_LOADING=EAGER.
  * Allocates nothing: no cudaMalloc/cudaFree.
  */
 HC_API int hc_attention_dense_noalloc(const void* q, const void* k, const void* v, const uint8_t* mask, void* out,

@@ -375,6 +375,13 @@ class OracleLayer:
         # records for tests
         self.events = []          # dicts per retrieval: step, ids, pos, valid, kmem
         self.compress_log = []    # dicts per compression: step, S, keep, evicted, gap
+        # optional test hooks that may replace a selection of this restatement by another one
+        # that differs only at a near-tie of its boundary (a parity test adopts the selection
+        # of the implementation under test there and goes on comparing):
+        #   resolve_keep(step, b, scores, prefix_len, n_top, top, P_b) -> top indices to keep
+        #   resolve_hits(step, b, scores, ids, ring_pos) -> ring ids of the hits, best first
+        self.resolve_keep = None
+        self.resolve_hits = None
 
     # -- hot tier ------------------------------------------------------------
     def _compress(self, q_obs, step):
@@ -389,6 +396,9 @@ class OracleLayer:
         for b in range(B):
             sc = token_scores(self.pol, q_obs[b], self.K[b], self.scale, self.dt)
             top = topk_lower_index(sc[:prefix_len], n_top) if n_top > 0 else np.zeros(0, np.int64)
+            if self.resolve_keep is not None:
+                top = np.sort(np.asarray(self.resolve_keep(step, b, sc[:prefix_len], prefix_len, n_top, top,
+                                                           self.P[b]), np.int64))
             keep = np.concatenate([top, np.arange(prefix_len, S)])
             ev = np.setdiff1d(np.arange(prefix_len), top)
             keep_all.append(keep)
@@ -431,6 +441,10 @@ class OracleLayer:
                 continue
             qv = query_vector(q_rows_per_b[b], self.faiss_dim, self.normalize, self.dt)
             ids, _ = self.cold[b].search(qv, R)
+            if self.resolve_hits is not None:
+                X = np.stack(list(self.cold[b].vec), axis=0)
+                ids = np.asarray(self.resolve_hits(step, b, X @ np.asarray(qv, np.float64), ids,
+                                                   np.asarray(self.cold[b].pos, np.int64)), np.int64)
             ids_all.append(ids)
             for j, i in enumerate(ids):
                 kpre[b, :, j] = self.cold[b].kpre[i]
@@ -505,7 +519,8 @@ class OracleLayer:
             if self.step_count % self.window_size == 0:
                 self.dbg["retrieval_skipped_no_cold"] += 1
         r = self.pol.recent
-        for c0, c1 in zip(bounds[:-1], bounds[1:]):
+        for ci, (c0, c1) in enumerate(zip(bounds[:-1], bounds[1:])):
+            self.chunk_index = ci
             pos = np.arange(c0, c1, dtype=np.int64)
             cos, sin = rope_cos_sin(pos, self.inv_freq, self.att_scale, self.dt)
             q_post = apply_rope(q_pre[:, :, c0:c1], cos, sin, self.dt)
@@ -597,10 +612,14 @@ class OracleLayer:
         return [np.array(list(c.pos), np.int64) for c in self.cold]
 
 
-def run_layer(inputs: dict, n_steps: int, chunks=None, **kw):
+def run_layer(inputs: dict, n_steps: int, chunks=None, follow=None, **kw):
     """Drive OracleLayer over `inputs` (synth.layer_inputs layout), the prompt whole or in
-    chunks with the given boundaries. Returns (layer, outs (n,B,Hq,D), hot_pos list per step)."""
+    chunks with the given boundaries. `follow`, a test object with attach(layer), installs
+    the resolve_keep / resolve_hits hooks. Returns (layer, outs (n,B,Hq,D), hot_pos list per
+    step)."""
     layer = OracleLayer(**kw)
+    if follow is not None:
+        follow.attach(layer)
     if chunks is None:
         layer.prefill(inputs["q_pre"], inputs["k_pre"], inputs["v"])
     else:

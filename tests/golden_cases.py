@@ -66,3 +66,27 @@ def assert_close(actual, desired, dtype, what=""):
     err = np.abs(a - d) - rel * np.abs(d)
     worst = float(err.max() / scale) if err.size else 0.0
     assert worst <= rel, f"{what}: max scaled error {worst:.3e} > {rel:.1e}"
+
+
+# the fp16 band of a comparison with the reference's own fp16-logit selections: its logits are
+# rounded to fp16, so its scores carry relative errors up to about 1e-3
+REF_F16_BAND = 2e-3
+
+
+def assert_keep_within_band(kept_pos, ref_keep, ref_scores, prefix_len, n_top, band=REF_F16_BAND, what=""):
+    """A prompt compression's kept positions against the reference's keep set: equal, except
+    for tokens of the prefix whose reference score lies within `band` (relative) of both sides
+    of the reference's own top-n_top boundary. Returns the number of such swaps."""
+    sc = np.asarray(ref_scores, np.float64)[:prefix_len]
+    got = set(int(x) for x in np.asarray(kept_pos).ravel())
+    want = set(int(x) for x in np.asarray(ref_keep).ravel())
+    assert len(got) == len(want), f"{what}: kept {len(got)} tokens, reference {len(want)}"
+    order = np.sort(sc)[::-1]
+    thr_in, thr_out = order[n_top - 1], order[n_top]
+    rel = lambda a, b: abs(a - b) / max(abs(a), abs(b), 1e-300)
+    diff = got ^ want
+    for t in diff:
+        assert t < prefix_len, f"{what}: the recent window differs at {t}"
+        g = max(rel(sc[t], thr_in), rel(sc[t], thr_out))
+        assert g <= band, f"{what}: token {t} kept/evicted differently, {g:.2e} from the boundary"
+    return len(diff) // 2

@@ -1,6 +1,10 @@
 """CUDA hot path of one layer against the CPU oracle and against the golden
 vectors of the reference itself: attention outputs, hot sets after every step,
-cold ring contents, retrieved sets, re-rotated held keys and debug counters."""
+cold ring contents, retrieved sets, re-rotated held keys and debug counters.
+
+Every test compares every step. Where the oracle's selection (float64 scores) and the CUDA
+path's (float32) differ only at a near-tie of the top-k boundary (relative gap <= 1e-4), the
+oracle adopts the CUDA selection and the comparison goes on (tests/oracle_follow.py)."""
 
 import math
 
@@ -9,6 +13,7 @@ import pytest
 import torch
 
 from golden_cases import LAYER_CASES, assert_close, inputs, load, oracle_kwargs, split_hot
+from oracle_follow import NEAR, assert_same_run, run_following
 
 pytestmark = pytest.mark.gpu
 
@@ -20,19 +25,9 @@ def _run(case, model_cos=True):
     return run_cuda_layer(case, inputs(case), case["steps"], model_cos=model_cos)
 
 
-def _compare_layer(res, case, layer, o_outs, o_hot, near_tie=1e-4):
-    """Step-by-step comparison. A hot-set difference is accepted only where the oracle's
-    selection boundary has a relative score gap within `near_tie`; the states differ from
-    there on, so the comparison stops. Returns the number of steps compared."""
-    dt = case["dtype"]
-    n = len(o_hot)
-    for i in range(n):
-        if not np.array_equal(res["hot"][i], o_hot[i]):
-            gaps = [e["gap"] for e in layer.compress_log if e["step"] == i + 1]
-            assert gaps and min(gaps) <= near_tie, f"hot set differs at step {i + 1} (gap {gaps})"
-            return i
-        assert_close(res["outs"][i], o_outs[i], dt, f"attention step {i + 1}")
-    return n
+def _oracle(c, inp, res, chunks=None, near=NEAR):
+    """The oracle over the same inputs, following the CUDA run at near-ties (gap <= near)."""
+    return run_following(O, inp, c["steps"], res, near=near, chunks=chunks, **oracle_kwargs(c))
 
 
 @pytest.mark.parametrize("name", LAYER_CASES)
@@ -40,10 +35,10 @@ def _compare_layer(res, case, layer, o_outs, o_hot, near_tie=1e-4):
 def test_layer_vs_oracle_and_golden(name, model_cos):
     g = load(name)
     c = g["case"]
-    layer, o_outs, o_hot = O.run_layer(inputs(c), c["steps"], **oracle_kwargs(c))
     res = _run(c, model_cos)
-    steps = _compare_layer(res, c, layer, o_outs, o_hot)
-    assert steps == c["steps"], "golden cases are chosen free of near-ties"
+    layer, o_outs, o_hot, fc = _oracle(c, inputs(c), res)
+    assert fc.adopted == [], "golden cases are chosen free of near-ties"
+    assert assert_same_run(res, layer, o_outs, o_hot, c["dtype"], c["steps"]) == c["steps"]
     # against the reference's own outputs
     assert_close(res["outs"], g["outs"], c["dtype"], "attention vs reference")
     for i, (a, b) in enumerate(zip(res["hot"], split_hot(g))):
@@ -54,13 +49,6 @@ def test_layer_vs_oracle_and_golden(name, model_cos):
         assert np.array_equal(np.stack(cold), g["cold_pos"])
     for b, cp in enumerate(layer.cold_positions()):
         assert np.array_equal(cold[b], cp)
-    # retrieved sets: same steps, same positions and validity, held keys re-rotated alike
-    assert sorted(res["held"]) == [e["step"] for e in layer.events]
-    for e in layer.events:
-        pos, valid, k = res["held"][e["step"]]
-        assert np.array_equal(valid, e["valid"]), e["step"]
-        assert np.array_equal(pos[valid], e["pos"][e["valid"]]), e["step"]
-        assert_close(k, e["kmem"], c["dtype"], f"held keys step {e['step']}")
     if "ret_pos" in g:
         for e, p, v in zip(sorted(res["held"]), g["ret_pos"], g["ret_valid"]):
             pos, valid, _ = res["held"][e]
@@ -90,26 +78,59 @@ def test_fused_step_matches_split_ops(name):
     assert fused["ctrl"].device_status() == 0
 
 
+def bench_case(policy="snapkv", steps=63, T=8192):
+    """The benchmark's layer configuration (bench.py config()): fp16, 32/8 heads, D 128, an
+    8192-token prompt compressed to budget 512, top-64 retrieval every 16 steps from a pool of
+    4 queries, held until replaced, no prompt-end retrieval."""
+    recent = 32 if policy == "snapkv" else 128
+    return dict(B=1, Hq=32, Hk=8, D=128, T=T, steps=steps, dtype="float16", policy=policy, cap=512,
+                recent=recent, topk_ratio=0.0 if policy == "snapkv" else max(0.05, 0.75 - recent / 512),
+                pool_kernel=7, ccap=32768, faiss_dim=128, window_size=16, pool=4, R=64, hold=True, rap=False,
+                theta=500000.0, seed=1234)
+
+
+def test_bench_configuration_all_steps():
+    """The exact layer configuration bench.py times, two layers chained as in a model (each
+    layer's step launched right after the previous layer's), 63 decode steps through the fused
+    step with the decode-step retrievals (steps 15, 31, 47, 63) through hc_retrieve_decode;
+    every step of both layers against the oracle: hot sets, attention outputs, retrieved sets
+    and re-rotated held keys, counters."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import run_cuda_layers
+    c = bench_case()
+    ins = [synth.layer_inputs(c["seed"] + li, 1, 32, 8, 128, c["T"], c["steps"], "float16") for li in range(2)]
+    res = run_cuda_layers(c, ins, c["steps"], fused=True)
+    ctrl = res[0]["ctrl"]
+    # one step_kernel per layer-step, one retr_kernel per search, nothing else
+    n_search = c["steps"] // c["window_size"]
+    for li in range(2):
+        assert ctrl.arenas[li].launches == c["steps"] + n_search, "the fused kernels did not run"
+    for li in range(2):
+        layer, o_outs, o_hot, fc = _oracle(c, ins[li], res[li])
+        assert assert_same_run(res[li], layer, o_outs, o_hot, "float16", c["steps"], f"layer {li}") == 63
+        assert [e["step"] for e in layer.events] == [15, 31, 47, 63]
+        assert len(layer.compress_log) == 1 + c["steps"]
+        for k, v in layer.dbg.items():
+            assert ctrl.dbg[k] == 2 * v, (k, ctrl.dbg[k], v)
+    assert ctrl.device_status() == 0
+
+
 @pytest.mark.parametrize("policy", ["snapkv", "hotcold"])
 def test_fused_step_bench_geometry(policy):
     """The benchmark's layer geometry (fp16, 32/8 heads, budget 512, 64 held): 289 tokens per
-    CTA, more than its 256 threads. Fused against the oracle and against the split ops."""
+    CTA, more than its 256 threads. Fused against the oracle over every step and against the
+    split ops, with a 1024-token prompt and a search every 4 steps."""
     from hotcold_kv_cache_b200 import synth
     from cuda_runner import run_cuda_layer
-    recent = 32 if policy == "snapkv" else 128
-    c = dict(B=1, Hq=32, Hk=8, D=128, T=1024, steps=8, dtype="float16", policy=policy, cap=512, recent=recent,
-             topk_ratio=0.0 if policy == "snapkv" else 0.5, pool_kernel=7, ccap=4096, faiss_dim=128,
-             window_size=1 << 20, pool=4, R=64, hold=True, rap=True, theta=500000.0, seed=77)
+    c = dict(bench_case(policy, steps=12, T=1024), window_size=4, rap=True, ccap=4096, seed=77)
     inp = synth.layer_inputs(c["seed"], 1, 32, 8, 128, c["T"], c["steps"], "float16")
-    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], **oracle_kwargs(c))
     fused = run_cuda_layer(c, inp, c["steps"], fused=True)
     split = run_cuda_layer(c, inp, c["steps"], fused=False)
-    # one launch per fused step, plus the one-launch prompt-end retrieval
-    assert fused["ctrl"].arenas[0].launches == c["steps"] + 1, "the fused step did not run"
     for i in range(c["steps"]):
         assert np.array_equal(fused["hot"][i], split["hot"][i]), f"fused vs split hot set, step {i + 1}"
         assert_close(fused["outs"][i], split["outs"][i], "float16", f"fused vs split, step {i + 1}")
-    assert _compare_layer(fused, c, layer, o_outs, o_hot, near_tie=2e-3) >= 1
+    layer, o_outs, o_hot, _ = _oracle(c, inp, fused)
+    assert assert_same_run(fused, layer, o_outs, o_hot, "float16", c["steps"]) == c["steps"]
     assert fused["ctrl"].device_status() == 0
 
 
@@ -123,12 +144,10 @@ def test_random_configs_vs_oracle(dtype, policy):
              topk_ratio=0.5, pool_kernel=7, ccap=200, faiss_dim=128, window_size=3, pool=4, R=12, hold=True,
              rap=True, theta=500000.0, seed=4242)
     inp = synth.layer_inputs(c["seed"], c["B"], c["Hq"], c["Hk"], c["D"], c["T"], c["steps"], dtype)
-    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], **oracle_kwargs(c))
     from cuda_runner import run_cuda_layer
     res = run_cuda_layer(c, inp, c["steps"])
-    near = 1e-4 if dtype == "float32" else 2e-3 if dtype == "float16" else 2e-2
-    steps = _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near)
-    assert steps >= 1
+    layer, o_outs, o_hot, _ = _oracle(c, inp, res)
+    assert assert_same_run(res, layer, o_outs, o_hot, dtype, c["steps"]) == c["steps"]
     assert res["ctrl"].device_status() == 0
 
 
@@ -141,14 +160,12 @@ def test_cfg0_full_size():
              topk_ratio=0.0, pool_kernel=7, ccap=4096, faiss_dim=128, window_size=1 << 20, pool=8, R=64,
              hold=True, rap=True, theta=500000.0, seed=0)
     inp = synth.layer_inputs(c["seed"], 1, 32, 8, 128, 4096, 63, "float32")
-    layer, o_outs, o_hot = O.run_layer(inp, 63, **oracle_kwargs(c))
     from cuda_runner import run_cuda_layer
     res = run_cuda_layer(c, inp, 63)
-    steps = _compare_layer(res, c, layer, o_outs, o_hot)
-    assert steps >= 1
-    if steps == 63:
-        for k, v in layer.dbg.items():
-            assert res["ctrl"].dbg[k] == v, k
+    layer, o_outs, o_hot, _ = _oracle(c, inp, res)
+    assert assert_same_run(res, layer, o_outs, o_hot, "float32", 63) == 63
+    for k, v in layer.dbg.items():
+        assert res["ctrl"].dbg[k] == v, k
 
 
 @pytest.mark.parametrize("dtype,D,recent,T", [("float16", 128, 32, 2048), ("bfloat16", 128, 20, 1537),
@@ -164,10 +181,28 @@ def test_snapkv_prompt_scoring_tensor_cores(dtype, D, recent, T):
              topk_ratio=0.0, pool_kernel=7, ccap=4096, faiss_dim=D, window_size=1 << 20, pool=4, R=16,
              hold=True, rap=True, theta=500000.0, seed=91 + D + recent)
     inp = synth.layer_inputs(c["seed"], c["B"], c["Hq"], c["Hk"], D, T, c["steps"], dtype)
-    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], **oracle_kwargs(c))
     res = run_cuda_layer(c, inp, c["steps"])
-    near = 2e-3 if dtype == "float16" else 2e-2
-    assert _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near) >= 1
+    layer, o_outs, o_hot, _ = _oracle(c, inp, res)
+    assert assert_same_run(res, layer, o_outs, o_hot, dtype, c["steps"]) == c["steps"]
+    assert res["ctrl"].device_status() == 0
+
+
+def test_snapkv_f16_prompt_vs_reference():
+    """The tensor-core prompt scoring (fp16, 2048 tokens, window 32, max-pool 7, budget 256)
+    against the reference's own SnapKV selection (tests/golden/snapkv_f16_prompt.npz): kept set
+    equal up to tokens within the fp16 band of the reference's boundary; then the prompt and one
+    decode step against the oracle, every selection within 1e-4."""
+    from golden_cases import assert_keep_within_band
+    from cuda_runner import run_cuda_layer
+    g = load("snapkv_f16_prompt")
+    c = g["case"]
+    inp = inputs(c)
+    res = run_cuda_layer(c, inp, c["steps"])
+    T, W = c["T"], c["recent"]
+    assert_keep_within_band(res["hot0"][0][0], g["keep_idx"][0], g["token_scores"][0], T - W, c["cap"] - W,
+                            what="CUDA vs reference")
+    layer, o_outs, o_hot, _ = _oracle(c, inp, res)
+    assert assert_same_run(res, layer, o_outs, o_hot, "float16", c["steps"]) == c["steps"]
     assert res["ctrl"].device_status() == 0
 
 
@@ -236,18 +271,15 @@ def test_chunked_prefill_vs_oracle(dtype, policy, chunks):
              ccap=2000, faiss_dim=128, window_size=1 << 20, pool=8, R=16, hold=True, rap=True, theta=500000.0,
              seed=515)
     inp = synth.layer_inputs(c["seed"], 2, 8, 2, 128, c["T"], c["steps"], dtype)
-    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], chunks=chunks, **oracle_kwargs(c))
     res = run_cuda_layer(c, inp, c["steps"], chunks=chunks)
-    near = 1e-4 if dtype == "float32" else 2e-3 if dtype == "float16" else 2e-2
-    steps = _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near)
-    assert steps >= 1
-    if steps == c["steps"]:
-        got = cold_positions(res["ctrl"])
-        want = layer.cold_positions()
-        for b in range(2):
-            assert np.array_equal(np.sort(got[b]), np.sort(want[b])), f"cold ring of sequence {b}"
-        for k, v in layer.dbg.items():
-            assert res["ctrl"].dbg[k] == v, k
+    layer, o_outs, o_hot, _ = _oracle(c, inp, res, chunks=chunks)
+    assert assert_same_run(res, layer, o_outs, o_hot, dtype, c["steps"]) == c["steps"]
+    got = cold_positions(res["ctrl"])
+    want = layer.cold_positions()
+    for b in range(2):
+        assert np.array_equal(np.sort(got[b]), np.sort(want[b])), f"cold ring of sequence {b}"
+    for k, v in layer.dbg.items():
+        assert res["ctrl"].dbg[k] == v, k
     assert res["ctrl"].device_status() == 0
 
 
@@ -262,8 +294,7 @@ def test_split_attention_large_batch_vs_oracle(dtype):
              topk_ratio=0.0, pool_kernel=7, ccap=1000, faiss_dim=128, window_size=2, pool=1, R=16, hold=True,
              rap=True, theta=500000.0, seed=2024)
     inp = synth.layer_inputs(c["seed"], 16, 32, 8, 128, c["T"], c["steps"], dtype)
-    layer, o_outs, o_hot = O.run_layer(inp, c["steps"], **oracle_kwargs(c))
     res = run_cuda_layer(c, inp, c["steps"], fused=False)
-    near = 1e-4 if dtype == "float32" else 2e-3
-    assert _compare_layer(res, c, layer, o_outs, o_hot, near_tie=near) >= 1
+    layer, o_outs, o_hot, _ = _oracle(c, inp, res)
+    assert assert_same_run(res, layer, o_outs, o_hot, dtype, c["steps"]) == c["steps"]
     assert res["ctrl"].device_status() == 0

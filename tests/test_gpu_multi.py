@@ -8,6 +8,7 @@ import pytest
 import torch
 
 from golden_cases import assert_close, oracle_kwargs
+from oracle_follow import assert_same_run, run_following
 
 pytestmark = pytest.mark.gpu
 
@@ -56,23 +57,31 @@ def test_cold_topk_vs_oracle_and_shards(n, F, k):
 
 
 class _EmulatedRanks:
-    """The ranks of a sharded search emulated in one process: search() scans every rank's
-    token range of the arena's cold index and merges them as the all-gather would."""
+    """The ranks of a sharded search emulated in one process: search() runs every rank's
+    search of its token range (the age runs of the arena's cold ring that rank r would get)
+    and merges them as the all-gather would."""
 
-    def __init__(self, world, cold_vec):
-        self.rank, self.world, self.ws, self.cold_vec = 0, world, None, cold_vec
+    def __init__(self, world, arena_of):
+        self.rank, self.world, self.ws, self.arena_of = 0, world, None, arena_of
 
-    def search(self, rows, n, qvecs, k):
-        from hotcold_kv_cache_b200.shard import local_topk, merge_candidates, token_range
+    def check_k(self, k):
+        from hotcold_kv_cache_b200.shard import ShardedColdSearch
+        ShardedColdSearch(rank=0, world=self.world).check_k(k)
+
+    def search(self, runs, n, qvecs, k):
+        from hotcold_kv_cache_b200.shard import ShardedColdSearch, age_runs, merge_candidates, token_range
+        a = self.arena_of()
+        heads = a.cold_head()
         out = torch.empty((len(n), k), dtype=torch.int32, device=qvecs.device)
         for b in range(len(n)):
-            cs, ci = [], []
+            cs = torch.empty((self.world, k), dtype=torch.float32, device=qvecs.device)
+            ci = torch.empty((self.world, k), dtype=torch.int32, device=qvecs.device)
             for r in range(self.world):
                 lo, hi = token_range(int(n[b]), r, self.world)
-                s_r, i_r = local_topk(self.cold_vec[b, lo:hi], lo, qvecs[b], k)
-                cs.append(s_r)
-                ci.append(i_r)
-            _, out[b] = merge_candidates(torch.cat(cs), torch.cat(ci), self.world, k)
+                rr = [(a.cold_vec[b, s0:s0 + c], age0) for s0, c, age0 in age_runs(int(heads[b]), a.ccaps[b], lo, hi)]
+                one = ShardedColdSearch(rank=r, world=self.world)
+                one._local_runs(rr, qvecs[b], k, (cs[r], ci[r]))
+            merge_candidates(cs.view(-1), ci.view(-1), self.world, k, out_id=out[b])
         return out
 
 
@@ -94,7 +103,7 @@ def test_sharded_retrieval_matches_single_device(dtype):
     ref = [t.clone() for t in (a.held_k, a.held_v, a.held_pos, a.held_valid, a.held_src)]
     a.held_k.zero_()
     a.held_src.fill_(-1)
-    em = _EmulatedRanks(4, a.cold_vec)
+    em = _EmulatedRanks(4, lambda: a)
     a.retrieve_sharded(em, q_dense=q_tail)
     got = (a.held_k, a.held_v, a.held_pos, a.held_valid, a.held_src)
     for r, g2, name in zip(ref, got, ("held_k", "held_v", "held_pos", "held_valid", "held_src")):
@@ -116,14 +125,39 @@ def test_ragged_batch_vs_oracle(dtype, policy):
              window_size=1 << 20, pool=8, R=16, hold=True, rap=True, theta=500000.0)
     ins = [synth.layer_inputs(900 + b, 1, 8, 2, 128, lens[b], steps, dtype) for b in range(3)]
     res = run_cuda_ragged(c, ins, budgets, ccaps, steps)
-    near = 1e-4 if dtype == "float32" else 2e-3 if dtype == "float16" else 2e-2
+    from cuda_runner import ragged_seq
     for b in range(3):
         cb = dict(c, B=1, T=lens[b], cap=budgets[b], ccap=ccaps[b])
-        layer, o_outs, o_hot = O.run_layer(ins[b], steps, **oracle_kwargs(cb))
-        for i in range(steps):
-            if not np.array_equal(res["hot"][i][b], o_hot[i][0]):
-                gaps = [e["gap"] for e in layer.compress_log if e["step"] == i + 1]
-                assert gaps and min(gaps) <= near, f"seq {b}: hot set differs at step {i + 1} (gap {gaps})"
-                break
-            assert_close(res["outs"][i][b:b + 1], o_outs[i], dtype, f"seq {b} step {i + 1}")
+        rb = ragged_seq(res, b)
+        layer, o_outs, o_hot, _ = run_following(O, ins[b], steps, rb, **oracle_kwargs(cb))
+        assert assert_same_run(rb, layer, o_outs, o_hot, dtype, steps, f"seq {b}") == steps
     assert res["ctrl"].device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", ["float16", "float32"])
+def test_sharded_retrieval_on_wrapped_ring(dtype):
+    """A decode that keeps evicting into a cold ring past its capacity (the ring wraps), with
+    a search every 3 steps through the sharded path (3 emulated ranks, so some ranks' token
+    ranges cross the end of the ring): held segments, hot sets and outputs equal those of the
+    same run with the single-device search (both on the split ops, which a sharded search
+    uses)."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import run_cuda_layer
+    c = dict(B=2, Hq=8, Hk=2, D=128, T=300, steps=40, dtype=dtype, policy="snapkv", cap=64, recent=16,
+             topk_ratio=0.0, pool_kernel=7, ccap=250, faiss_dim=128, window_size=3, pool=4, R=16,
+             hold=True, rap=True, theta=500000.0, seed=4711)
+    inp = synth.layer_inputs(c["seed"], 2, 8, 2, 128, c["T"], c["steps"], dtype)
+    single = run_cuda_layer(c, inp, c["steps"], fused=False)
+    sharded = run_cuda_layer(c, inp, c["steps"], fused=False,
+                             searcher=lambda ctrl: _EmulatedRanks(3, lambda: ctrl.arenas[0]))
+    a = sharded["ctrl"].arenas[0]
+    assert (a.cold_pushed > a.ccaps[0]).all(), "the ring did not wrap"
+    assert sorted(single["held"]) == sorted(sharded["held"])
+    for st in single["held"]:
+        for x, y in zip(single["held"][st], sharded["held"][st]):
+            assert np.array_equal(x, y), st
+    for i in range(c["steps"]):
+        assert np.array_equal(single["hot"][i], sharded["hot"][i]), i
+        assert np.array_equal(single["outs"][i], sharded["outs"][i]), i
+    assert np.array_equal(a.cold_head(), a.device_state()[:, 2])
+    assert sharded["ctrl"].device_status() == 0

@@ -65,20 +65,30 @@ def _sharded_worker(rank, world, port, out_q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
-        from hotcold_kv_cache_b200.shard import ShardedColdSearch, token_range
+        from hotcold_kv_cache_b200.shard import ShardedColdSearch, age_runs, token_range
         from hotcold_kv_cache_b200 import synth
         ns, F, k, q, index = _problem()
         s = ShardedColdSearch(local=_host_local, merge=_host_merge)
         assert (s.rank, s.world) == (rank, world)
-        rows = [torch.from_numpy(index[b][slice(*token_range(ns[b], rank, world))]) for b in range(len(ns))]
-        ids = s.search(rows, ns, torch.from_numpy(q), k).numpy()
+        runs = [[(torch.from_numpy(index[b][lo:hi]), lo)] if hi > lo else []
+                for b in range(len(ns)) for lo, hi in [token_range(ns[b], rank, world)]]
+        ids = s.search(runs, ns, torch.from_numpy(q), k).numpy()
+        # the same index in a wrapped ring: age a sits at slot (head + a) % n, so a rank's ages can
+        # cross the end of the ring and come as two runs of slots
+        wids = []
+        for b, n in enumerate(ns):
+            head = (7 * n) // 10
+            ring = np.roll(index[b], head, axis=0) if n else index[b]
+            lo, hi = token_range(n, rank, world)
+            rr = [(torch.from_numpy(ring[s0:s0 + c]), a0) for s0, c, a0 in age_runs(head, max(n, 1), lo, hi)]
+            wids.append(s.search([rr], [n], torch.from_numpy(q[b:b + 1]), k).numpy()[0])
         # the ragged partition: every rank derives the same one and the parts cover the batch
         items = synth.ragged_batch(3, 64)
         parts = synth.balanced_partition(items, world)
         mine = parts[rank]
         gathered = [None] * world
         dist.all_gather_object(gathered, mine)
-        out_q.put((rank, ids, gathered, parts))
+        out_q.put((rank, ids, gathered, parts, np.stack(wids, 0)))
     finally:
         dist.destroy_process_group()
 
@@ -94,8 +104,8 @@ def test_sharded_search_and_partition_gloo(world):
     res = {}
     try:
         for _ in range(world):
-            r, ids, gathered, parts = q.get(timeout=120)
-            res[r] = (ids, gathered, parts)
+            r, ids, gathered, parts, wids = q.get(timeout=120)
+            res[r] = (ids, gathered, parts, wids)
     finally:
         for p in procs:
             p.join(timeout=60)
@@ -110,8 +120,9 @@ def test_sharded_search_and_partition_gloo(world):
             want[: len(o)] = o
         for r in range(world):
             assert np.array_equal(res[r][0][b], want), (r, b)
+            assert np.array_equal(res[r][3][b], want), ("wrapped ring", r, b)
     assert list(res[0][0][0][:2]) == [10, 990]
     for r in range(world):
-        ids, gathered, parts = res[r]
+        ids, gathered, parts, _ = res[r]
         assert gathered == parts
         assert sorted(i for p in parts for i in p) == list(range(64))

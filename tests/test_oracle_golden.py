@@ -84,3 +84,26 @@ def test_decode_attention_edge_cases():
     big[0, 0, 2] = q[0, 0] * 100
     out = O.decode_attention(q, big, v, np.ones((1, 5), bool), 0.25, "float32")
     assert np.isnan(out[0, 0]).all()
+
+
+def test_snapkv_f16_prompt_compression():
+    """fp16 SnapKV prompt compression (2048 tokens, window 32, max-pool 7, budget 256): the
+    oracle's token scores against the reference's own (fp16 logits, scoring.py:50-79 averaged
+    over heads), and its keep set against the reference's keep_index (scoring.py:110-132) up to
+    tokens within the fp16 band of the reference's boundary."""
+    from golden_cases import assert_keep_within_band
+    g = load("snapkv_f16_prompt")
+    c = g["case"]
+    inp = inputs(c)
+    T, W = c["T"], c["recent"]
+    inv = synth.rope_inv_freq(c["D"], c["theta"])
+    cos, sin = O.rope_cos_sin(np.arange(T), inv, 1.0, c["dtype"])
+    qp = O.apply_rope(inp["q_pre"][0], cos, sin, c["dtype"])
+    kp = O.apply_rope(inp["k_pre"][0], cos, sin, c["dtype"])
+    sc = O.snapkv_token_scores(qp[:, -W:], kp, 1.0 / math.sqrt(c["D"]), c["pool_kernel"], "maxpool", c["dtype"])
+    ref = g["token_scores"][0].astype(np.float64)
+    err = np.abs(sc - ref) / np.abs(ref).max()
+    assert err.max() <= 3e-3, err.max()
+    prefix, ntop = T - W, c["cap"] - W
+    keep = np.concatenate([O.topk_lower_index(sc[:prefix], ntop), np.arange(prefix, T)])
+    assert_keep_within_band(keep, g["keep_idx"][0], ref, prefix, ntop, what="oracle vs reference")

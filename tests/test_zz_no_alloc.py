@@ -70,6 +70,37 @@ def test_noalloc_matches_workspace_entry_point_twice(dtype, code):
 def test_noalloc_rejects_shapes_beyond_its_static_area():
     from hotcold_kv_cache_b200 import _lib
     lib = _lib.load()
-    # 64 sequences x 8 KV heads x 65 chunks of partials needs more than the 8 MiB area
+    # 64 sequences x 8 KV heads x 130 chunks of 32 rows of partials needs more than the 8 MiB area
     rc = lib.hc_attention_dense_noalloc(1, 1, 1, 1, 1, None, 64, 32, 8, 4100, 128, 1, 0.1, 1, None)
     assert rc == 3 and b"scratch" in lib.hc_last_error()
+    # one row past the largest 16-sequence shape that fits
+    assert lib.hc_attention_dense_scratch_bytes(16, 32, 8, 961, 128) > 8 << 20
+    rc = lib.hc_attention_dense_noalloc(1, 1, 1, 1, 1, None, 16, 32, 8, 961, 128, 1, 0.1, 1, None)
+    assert rc == 3 and b"scratch" in lib.hc_last_error()
+
+
+def test_noalloc_accepts_the_largest_shape_that_fits():
+    """16 sequences x 960 rows: the split-K partials fill the static area to within 1 %."""
+    from hotcold_kv_cache_b200 import _lib
+    lib = _lib.load()
+    B, Hq, Hk, S, D = 16, 32, 8, 960, 128
+    need = lib.hc_attention_dense_scratch_bytes(B, Hq, Hk, S, D)
+    assert 0.99 * (8 << 20) <= need <= 8 << 20
+    torch.cuda.init()
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(7)
+    q = torch.randn((B, Hq, 1, D), generator=g, device="cuda").half()
+    k = torch.randn((B, Hk, S, D), generator=g, device="cuda").half()
+    v = torch.randn((B, Hk, S, D), generator=g, device="cuda").half()
+    m = torch.ones((B, S), dtype=torch.uint8, device="cuda")
+    want = torch.empty((B, Hq, D), dtype=torch.float16, device="cuda")
+    want_idx = torch.empty(B, dtype=torch.int64, device="cuda")
+    _reference_call(lib, q, k, v, m, want, want_idx, B, Hq, Hk, S, D, 1, stream)
+    got = torch.empty_like(want)
+    got_idx = torch.empty_like(want_idx)
+    rc = lib.hc_attention_dense_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), m.data_ptr(), got.data_ptr(),
+                                        got_idx.data_ptr(), B, Hq, Hk, S, D, 1, 1.0 / math.sqrt(D), 1, stream)
+    assert rc == 0, lib.hc_last_error()
+    torch.cuda.synchronize()
+    _close(got, want, torch.float16)
+    assert torch.equal(got_idx, want_idx)
