@@ -16,7 +16,8 @@ L2 is flushed before each replay, and each replay is bracketed by CUDA events
 on the launching stream. value = device time / layer-steps (us per layer-step,
 lower is better), max over ranks at N > 1 (each rank runs its own replica).
 
-Two more workloads (--workload), measured on request and not part of the default line:
+Three more workloads (--workload); the first two also run as sub-results of the default line
+("ragged", "cold_shard"; --no-partitioned skips them), so every N of a scaling run times them:
   ragged      the ragged continuous batch: 64 sequences of lengths
               uniform in [2048, 32768] with budgets cycling 512/1024/2048, one layer,
               partitioned over the N ranks by balanced token count, no collective on the
@@ -69,8 +70,10 @@ def parse():
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--cpu-steps", type=int, default=16)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="decode", choices=["decode", "ragged", "cold-shard", "prefill"])
+    p.add_argument("--workload", default="decode", choices=["decode", "ragged", "cold-shard", "prefill", "model"])
     p.add_argument("--seqs", type=int, default=64)
+    p.add_argument("--no-partitioned", action="store_true",
+                   help="skip the ragged-batch and sharded-cold-store sub-results of the default line")
     return p.parse_args()
 
 
@@ -149,16 +152,34 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def profiled_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if present."""
+def source_sha(name: str) -> str:
+    """First 12 hex digits of the SHA-1 of a kernel source file (csrc/<name>)."""
+    import hashlib
+    with open(os.path.join(ROOT, "hotcold_kv_cache_b200", "csrc", name), "rb") as f:
+        return hashlib.sha1(f.read()).hexdigest()[:12]
+
+
+def profiled_traffic(kernel: str, source: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary (profiles/traffic.md),
+    with where it comes from. DRAM counters cannot be read inside this run, so the figure is
+    the one ncu measured; it is withheld (None) when the kernel's source file changed since
+    that capture (the summary records the file's SHA-1)."""
     path = os.path.join(ROOT, "profiles", "traffic.md")
+    val = sha = None
     try:
         for line in open(path):
             if line.startswith(f"traffic[{kernel}]"):
-                return int(float(line.split("=", 1)[1].split()[0]))
+                val = int(float(line.split("=", 1)[1].split()[0]))
+            elif line.startswith(f"source_sha[{kernel}]"):
+                sha = line.split("=", 1)[1].strip()
     except OSError:
-        pass
-    return None
+        return None, "no ncu summary"
+    now = source_sha(source)
+    if val is None:
+        return None, "no ncu figure for this kernel"
+    if sha != now:
+        return None, f"stale: {source} changed since the ncu capture (sha {sha} vs {now})"
+    return val, f"ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, profiles/traffic.md ({source} sha {now})"
 
 
 # ------------------------------------------------------------------------------------------
@@ -381,9 +402,10 @@ def run_ours(a, rank, world):
             us_launch = statistics.median(plain) * 1e3 / c["layers"]
             timing = f"median replay time / layers over the {len(plain)} timed steps without retrieval"
     gbs = att["bytes"] / (us_launch * 1e-6) / 1e9
+    traffic, traffic_src = profiled_traffic(key, "hc_step.cu" if key == "step" else "hc_attention.cu")
     roof = {"bound": "hbm", "kernel": kname, "achieved": round(gbs, 1),
             "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
-            "traffic": profiled_traffic(key), "peak_source": f"{peak_kind} hbm_gbs",
+            "traffic": traffic, "traffic_source": traffic_src, "peak_source": f"{peak_kind} hbm_gbs",
             "bytes_per_launch": att["bytes"], "us_per_launch": round(us_launch, 3), "timing": timing}
     res = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
            "ms_per_step": round(step_ms, 4), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
@@ -701,6 +723,92 @@ def run_cold_shard(a, rank, world):
             "gpu_launches": int(launches), "ops_us_per_layer_step": ops}
 
 
+def run_model(a, rank, world):
+    """BASELINE configs[1] end to end through the reference-facing entry point: a random-init
+    32-layer Llama-3.1-8B in fp16, install_monkeypatch + build_hotcold_cache, an 8192-token
+    uniform-random prompt, budget 512 (SnapKV, window 32, max-pool 7), top-64 retrieval every 16
+    steps, held; teacher-forced decode of uniform-random tokens. Per decode token: the eager call
+    a user makes (CUDA events around model(...)), and the device time of the same step captured
+    as a CUDA graph (the host's Python out of the picture). Each rank runs its own replica."""
+    import torch
+    import hotcold_kv_cache_b200 as hc
+    from hotcold_kv_cache_b200 import synth
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    model = synth.llama8b_random(dev, seed=a.seed + rank)
+    T, K, W = a.prompt or 8192, a.steps, a.warmup
+    ctrl = hc.KVController(max_capacity_prompt=a.budget or 512, topk_ratio=0.0, recent_size=32,
+                           cpu_buffer_size=32768, faiss_dim=128, window_size=16, query_pool_size=4, lookahead_k=64,
+                           hold_retrieved=True, retrieve_after_prefill=False, policy="snapkv", pool_kernel=7,
+                           profile_overlap=False)
+    g = torch.Generator().manual_seed(a.seed + 100 + rank)
+    n = W + 2 * K
+    ids = torch.randint(0, model.config.vocab_size, (1, T + n), generator=g).to(dev)
+    hc.uninstall_monkeypatch()
+    hc.set_active_rotary_emb(model.model.rotary_emb)
+    hc.install_monkeypatch(enable_debug=False)
+    hc.set_active_kvctrl(ctrl)
+    try:
+        cache = hc.build_hotcold_cache(model, ctrl)
+        with torch.inference_mode():
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            model(input_ids=ids[:, :T], use_cache=True, past_key_values=cache, logits_to_keep=1)
+            e1.record()
+            e1.synchronize()
+            prefill_ms = e0.elapsed_time(e1)
+
+            def step(i):
+                return model(input_ids=ids[:, T + i:T + i + 1], cache_position=torch.arange(T + i, T + i + 1, device=dev),
+                             past_key_values=cache, use_cache=True, logits_to_keep=1).logits
+
+            for i in range(W):
+                step(i)
+            torch.cuda.synchronize(dev)
+            eager = []
+            for i in range(W, W + K):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                lg = step(i)
+                tok = lg[0, -1].argmax().item()  # the token a generation loop would read back
+                e1.record()
+                e1.synchronize()
+                eager.append(e0.elapsed_time(e1))
+            stream = torch.cuda.Stream(dev)
+            flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+            graphed = []
+            for i in range(W + K, W + 2 * K):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(stream):
+                    with torch.cuda.graph(gr, stream=stream):
+                        step(i)
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                gr.replay()
+                e1.record()
+                e1.synchronize()
+                graphed.append(e0.elapsed_time(e1))
+                del gr
+        if ctrl.device_status():
+            raise RuntimeError("device status word set")
+        del tok
+    finally:
+        hc.uninstall_monkeypatch()
+        hc.set_active_kvctrl(None)
+    eg, gp = statistics.median(eager), statistics.median(graphed)
+    res = {"metric": "decode ms per token through the patched Llama-3.1-8B forward (32 layers, random init)",
+           "value": round(eg, 3), "unit": "ms/token", "higher_is_better": False, "scaling": "weak",
+           "steps": K, "warmup": W, "graph_ms_per_token": round(gp, 3), "prefill_ms": round(prefill_ms, 1),
+           "config": {"workload": f"random-init Llama-3.1-8B fp16, {T}-token prompt, budget {a.budget or 512}, "
+                                  "top-64 every 16 steps, held, SnapKV", "api": "install_monkeypatch + "
+                                  "build_hotcold_cache + model(...) per token; argmax read back per token (eager)",
+                      "graph": "the same decode step captured as a CUDA graph, L2 flushed before each replay"}}
+    del model, cache, ctrl
+    return res
+
+
 def run_prefill(a, rank, world):
     import torch
     from hotcold_kv_cache_b200 import KVController
@@ -744,8 +852,92 @@ def run_prefill(a, rank, world):
             "hbm_gbs": round(kv_bytes / (us * 1e-6) / 1e9, 1)}
 
 
+def triton_bar(c, dev, sets: int = 32, reps: int = 10):
+    """The reference's own GPU decode attention, triton_evict_attention_forward (kernels.py:77-137,
+    called as patch.py:295 calls it), against this library's drop-in of the same call
+    (kernels.triton_evict_attention_forward: hc_attention_dense + evict_idx), on this GPU at the
+    benchmark's attended rows (budget + 1 hot + R held), fp16, 32/8 heads. Each is captured as
+    one CUDA graph of `sets` calls over distinct K/V buffers, replayed after an L2 flush; us per
+    call = median replay / sets."""
+    import torch
+    try:
+        from oracle.ref_shims import load_reference
+        ref = load_reference(cpu=False).hotcold_kv
+    except Exception as e:  # the reference is not installed next to the repo
+        return {"unavailable": f"reference not importable: {e}"}
+    from hotcold_kv_cache_b200.kernels import triton_evict_attention_forward as ours
+    S, Hq, Hk, D = c["budget"] + 1 + c["lookahead_k"], c["Hq"], c["Hk"], c["D"]
+    g = torch.Generator(device=dev).manual_seed(5)
+    bufs = [(torch.randn((1, Hq, 1, D), generator=g, device=dev, dtype=torch.float16),
+             torch.randn((1, Hk, S, D), generator=g, device=dev, dtype=torch.float16),
+             torch.randn((1, Hk, S, D), generator=g, device=dev, dtype=torch.float16)) for _ in range(sets)]
+    mask = torch.ones((1, S), dtype=torch.bool, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+    out = {"rows": S, "calls_per_graph": sets, "dtype": "f16"}
+    for name, fn in (("reference_triton_us", ref.triton_evict_attention_forward), ("hc_dropin_us", ours)):
+        def run():
+            for q, k, v in bufs:
+                fn(q, k, v, mask, Hq // Hk, 1.0 / math.sqrt(D))
+        run()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            run()  # warm the allocator on the capture stream
+            with torch.cuda.graph(graph, stream=stream):
+                run()
+        torch.cuda.synchronize(dev)
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            graph.replay()
+            e1.record(cur)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e3 / sets)
+        out[name] = round(statistics.median(times), 3)
+        del graph
+    out["speedup"] = round(out["reference_triton_us"] / out["hc_dropin_us"], 2)
+    return out
+
+
 # ------------------------------------------------------------------------------------------
-# CPU arm: the oracle port of the reference path on one layer
+# CPU arm: the reference's own code (baseline/_ref), else the oracle port, on one layer
+# ------------------------------------------------------------------------------------------
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def reference_cpu(c, seed, warmup, steps):
+    """The reference's own CPU path (patched forward with its SDPA decode fallback, its cache and
+    controller, SnapKV as the composition of its scoring functions, faiss -> exact flat-IP
+    stand-in; oracle/ref_shims.py) on ONE layer of the workload with every host thread: prompt
+    untimed, `warmup` + `steps` decode steps, the latter timed. Falls back to the oracle port
+    when the reference is not installed. Returns (us per layer-step, cpu_baseline dict)."""
+    import torch
+    thr = host_threads()
+    torch.set_num_threads(thr)
+    try:
+        from oracle.ref_shims import time_reference_layer
+        us, _, dbg = time_reference_layer(c, seed, warmup, steps, "cpu")
+        sample = (f"1 of {c['layers']} layers: {c['prompt']}-token prompt (untimed), {warmup} warm-up + {steps} timed "
+                  f"decode steps ({dbg['retrieval_launched']} cold searches among them), the reference's own "
+                  f"patched forward on the CPU (SDPA decode fallback), faiss unavailable: exact flat-IP stand-in")
+        return us, {"value": round(us, 1), "unit": UNIT, "cores": thr, "kind": "reference", "sample": sample}
+    except ImportError:
+        us, thr = cpu_port(c, max(warmup + steps, 1), seed)
+        return us, {"value": round(us, 1), "unit": UNIT, "cores": thr, "kind": "port",
+                    "sample": f"1 of {c['layers']} layers, {warmup + steps} decode steps, numpy restatement in "
+                              f"oracle/ (the reference is not installed under baseline/_ref)"}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU port: the oracle restatement of the reference path on one layer
 # ------------------------------------------------------------------------------------------
 def cpu_port(c, n_steps, seed):
     """Time the CPU restatement of the reference per-layer decode step (torch-free numpy port)
@@ -777,10 +969,14 @@ def cpu_port(c, n_steps, seed):
 
 
 def cpu_baseline_obj(c, n_steps, seed):
-    us, thr = cpu_port(c, n_steps, seed)
-    return {"value": round(us, 1), "unit": UNIT, "cores": thr, "kind": "port",
-            "sample": f"1 of {c['layers']} layers, {n_steps} decode steps (one retrieval per 16), "
-                      f"numpy restatement in oracle/, faiss replaced by exact flat inner product"}
+    return reference_cpu(c, seed, 0, n_steps)[1]
+
+
+def sub_result(r: dict) -> dict:
+    """A workload's line, reduced to what a sub-result of the default line needs."""
+    keep = ("metric", "value", "unit", "higher_is_better", "scaling", "ms_per_step", "steps", "warmup", "config",
+            "aggregate_hbm_gbs", "gpu_launches", "ops_us_per_step", "ops_us_per_layer_step")
+    return {k: r[k] for k in keep if k in r}
 
 
 def main():
@@ -791,14 +987,14 @@ def main():
         if rank != 0:
             return 0
         c = config(a)
-        us, thr = cpu_port(c, max(a.cpu_steps, 1), a.seed)
+        us, cb = reference_cpu(c, a.seed, a.warmup, a.steps)
         out = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": UNIT, "n_gpus": a.gpus,
-               "steps": a.cpu_steps, "warmup": 0, "ms_per_step": round(us * c["layers"] / 1e3, 3),
+               "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(us * c["layers"] / 1e3, 3),
+               "ms_per_step_note": "per layer-step time x layers (one layer of the workload is timed)",
                "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
                "data": "synthetic N(0,1) pre-RoPE q/k/v, seeded",
                "config": workload_config(c, {"parallelism": "cpu"}),
-               "cpu_baseline": {"value": round(us, 1), "unit": UNIT, "cores": thr, "kind": "port",
-                                "sample": f"1 of {c['layers']} layers, {a.cpu_steps} decode steps"},
+               "cpu_baseline": cb,
                "e2e": {"value": round(us, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(out))
         return 0
@@ -808,7 +1004,7 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     if a.workload != "decode":
-        run = {"ragged": run_ragged, "cold-shard": run_cold_shard, "prefill": run_prefill}[a.workload]
+        run = {"ragged": run_ragged, "cold-shard": run_cold_shard, "prefill": run_prefill, "model": run_model}[a.workload]
         res = run(a, rank, world)
         if world > 1:
             import torch
@@ -817,7 +1013,17 @@ def main():
         if rank == 0:
             print(json.dumps(res))
         return 0
+    import torch
     res = run_ours(a, rank, world)
+    if not a.no_partitioned:
+        # the partitioned configurations at this N, timed in the same run (every rank takes part)
+        torch.cuda.empty_cache()
+        res["ragged"] = sub_result(run_ragged(a, rank, world))
+        torch.cuda.empty_cache()
+        res["cold_shard"] = sub_result(run_cold_shard(a, rank, world))
+        torch.cuda.empty_cache()
+    if rank == 0:
+        res["triton_reference"] = triton_bar(config(a), torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
     if rank == 0 and not a.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_obj(config(a), a.cpu_steps, a.seed)
     if world > 1:

@@ -81,7 +81,7 @@ SIGNATURES = {
     "hc_step_check": (c_int, [_P, c_int]),
     "hc_retrieve_decode": (c_int, [_P, _P, _I64, c_int, _P, c_size_t, _P]),
     "hc_encode_kmap": (c_int, [_P, _P, c_int, _I64, c_int, c_int]),
-    "hc_step": (c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, c_int, _P, c_int, _P]),
+    "hc_step": (c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, c_int, _P, c_int, c_int, _P]),
 }
 
 _lib = None

@@ -25,6 +25,13 @@ from . import _lib
 from ._lib import byref, call, ptr, size
 
 
+# The last launch of this library on each stream, as (arena id, op name). hc_step may read part
+# of a layer's state before its dependency wait (overlapping those copies with the launch before
+# it) only when that launch wrote none of that state: see LayerArena._early_bits.
+_LAST_OP: dict = {}
+HC_STEP_EARLY_HOT, HC_STEP_EARLY_HELD = 1, 2
+
+
 class Workspace:
     """Grow-only scratch buffer shared by the ops of one stream."""
 
@@ -104,6 +111,7 @@ class LayerArena:
 
         self.pool_kernel, self.pooling, self.normalize, self.rope_scaling = pool_kernel, pooling, normalize, rope_scaling
         self._step_ok: dict = {}
+        self._dirty = True  # host-side (torch) writes since the last launch: no early reads next step
         self.launches = 0  # kernels launched by the decode-path ops (append/compress/retrieve/attend/step)
         self._build_descriptors()
         # host mirrors: hot and cold lengths, and the entries ever appended to each cold ring (the
@@ -158,6 +166,7 @@ class LayerArena:
         self._Lref = byref(L)
         self._caps_np = np.asarray(self.caps, np.int64)
         self._plan_cache = {}
+        self._dirty = True
 
     def _encode_kmaps(self):
         """TMA tensor maps of the hot K slab (all sequences as rows of D, 64-row boxes) and the
@@ -235,6 +244,22 @@ class LayerArena:
     def _stream(self):
         return _lib.stream_of(self.device)
 
+    def _launched(self, op: str, stream=None):
+        """Record that `op` of this arena was the last launch on the stream."""
+        _LAST_OP[stream if stream is not None else self._stream()] = (id(self), op)
+
+    def _early_bits(self, stream) -> int:
+        """HC_STEP_EARLY_* bits for a step about to launch on `stream`: what of this layer's
+        state the launch before it left alone. Another layer's launch (or none of this library)
+        writes nothing of it; this layer's decode retrieval writes the held segment only; any
+        other op of this layer, or a host-side write, may write all of it."""
+        if self._dirty:
+            return 0
+        last = _LAST_OP.get(stream)
+        if last is None or last[0] != id(self):
+            return HC_STEP_EARLY_HOT | HC_STEP_EARLY_HELD
+        return HC_STEP_EARLY_HOT if last[1] == "retrieve_decode" else 0
+
     def _fast_rows(self, t: torch.Tensor, rows: int):
         """(tensor, sequence stride) of a (n_seq, rows, D) operand without copies when it is
         contiguous and 16-byte aligned; else the general _row_major path."""
@@ -283,6 +308,7 @@ class LayerArena:
         T = k_post.shape[2]
         call("hc_store_prompt", byref(self.L), T, ptr(k_post), ptr(v), ptr(k_pre), *self._strides(k_post, v, k_pre),
              ptr(pos.contiguous()), self._stream())
+        self._launched("store_prompt")
         self.n_hot[:] = T
 
     def _strides(self, k, v, kp):
@@ -340,6 +366,7 @@ class LayerArena:
         pos = pos.contiguous()
         call("hc_compress_ex", byref(L), ptr(q_obs), qs[0], qs[1], qs[2], tq, T, ptr(k_post), ptr(v), ptr(k_pre),
              *self._strides(k_post, v, k_pre), ptr(pos), ptr(ws), ws.numel(), 1 << 30, self._stream())
+        self._launched("compress_prompt")
         ev = np.zeros(self.n_seq, np.int64)
         for s in seqs:
             p = self.plan(s, T)
@@ -368,6 +395,7 @@ class LayerArena:
             sin = sin.reshape(self.n_seq, self.D).contiguous()
         call("hc_append", byref(self.L), ptr(q), qss, ptr(k), ptr(vv), kss, ptr(cos), ptr(sin), ptr(pos),
              ptr(self.q_post), self._stream())
+        self._launched("append")
         self.launches += 1
         self.n_hot += 1
         return self.q_post
@@ -401,14 +429,17 @@ class LayerArena:
             cos = cos.reshape(self.n_seq, self.D).contiguous()
             sin = sin.reshape(self.n_seq, self.D).contiguous()
         o = self.out if out is None else out
+        stream = self._stream()
         rc = _lib.load().hc_step(self._Lref, q.data_ptr(), qss, k.data_ptr(), vv.data_ptr(), kss, ptr(cos), ptr(sin),
                                  pos.data_ptr(), 1 if use_held else 0, o.data_ptr(), 1 if overflow_nan else 0,
-                                 self._stream())
+                                 self._early_bits(stream), stream)
         if rc == 3:  # HC_ERR_UNSUPPORTED: nothing was launched
             self._step_ok[bool(use_held)] = False
             return None
         if rc != 0:
             raise RuntimeError(f"hc_step failed (code {rc}): {_lib.load().hc_last_error().decode()}")
+        self._launched("step", stream)
+        self._dirty = False
         self.launches += 1
         ev, tot, capped = self._step_plan()
         self.last_ev = (tot, capped)
@@ -428,6 +459,7 @@ class LayerArena:
         vv = v.reshape(self.n_seq, self.Hk, self.D).contiguous()
         k = k.contiguous()
         call("hc_append_rotated", byref(self.L), ptr(k), ptr(kp), ptr(vv), k.stride(0), ptr(pos), self._stream())
+        self._launched("append_rotated")
         self.n_hot += 1
 
     def compress_decode(self, q_obs):
@@ -449,6 +481,7 @@ class LayerArena:
         ws = self.ws.get(nbytes)
         call("hc_compress_ex", byref(self.L), ptr(q_obs), qs[0], qs[1], qs[2], tq, 0, None, None, None, 0, 0, 0, None,
              ptr(ws), ws.numel(), int(ev.max()), self._stream())
+        self._launched("compress_decode")
         self.launches += 2 + (1 if int(ev.max()) > 32 else 0)
         self.n_hot -= ev
         self._cold_push(ev)
@@ -466,6 +499,7 @@ class LayerArena:
         mc = int(self.cold_count.max())
         call("hc_retrieve_ex", byref(self.L), ptr(q_dense), qd[0], qd[1], qd[2], P, int(n_pool), ptr(extra_sum),
              int(extra_n), ptr(qvec), ptr(ws), ws.numel(), mc, self._stream())
+        self._launched("retrieve")
         self.launches += 1 if self._retr_fused() else (3 if qvec is not None else 4)
 
     def retrieve_sharded(self, searcher, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0,
@@ -498,6 +532,7 @@ class LayerArena:
         k = max(self.r_max, 1)
         ids = searcher.search(runs, n, qvec, k)
         call("hc_splice_hits", byref(self.L), ptr(ids), k, self._stream())
+        self._launched("retrieve_sharded")
         # per sequence: scan + merge per run, a merge of two runs, the merge of the ranks; one splice
         self.launches += sum(2 * max(len(r), 1) + (len(r) == 2) for r in runs) + \
             (self.n_seq if searcher.world > 1 else 0) + 1
@@ -529,6 +564,7 @@ class LayerArena:
             return False
         if rc != 0:
             raise RuntimeError(f"hc_retrieve_decode failed (code {rc}): {_lib.load().hc_last_error().decode()}")
+        self._launched("retrieve_decode")
         self.launches += 1
         return True
 
@@ -537,6 +573,7 @@ class LayerArena:
         qs = q_dense.stride()
         call("hc_prompt_query_sum", byref(self.L), ptr(q_dense), qs[0], qs[1], qs[2], q_dense.shape[2], ptr(out),
              self._stream())
+        self._launched("prompt_query_sum")
         return out
 
     def attend(self, q_post, cur_pos, use_held: bool, overflow_nan: bool = True, out=None):
@@ -546,6 +583,7 @@ class LayerArena:
         o = self.out if out is None else out
         call("hc_attend", byref(self.L), ptr(q), ptr(cur_pos), 1 if use_held else 0, ptr(o),
              1 if overflow_nan else 0, ptr(ws), ws.numel(), self._stream())
+        self._launched("attend")
         self.launches += 1
         return o
 
@@ -560,6 +598,7 @@ class LayerArena:
         idx = evicted_idx.to(device=self.device, dtype=torch.int64).contiguous()
         call("hc_cold_append", byref(self.L), ptr(k_pre), ptr(v), st[0], st[1], st[2],
              ptr(pos.to(device=self.device, dtype=torch.int64).contiguous()), ptr(idx), Te, self._stream())
+        self._launched("cold_append")
         m = (evicted_idx >= 0).sum(dim=1).cpu().numpy()
         self._cold_push(m)
         return m
@@ -617,6 +656,7 @@ class LayerArena:
         # entries ever appended, up to a multiple of the ring size: head + count
         self.cold_pushed[:] = sd["st"][:, 2].numpy().astype(np.int64) + self.cold_count
         self._plan_cache = {}
+        self._dirty = True
 
     def logical_order(self, s: int) -> torch.Tensor:
         return self.hot_ord[s, : int(self.n_hot[s])].long()

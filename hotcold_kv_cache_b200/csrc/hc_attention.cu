@@ -607,42 +607,84 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
 // Second output of the dense drop-in (kernels.py:103,134-137): per token the mean over query
 // heads of softmax probability times sum_d |v_d| / D, rounded to the input dtype; masked
 // tokens contribute exactly 0 (the reference's exp(-1e35)).
+// The wrapper's second result (kernels.py:134-137): loss[t] = mean over query heads of
+// softmax(q.k)[t] * sum_d |v[t]| / D, cast to the input dtype, then its argmin (first index on
+// ties, argmin_kernel). A CTA takes 32 tokens of one sequence with a warp per KV head and a lane
+// per token: the head group's query rows and final softmax statistics (written by the attention
+// kernel) sit in shared memory, so a lane reads its token's K and V rows once and needs no
+// cross-lane reductions; the per-head terms are summed in head order through shared memory.
+constexpr int kLossTok = 32;
+
 template <int DT, int D, int G>
-__global__ void __launch_bounds__(128) evict_loss_kernel(const void* q_, const void* k_, const void* v_,
-                                                         const uint8_t* mask, const float* ml, float* loss,
-                                                         int Hq, int Hk, int S, float scale) {
+__global__ void __launch_bounds__(256) evict_loss_kernel(const void* q_, const void* k_, const void* v_,
+                                                         const uint8_t* mask, const float* ml, float* loss, int Hq,
+                                                         int Hk, int S, float scale) {
   using E = Elem<DT>;
   using T = typename E::T;
+  constexpr int VE = 16 / sizeof(T);  // elements per 16-byte chunk
+  constexpr int NC = D / VE;          // chunks per row
+  extern __shared__ float sq[];       // [Hq][D] query rows, [Hq][2] (max, sum), [Hk][kLossTok] terms
+  float* sml = sq + (size_t)Hq * D;
+  float* sterm = sml + 2 * (size_t)Hq;
   const int b = blockIdx.y;
-  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= S) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  pdl_wait();
   const T* q = reinterpret_cast<const T*>(q_) + (size_t)b * Hq * D;
-  float acc = 0.f;
-  const bool m = mask[(size_t)b * S + t] != 0;
-  for (int h = 0; h < Hk; ++h) {
-    const T* kr = reinterpret_cast<const T*>(k_) + (((size_t)b * Hk + h) * S + t) * D;
-    const T* vr = reinterpret_cast<const T*>(v_) + (((size_t)b * Hk + h) * S + t) * D;
-    float av = 0.f;
-    for (int dd = lane; dd < D; dd += 32) av += fabsf(E::to_f(vr[dd]));
-    av = warp_sum(av) / (float)D;
-    for (int g = 0; g < G; ++g) {
-      const int hq = h * G + g;
-      float dot = 0.f;
-      for (int dd = lane; dd < D; dd += 32) dot = fmaf(E::to_f(q[(size_t)hq * D + dd]), E::to_f(kr[dd]), dot);
-      dot = warp_sum(dot) * scale;
-      const float M = ml[((size_t)b * Hq + hq) * 2], L = ml[((size_t)b * Hq + hq) * 2 + 1];
-      const float p = m ? __expf(dot - M) / L : 0.f;
-      acc += p * av;
-    }
+  for (int i = threadIdx.x; i < Hq * D; i += blockDim.x) sq[i] = E::to_f(q[i]);
+  for (int i = threadIdx.x; i < Hq; i += blockDim.x) {
+    sml[2 * i] = ml[((size_t)b * Hq + i) * 2];
+    sml[2 * i + 1] = ml[((size_t)b * Hq + i) * 2 + 1];
   }
-  if (lane == 0) loss[(size_t)b * S + t] = E::round(acc / (float)Hq);
+  __syncthreads();
+  const int t = blockIdx.x * kLossTok + lane;
+  const bool live = t < S;
+  const bool m = live && mask[(size_t)b * S + t] != 0;
+  for (int h = warp; h < Hk; h += nw) {
+    float term = 0.f;
+    if (live) {
+      const uint4* kr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(k_) + (((size_t)b * Hk + h) * S + t) * D);
+      const uint4* vr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(v_) + (((size_t)b * Hk + h) * S + t) * D);
+      float dot[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) dot[g] = 0.f;
+      float av = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < NC; ++c) {
+        float kf[VE], vf[VE];
+        unpack16<DT>(kr[c], kf);
+        unpack16<DT>(vr[c], vf);
+#pragma unroll
+        for (int e = 0; e < VE; ++e) av += fabsf(vf[e]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float* qg = sq + (size_t)(h * G + g) * D + c * VE;
+#pragma unroll
+          for (int e = 0; e < VE; ++e) dot[g] = fmaf(qg[e], kf[e], dot[g]);
+        }
+      }
+      av /= (float)D;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int hq = h * G + g;
+        const float p = m ? __expf(dot[g] * scale - sml[2 * hq]) / sml[2 * hq + 1] : 0.f;
+        term += p * av;
+      }
+    }
+    sterm[h * kLossTok + lane] = term;
+  }
+  __syncthreads();
+  if (threadIdx.x < kLossTok && t < S) {
+    float acc = 0.f;
+    for (int h = 0; h < Hk; ++h) acc += sterm[h * kLossTok + threadIdx.x];
+    loss[(size_t)b * S + t] = E::round(acc / (float)Hq);
+  }
 }
 
 __global__ void __launch_bounds__(1024) argmin_kernel(const float* loss, int S, int64_t* out) {
   const int b = blockIdx.x;
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_wait();
   float best = __int_as_float(0x7f800000);
   int bi = 0x7fffffff;
   for (int t = threadIdx.x; t < S; t += blockDim.x) {
@@ -799,34 +841,30 @@ size_t attention_part_bytes(int n_seq, int Hq, int Hk, int D, int max_tokens) {
 
 template <int DT, int D, int G>
 cudaError_t launch_loss_t(const void* q, const void* k, const void* v, const uint8_t* mask, const float* ml,
-                          float* loss, int B, int Hq, int Hk, int S, float scale, cudaStream_t stream) {
-  evict_loss_kernel<DT, D, G><<<dim3((S + 3) / 4, B), 128, 0, stream>>>(q, k, v, mask, ml, loss, Hq, Hk, S, scale);
-  return cudaGetLastError();
+                          float* loss, int64_t* out, int B, int Hq, int Hk, int S, float scale, cudaStream_t stream) {
+  auto kern = evict_loss_kernel<DT, D, G>;
+  const size_t smem = ((size_t)Hq * D + 2 * (size_t)Hq + (size_t)Hk * kLossTok) * sizeof(float);
+  cudaError_t e = ensure_smem(kern, smem);
+  if (e != cudaSuccess) return e;
+  const int warps = Hk < 8 ? Hk : 8;
+  e = launch_pdl(kern, dim3((S + kLossTok - 1) / kLossTok, B), dim3(32 * warps), smem, stream, q, k, v, mask, ml, loss,
+                 Hq, Hk, S, scale);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(argmin_kernel, dim3(B), dim3(1024), 0, stream, (const float*)loss, S, out);
 }
 
 cudaError_t launch_evict_idx(int dtype, const void* q, const void* k, const void* v, const uint8_t* mask,
                              const float* ml, float* loss, int64_t* out, int B, int Hq, int Hk, int S, int D,
                              float scale, cudaStream_t stream) {
   const int G = Hq / Hk;
-  cudaError_t e = cudaErrorInvalidValue;
-#define HC_LOSS_CASE(DTV)                                                                          \
-  if (dtype == DTV) {                                                                              \
-    if (D == 128 && G == 1) e = launch_loss_t<DTV, 128, 1>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream); \
-    if (D == 128 && G == 2) e = launch_loss_t<DTV, 128, 2>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream); \
-    if (D == 128 && G == 4) e = launch_loss_t<DTV, 128, 4>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream); \
-    if (D == 128 && G == 8) e = launch_loss_t<DTV, 128, 8>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream); \
-    if (D == 64 && G == 1) e = launch_loss_t<DTV, 64, 1>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream);   \
-    if (D == 64 && G == 2) e = launch_loss_t<DTV, 64, 2>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream);   \
-    if (D == 64 && G == 4) e = launch_loss_t<DTV, 64, 4>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream);   \
-    if (D == 64 && G == 8) e = launch_loss_t<DTV, 64, 8>(q, k, v, mask, ml, loss, B, Hq, Hk, S, scale, stream);   \
-  }
-  HC_LOSS_CASE(HC_F32)
-  HC_LOSS_CASE(HC_F16)
-  HC_LOSS_CASE(HC_BF16)
+#define HC_LOSS_CASE(DTV, DV, GV) \
+  if (dtype == DTV && D == DV && G == GV) return launch_loss_t<DTV, DV, GV>(q, k, v, mask, ml, loss, out, B, Hq, Hk, S, scale, stream);
+#define HC_LOSS_G(DTV, DV) HC_LOSS_CASE(DTV, DV, 1) HC_LOSS_CASE(DTV, DV, 2) HC_LOSS_CASE(DTV, DV, 4) HC_LOSS_CASE(DTV, DV, 8)
+  HC_LOSS_G(HC_F32, 128) HC_LOSS_G(HC_F16, 128) HC_LOSS_G(HC_BF16, 128)
+  HC_LOSS_G(HC_F32, 64) HC_LOSS_G(HC_F16, 64) HC_LOSS_G(HC_BF16, 64)
+#undef HC_LOSS_G
 #undef HC_LOSS_CASE
-  if (e != cudaSuccess) return e;
-  argmin_kernel<<<B, 1024, 0, stream>>>(loss, S, out);
-  return cudaGetLastError();
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace hc

@@ -321,7 +321,7 @@ int hc_step_check(const hc_layer* L, int use_held) {
   if (int rc = check_layer(L)) return rc;
   if (int rc = step_checks(L, use_held)) return rc;
   const cudaError_t e = hc::launch_step(*L, nullptr, 0, nullptr, nullptr, 0, nullptr, nullptr, nullptr, use_held, nullptr,
-                                        0, nullptr, true);
+                                        0, 0, nullptr, true);
   if (e == cudaErrorNotSupported) {
     (void)cudaGetLastError();
     return fail(HC_ERR_UNSUPPORTED, "no resident 16-CTA cluster for this shared memory size");
@@ -331,14 +331,15 @@ int hc_step_check(const hc_layer* L, int use_held) {
 
 int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const void* k_pre, const void* v,
             int64_t kv_stride_seq, const void* cos, const void* sin, const int64_t* pos, int use_held, void* out,
-            int overflow_nan, void* stream) {
+            int overflow_nan, int early, void* stream) {
   if (int rc = check_layer(L)) return rc;
   if (!q_pre || !k_pre || !v || !pos || !out) return fail(HC_ERR_ARG, "NULL tensor argument");
   if ((cos == nullptr) != (sin == nullptr)) return fail(HC_ERR_ARG, "cos and sin must both be given or both NULL");
   if (!cos && !L->inv_freq) return fail(HC_ERR_ARG, "no cos/sin and no inv_freq");
   if (int rc = step_checks(L, use_held)) return rc;
+  if (early & ~(HC_STEP_EARLY_HOT | HC_STEP_EARLY_HELD)) return fail(HC_ERR_ARG, "unknown early-read bits 0x%x", early);
   const cudaError_t e = hc::launch_step(*L, q_pre, q_stride_seq, k_pre, v, kv_stride_seq, cos, sin, pos, use_held, out,
-                                        overflow_nan, reinterpret_cast<cudaStream_t>(stream));
+                                        overflow_nan, early, reinterpret_cast<cudaStream_t>(stream));
   if (e == cudaErrorNotSupported) {
     (void)cudaGetLastError();
     return fail(HC_ERR_UNSUPPORTED, "no resident 16-CTA cluster for this shared memory size");

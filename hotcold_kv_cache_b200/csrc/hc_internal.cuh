@@ -57,7 +57,7 @@ cudaError_t launch_cold_append(const hc_layer& L, const void* kpre, const void* 
 size_t retrieve_scratch_bytes(const hc_layer& L);
 cudaError_t launch_step(const hc_layer& L, const void* q, int64_t qss, const void* k, const void* v, int64_t kvss,
                         const void* c, const void* sn, const int64_t* pos, int use_held, void* out, int overflow_nan,
-                        cudaStream_t stream, bool check_only = false);
+                        int early, cudaStream_t stream, bool check_only = false);
 size_t step_smem_bytes(const hc_layer& L, int use_held);
 int step_parts(int Hk);
 

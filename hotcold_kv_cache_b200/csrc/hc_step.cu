@@ -75,15 +75,17 @@ struct StepArgs {
   const int64_t* pos;
   void* out;
   int use_held, overflow_nan;
+  int early;  // HC_STEP_EARLY_* bits: state this launch may read before its dependency wait
   StepGeom g;
 };
 
 struct StepSmem {
-  size_t k, qb, v, q, knew, a, inv, ord, fre, held, e, pool, key, red, best, mask, cnt, word, flag, evl, o, ml, qp,
-      misc, tmem, bars, total;
+  size_t k, qb, v, q, knew, a, inv, ord, fre, held, ev, key, red, mask, evl, o, ml, qp, misc, tmem, bars, total;
 };
 
 __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
+
+__host__ __device__ inline size_t step_words(int s_cap) { return (size_t)(s_cap + 31) / 32; }
 
 __host__ __device__ inline StepSmem step_smem(int D, int esz, int G, int Hk, int max_r, const StepGeom& g) {
   StepSmem m{};
@@ -104,16 +106,11 @@ __host__ __device__ inline StepSmem step_smem(int D, int esz, int G, int Hk, int
   m.ord = take((size_t)g.s_cap * 4);         // logical order (physical slot per logical index)
   m.fre = take((size_t)g.s_cap * 4);         // free-slot stack
   m.held = take((size_t)(max_r > 0 ? max_r : 1) * 4);  // held rows attended this step
-  m.e = take((size_t)g.s_cap * 4);           // eviction logits of head h, by logical index
-  m.pool = take((size_t)Hk * g.wpc * 32 * 4);  // per-head policy values of the tokens this CTA owns
-  m.key = take((size_t)g.s_cap * 4);         // policy score keys, by logical index
+  m.ev = take((size_t)Hk * g.s_cap * 4);     // eviction logits of every head, by logical index
+  m.key = take((size_t)g.s_cap * 4);         // policy score keys of the prefix, by logical index
   m.red = take((size_t)(4 * kStepMaxCluster + 4 * kStepWarps) * 8);
-  m.best = take((size_t)kStepMaxCluster * g.wpc * 8);
-  m.mask = take((size_t)((g.s_cap + 31) / 32) * 4);
-  m.cnt = take((size_t)2 * kStepMaxCluster * 4);
-  m.word = take((size_t)g.wpc * 4);
-  m.flag = take((size_t)g.wpc * 32 * 4);
-  m.evl = take((size_t)3 * g.wpc * 32 * 4);
+  m.mask = take(step_words(g.s_cap) * 4);    // evicted tokens, one bit per logical index
+  m.evl = take((size_t)3 * g.wpc * 32 * 4);  // evicted tokens of the words this CTA owns
   m.o = take((size_t)G * D * 4);             // partials of this CTA's column block from every part
   m.ml = take((size_t)2 * G * kStepMaxCluster * 4);
   m.qp = take((size_t)G * Hk * D * esz);  // the new token's pre-RoPE query rows (query-pool push)
@@ -301,15 +298,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   int* sOrd = reinterpret_cast<int*>(smem + M.ord);
   int* sFree = reinterpret_cast<int*>(smem + M.fre);
   int* sHeld = reinterpret_cast<int*>(smem + M.held);
-  float* sE = reinterpret_cast<float*>(smem + M.e);
-  float* sPool = reinterpret_cast<float*>(smem + M.pool);
+  float* sEv = reinterpret_cast<float*>(smem + M.ev);  // [Hk][s_cap]
   uint32_t* sKey = reinterpret_cast<uint32_t*>(smem + M.key);
   float* sRed = reinterpret_cast<float*>(smem + M.red);  // per-warp partials and per-head statistics
-  unsigned long long* sBest = reinterpret_cast<unsigned long long*>(smem + M.best);
   uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + M.mask);
-  int* sCnt = reinterpret_cast<int*>(smem + M.cnt);
-  uint32_t* sWord = reinterpret_cast<uint32_t*>(smem + M.word);
-  int* sFlag = reinterpret_cast<int*>(smem + M.flag);
   int* sEvl = reinterpret_cast<int*>(smem + M.evl);
   float* sO = reinterpret_cast<float*>(smem + M.o);
   float* sML = reinterpret_cast<float*>(smem + M.ml);
@@ -326,67 +318,154 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const int hb = u0, nh = max(0, min(u1, R) - hb);          // held rows [hb, hb + nh), nh % 8 == 0
   const int nhr = max(0, min(hb + nh, d.r_max) - hb);       // of which real held rows
   const int sb = max(u0, R) - R, ns = max(0, u1 - max(u0, R));  // slots [sb, sb + ns)
-  // L2 prefetch of the step's state and of this part's rows while the preceding kernel still
-  // runs. A prefetch only warms L2, so it is safe before the dependency wait even for lines
-  // that kernel writes.
-  {
-    const int nl_ord = (d.cap * 4 + 127) / 128, nl_pos = (d.r_max * 8 + 127) / 128;
-    if (MMA && tid == 32) {
+  const int cap = d.cap;
+  // What may be read before the dependency wait: the host sets these bits when the launch
+  // preceding this one on the stream wrote none of that state of this layer (the layer's own
+  // previous step finished before that launch started). The new token's inputs are always
+  // read after the wait: the preceding kernel of a model produces them.
+  const bool early_hot = (a.early & HC_STEP_EARLY_HOT) != 0;    // slab K/V, order table, free stack
+  const bool early_held = (a.early & HC_STEP_EARLY_HELD) != 0;  // held K/V rows and their flags
+
+  // ---- copies of this part's K rows (TMA tensor boxes into the swizzled MMA layout for 16-bit
+  //      types, else bulk copies) and V rows (bulk copies), issued by warp 0 ----
+  const int nhb = nh >> 3, nsb = (ns + 63) >> 6;  // 8-row held boxes, 64-row slot boxes
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_init(&bars[0], 1);
+      mbar_init(&bars[1], 1);
+      mbar_init(&bars[2], 1);
+      fence_mbar_init();
+      const uint32_t vbytes = (uint32_t)((nhr + ns) * ROWB);
+      if constexpr (MMA) mbar_arrive_expect_tx(&bars[0], (uint32_t)((nh + 64 * nsb) * 128 * PL));
+      else mbar_arrive_expect_tx(&bars[0], vbytes);
+      mbar_arrive_expect_tx(&bars[1], vbytes);
+    }
+    __syncwarp();
+  }
+  auto issue_rows = [&](bool held) {
+    // warp 0 only: the K boxes of the held rows or of the slab slots, then their V copy
+    if constexpr (MMA) {
+      const char* kmaps = reinterpret_cast<const char*>(L.kmaps);
+      const int y_held = (s * L.Hk + h) * d.r_max + hb;
+      const int y_hot = (s * L.Hk) * L.max_cap + h * d.cap + sb;
+      const int nb = held ? nhb : nsb;
+      for (int b = lane; b < nb * PL; b += 32) {
+        const int pl = b / nb, j = b - pl * nb;
+        unsigned char* plane = reinterpret_cast<unsigned char*>(sK) + (size_t)pl * gm.krows * 128;
+        if (held) tma_load_2d(plane + (size_t)j * 8 * 128, kmaps + 128, pl * 64, y_held + 8 * j, &bars[0]);
+        else tma_load_2d(plane + (size_t)(nh + 64 * j) * 128, kmaps, pl * 64, y_hot + 64 * j, &bars[0]);
+      }
+    } else {
+      if (lane == 1 && held && nhr > 0)
+        bulk_g2s(sK, reinterpret_cast<const T*>(d.held_k) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
+                 &bars[0]);
+      if (lane == 2 && !held && ns > 0)
+        bulk_g2s(sK + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + sb) * D,
+                 (uint32_t)(ns * ROWB), &bars[0]);
+    }
+    if (lane == 3 && held && nhr > 0)
+      bulk_g2s(sV, reinterpret_cast<const T*>(d.held_v) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
+               &bars[1]);
+    if (lane == 4 && !held && ns > 0)
+      bulk_g2s(sV + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_v) + ((size_t)h * d.cap + sb) * D,
+               (uint32_t)(ns * ROWB), &bars[1]);
+  };
+  if (warp == 0) {
+    if (MMA && lane == 31) {
       prefetch_tensormap(L.kmaps);  // both maps: the hot K slab and the held K rows
       prefetch_tensormap(reinterpret_cast<const char*>(L.kmaps) + 128);
     }
+    if (early_held) issue_rows(true);
+    if (early_hot) issue_rows(false);
+  }
+  // order table and free stack: all loads first, stores to shared memory later (one round trip)
+  constexpr int kPre = 4;
+  int ov[kPre], fv[kPre];
+  auto load_order = [&]() {
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int i = tid + j * kStepThreads;
+      if (i < cap) {
+        ov[j] = d.hot_ord[i];
+        fv[j] = d.hot_free[i];
+      }
+    }
+  };
+  const bool hv_ok = a.use_held && tid < d.r_max;
+  uint8_t hval = 0;
+  int64_t hpos = 0;
+  if (early_hot) load_order();
+  if (early_held && hv_ok) {
+    hval = d.held_valid[tid];
+    hpos = d.held_pos[tid];
+  }
+  // L2 prefetch of the state that is read after the wait (the launch before this one may still
+  // write it: a prefetch only warms L2, which is safe for such lines)
+  if (tid < 64) {
+    const int nl_ord = (d.cap * 4 + 127) / 128, nl_pos = (d.r_max * 8 + 127) / 128;
     if (tid == 0) {
-      prefetch_l2(d.st);
-      if (d.held_valid) prefetch_l2(d.held_valid);
-      if (nhr > 0) {
+      if (!early_held && nhr > 0) {
         const size_t off = ((size_t)h * d.r_max + hb) * ROWB;
         bulk_prefetch_l2(reinterpret_cast<const char*>(d.held_k) + off, (uint32_t)(nhr * ROWB));
         bulk_prefetch_l2(reinterpret_cast<const char*>(d.held_v) + off, (uint32_t)(nhr * ROWB));
       }
-      if (ns > 0) {
+      if (!early_hot && ns > 0) {
         const size_t off = ((size_t)h * d.cap + sb) * ROWB;
         bulk_prefetch_l2(reinterpret_cast<const char*>(d.hot_k) + off, (uint32_t)(ns * ROWB));
         bulk_prefetch_l2(reinterpret_cast<const char*>(d.hot_v) + off, (uint32_t)(ns * ROWB));
       }
-    } else if (tid <= nl_ord) {
+      if (!early_held && a.use_held && d.held_valid) prefetch_l2(d.held_valid);
+    } else if (!early_hot && tid <= nl_ord) {
       prefetch_l2(reinterpret_cast<const char*>(d.hot_ord) + (size_t)(tid - 1) * 128);
       prefetch_l2(reinterpret_cast<const char*>(d.hot_free) + (size_t)(tid - 1) * 128);
-    } else if (a.use_held && d.held_pos && tid <= nl_ord + nl_pos) {
+    } else if (!early_held && a.use_held && d.held_pos && tid > nl_ord && tid <= nl_ord + nl_pos) {
       prefetch_l2(reinterpret_cast<const char*>(d.held_pos) + (size_t)(tid - 1 - nl_ord) * 128);
-    } else if (tid >= 64) {
-      // this step's inputs (the query rows of this head group, or all of them for the CTA that
-      // pushes the query pool; the new key, value, cos/sin and position): written by the
-      // preceding kernel in a model, so only warmed here, read after the wait
-      const int lt = tid - 64;
-      const int rb = D * ESZ;  // bytes of one head row
-      const bool all_q = rank == ncta - 1;
-      const int nq = ((all_q ? L.Hq : G) * rb + 127) / 128, nr = (rb + 127) / 128;
-      const char* qrow = reinterpret_cast<const char*>(a.q_pre) + (size_t)s * a.qss * ESZ + (all_q ? 0 : (size_t)h * G * rb);
-      if (lt < nq) {
-        prefetch_l2(qrow + (size_t)lt * 128);
-      } else if (lt < nq + nr) {
-        prefetch_l2(reinterpret_cast<const char*>(a.k_pre) + ((size_t)s * a.kvss + (size_t)h * D) * ESZ +
-                    (size_t)(lt - nq) * 128);
-      } else if (lt < nq + 2 * nr) {
-        prefetch_l2(reinterpret_cast<const char*>(a.v) + ((size_t)s * a.kvss + (size_t)h * D) * ESZ +
-                    (size_t)(lt - nq - nr) * 128);
-      } else if (a.cos && lt < nq + 3 * nr) {
-        prefetch_l2(reinterpret_cast<const char*>(a.cos) + (size_t)s * rb + (size_t)(lt - nq - 2 * nr) * 128);
-      } else if (a.sin && lt < nq + 4 * nr) {
-        prefetch_l2(reinterpret_cast<const char*>(a.sin) + (size_t)s * rb + (size_t)(lt - nq - 3 * nr) * 128);
-      } else if (lt == nq + 4 * nr) {
-        prefetch_l2(a.pos + s);
-      }
+    }
+  }
+  // L2 prefetch of the counters and of this step's inputs (the query rows of this head group, or
+  // all of them for the CTA that pushes the query pool; the new key, value, cos/sin, position):
+  // written by the preceding kernel in a model, so only warmed here and read after the wait. A
+  // prefetch only warms L2, so it is safe for lines that kernel still writes.
+  if (tid >= 64) {
+    const int lt = tid - 64;
+    const int rb = D * ESZ;  // bytes of one head row
+    const bool all_q = rank == ncta - 1;
+    const int nq = ((all_q ? L.Hq : G) * rb + 127) / 128, nr = (rb + 127) / 128;
+    const char* qrow = reinterpret_cast<const char*>(a.q_pre) + (size_t)s * a.qss * ESZ + (all_q ? 0 : (size_t)h * G * rb);
+    if (lt < nq) {
+      prefetch_l2(qrow + (size_t)lt * 128);
+    } else if (lt < nq + nr) {
+      prefetch_l2(reinterpret_cast<const char*>(a.k_pre) + ((size_t)s * a.kvss + (size_t)h * D) * ESZ +
+                  (size_t)(lt - nq) * 128);
+    } else if (lt < nq + 2 * nr) {
+      prefetch_l2(reinterpret_cast<const char*>(a.v) + ((size_t)s * a.kvss + (size_t)h * D) * ESZ +
+                  (size_t)(lt - nq - nr) * 128);
+    } else if (a.cos && lt < nq + 3 * nr) {
+      prefetch_l2(reinterpret_cast<const char*>(a.cos) + (size_t)s * rb + (size_t)(lt - nq - 2 * nr) * 128);
+    } else if (a.sin && lt < nq + 4 * nr) {
+      prefetch_l2(reinterpret_cast<const char*>(a.sin) + (size_t)s * rb + (size_t)(lt - nq - 3 * nr) * 128);
+    } else if (lt == nq + 4 * nr) {
+      prefetch_l2(a.pos + s);
+    } else if (lt == nq + 4 * nr + 1) {
+      prefetch_l2(d.st);
     }
   }
   pdl_wait();
 
-  // ---- one round trip: counters, logical order, free stack, held flags, new token inputs ----
+  if (warp == 0) {
+    if (!early_held) issue_rows(true);
+    if (!early_hot) issue_rows(false);
+  }
+  if (!early_hot) load_order();
+  if (!early_held && hv_ok) {
+    hval = d.held_valid[tid];
+    hpos = d.held_pos[tid];
+  }
+  // ---- one round trip: counters and the new token's inputs ----
   hc_seq_state* st = d.st;
   const int n_hot = st->n_hot, n_free = st->n_free, held_len = st->held_len;
   const int qwin_head = st->qwin_head, cold_head = st->cold_head, cold_count = st->cold_count;
   const int64_t cur_pos = a.pos[s];
-  const int cap = d.cap;
   const T* __restrict__ qp = reinterpret_cast<const T*>(a.q_pre) + (size_t)s * a.qss;
   const T* __restrict__ kp = reinterpret_cast<const T*>(a.k_pre) + (size_t)s * a.kvss + (size_t)h * D;
   const T* __restrict__ vp = reinterpret_cast<const T*>(a.v) + (size_t)s * a.kvss + (size_t)h * D;
@@ -423,20 +502,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 #pragma unroll
     for (int j = 0; j < kQP; ++j)
       if (tid + j * kStepThreads < L.Hq * D) tq[j] = qp[tid + j * kStepThreads];
-  // all loads first, then the stores: one round trip for up to kPre entries per thread
-  constexpr int kPre = 4;
-  int ov[kPre], fv[kPre];
-#pragma unroll
-  for (int j = 0; j < kPre; ++j) {
-    const int i = tid + j * kStepThreads;
-    if (i < cap) {
-      ov[j] = d.hot_ord[i];
-      fv[j] = d.hot_free[i];
-    }
-  }
-  const bool hv_ok = a.use_held && tid < d.r_max;
-  const uint8_t hval = hv_ok ? d.held_valid[tid] : 0;
-  const int64_t hpos = hv_ok ? d.held_pos[tid] : 0;
 #pragma unroll
   for (int j = 0; j < RP; ++j) {
     if (tid + j * kStepThreads < (G + 1) * H) {
@@ -450,42 +515,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       }
     }
   }
-  // ---- this part's K rows (TMA tensor boxes into the swizzled MMA layout for 16-bit types,
-  //      else bulk copies); lanes of warp 0 issue them while the loads above are in flight ----
-  if (warp == 0) {
-    const uint32_t vbytes = (uint32_t)((nhr + ns) * ROWB);
-    const int nhb = nh >> 3, nsb = (ns + 63) >> 6;  // 8-row held boxes, 64-row slot boxes
-    if (lane == 0) {
-      mbar_init(&bars[0], 1);
-      mbar_init(&bars[1], 1);
-      mbar_init(&bars[2], 1);
-      fence_mbar_init();
-      if constexpr (MMA) mbar_arrive_expect_tx(&bars[0], (uint32_t)((nh + 64 * nsb) * 128 * PL));
-      else mbar_arrive_expect_tx(&bars[0], vbytes);
-      mbar_arrive_expect_tx(&bars[1], vbytes);
-    }
-    __syncwarp();
-    if constexpr (MMA) {
-      const char* kmaps = reinterpret_cast<const char*>(L.kmaps);
-      const int y_held = (s * L.Hk + h) * d.r_max + hb;
-      const int y_hot = (s * L.Hk) * L.max_cap + h * d.cap + sb;
-      const int nb = nhb + nsb;
-      for (int b = lane; b < nb * PL; b += 32) {
-        const int pl = b / nb, j = b - pl * nb;
-        unsigned char* plane = reinterpret_cast<unsigned char*>(sK) + (size_t)pl * gm.krows * 128;
-        if (j < nhb) tma_load_2d(plane + (size_t)j * 8 * 128, kmaps + 128, pl * 64, y_held + 8 * j, &bars[0]);
-        else tma_load_2d(plane + (size_t)(nh + 64 * (j - nhb)) * 128, kmaps, pl * 64, y_hot + 64 * (j - nhb), &bars[0]);
-      }
-    } else {
-      if (lane == 1 && nhr > 0)
-        bulk_g2s(sK, reinterpret_cast<const T*>(d.held_k) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
-                 &bars[0]);
-      if (lane == 2 && ns > 0)
-        bulk_g2s(sK + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + sb) * D,
-                 (uint32_t)(ns * ROWB), &bars[0]);
-    }
-  }
-
 #pragma unroll
   for (int j = 0; j < kPre; ++j) {
     const int i = tid + j * kStepThreads;
@@ -508,12 +537,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   if (a.use_held)
     for (int t = tid + kStepThreads; t < d.r_max; t += kStepThreads)
       sHeld[t] = d.held_valid[t] != 0 && d.held_pos[t] <= cur_pos;
-  if (tid == 0) {
-    sMisc[2] = 0;
-    sMisc[3] = 0;
-    sMisc[4] = 0;
-  }
-  for (int i = tid; i < kStepMaxCluster * gm.wpc; i += kStepThreads) sBest[i] = ~0ull;
+  if (tid == 0) sMisc[4] = 0;
   for (int i = tid; i < chunk; i += kStepThreads) sInv[i] = -1;
   __syncthreads();
 
@@ -522,10 +546,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 
   const int S = n_hot + 1;  // hot tokens after the append (logical index n_hot is the new one)
   // every CTA reads the same counters (nothing writes them before the last barrier): a
-  // uniform exit, after this CTA's bulk copies have landed
+  // uniform exit, after this CTA's copies have landed
   if (n_hot < 0 || S > cap || S > gm.s_cap || new_slot < 0 || new_slot >= cap) {
     if (rank == 0 && tid == 0) set_status(st, HC_DEV_CAPACITY);
-    mbar_wait(&bars[0], 0);  // the V rows are not requested yet
+    const bool k_ok = mbar_wait(&bars[0], 0);
+    const bool v_ok = mbar_wait(&bars[1], 0);
+    if (!(k_ok && v_ok) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
     cluster_wait();
     return;
   }
@@ -533,7 +559,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const int n_ev_plan = pl.active ? pl.prefix - pl.ntop : 0;
   const bool policy = pl.active && n_ev_plan > 0;
   const int nwords = (S + 31) >> 5;
-  // CTA r owns the 32-token words w with w * ncta / nwords == r
+  // CTA r owns the 32-token words w with w * ncta / nwords == r: it writes their entries of the
+  // order table and free stack and copies their evicted tokens into the cold ring
   const int w0 = (rank * nwords + ncta - 1) / ncta, w1 = ((rank + 1) * nwords + ncta - 1) / ncta;
   const int own0 = w0 * 32, own_n = max(0, min(w1 * 32, S) - own0), nw_own = w1 - w0;
   const int qwin_slot = d.p_max > 0 ? ((qwin_head % d.p_max) + d.p_max) % d.p_max : 0;
@@ -559,7 +586,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const int i_new = row_of_slot(new_slot);
   if (tid == 0 && i_new >= 0) sInv[i_new] = n_hot;
 
-  // ---- RoPE of the new token (patch.py:161-162) while the bulk copies are in flight --------
+  // ---- RoPE of the new token (patch.py:161-162) while the copies are in flight --------------
 #pragma unroll
   for (int j = 0; j < RP; ++j) {
     const int k = tid + j * kStepThreads;
@@ -606,16 +633,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   }
   // K rows landed: the new key replaces the stale copy of its slot
   if (!__syncthreads_and(mbar_wait(&bars[0], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
-  // V rows only now: K alone shares the cluster's L2 bandwidth (one GPC) until it has landed;
-  // V arrives during scoring and policy, long before P.V needs it
-  if (warp == 0) {
-    if (lane == 3 && nhr > 0)
-      bulk_g2s(sV, reinterpret_cast<const T*>(d.held_v) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
-               &bars[1]);
-    if (lane == 4 && ns > 0)
-      bulk_g2s(sV + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_v) + ((size_t)h * d.cap + sb) * D,
-               (uint32_t)(ns * ROWB), &bars[1]);
-  }
   if (i_new >= 0)
     for (int i = tid; i < D; i += kStepThreads) {
       if constexpr (MMA) {
@@ -640,6 +657,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 
   // ---- scoring: G attention logits + the eviction logit (GQA-mean query . k) per row --------
   cluster_wait();  // every CTA of the cluster has started
+  const int ecap = gm.s_cap;
   auto emit = [&](int i, const float* tot) {
     const int u = u0 + i;
     bool valid;
@@ -654,9 +672,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 #pragma unroll
     for (int g = 0; g < G; ++g) sA[g * chunk + i] = valid ? tot[g] * L.scale : kNegInf;
     if (policy && li >= 0) {
-      sE[li] = tot[G];
-      for (int pp = 0; pp < P; ++pp)
-        if (pp != p) cluster.map_shared_rank(sE, h * P + pp)[li] = tot[G];
+      // every CTA of the cluster receives every head's eviction logits (barrier A)
+      const float e = tot[G];
+      for (int r2 = 0; r2 < ncta; ++r2) {
+        float* dst = r2 == rank ? sEv : cluster.map_shared_rank(sEv, r2);
+        dst[h * ecap + li] = e;
+      }
     }
   };
   if constexpr (MMA) {
@@ -747,109 +768,104 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       if (sub == 0 && i < nrows) emit(i, tot);
     }
   }
-  if (policy) cluster.sync();  // every CTA of head h holds the full eviction row
+  if (policy) cluster.sync();  // barrier A: every CTA holds the eviction logits of every head
   else __syncthreads();
 
-  // ---- policy: per-head values pooled by the CTAs of each head, summed by token owners ------
+  // ---- policy, computed by every CTA from the same logits: the same selection everywhere -----
   int n_ev = 0;
   int ev_slot = -1, ev_dst = -1, ev_li = -1;  // the single evicted token, when exactly one leaves
   if (policy) {
-    const int wpc32 = gm.wpc * 32;
-    float* x = sE;  // eviction logit of logical index li of head h
-    const int pb = p * pl.prefix / P, pe = (p + 1) * pl.prefix / P;  // this CTA's share of the prefix
-    auto send = [&](int li, float v) {
-      const int w = li >> 5;
-      const int r2 = w * ncta / nwords;
-      const int o0 = ((r2 * nwords + ncta - 1) / ncta) * 32;
-      cluster.map_shared_rank(sPool, r2)[h * wpc32 + (li - o0)] = v;
-    };
+    const int wph = kStepWarps / L.Hk;  // warps per head (Hk divides the 16-CTA cluster, so >= 1)
+    const int hw = warp / wph, sub = warp - hw * wph;
+    float* sHm = sRed + 2 * kStepWarps;  // per head: max, then sum
     if (L.policy == HC_POLICY_SNAPKV) {
-      // softmax over every hot token of head h (the single observation row sees every key)
+      // softmax of every head over the S hot tokens (the single observation row sees every key)
       float m = kNegInf;
-      for (int li = tid; li < S; li += kStepThreads) m = fmaxf(m, x[li] * L.scale);
+      if (hw < L.Hk)
+        for (int li = sub * 32 + lane; li < S; li += wph * 32) m = fmaxf(m, sEv[hw * ecap + li] * L.scale);
       m = warp_max(m);
       if (lane == 0) sRed[warp] = m;
       __syncthreads();
-      m = sRed[0];
-#pragma unroll
-      for (int w = 1; w < kStepWarps; ++w) m = fmaxf(m, sRed[w]);
+      if (tid < L.Hk) {
+        float mh = kNegInf;
+        for (int k = 0; k < wph; ++k) mh = fmaxf(mh, sRed[tid * wph + k]);
+        sHm[tid] = mh;
+      }
+      __syncthreads();
       float l = 0.f;
-      for (int li = tid; li < S; li += kStepThreads) {
-        const float e = __expf(x[li] * L.scale - m);
-        x[li] = e;
-        l += e;
+      if (hw < L.Hk) {
+        const float mh = sHm[hw];
+        for (int li = sub * 32 + lane; li < S; li += wph * 32) {
+          const float e = __expf(sEv[hw * ecap + li] * L.scale - mh);
+          sEv[hw * ecap + li] = e;
+          l += e;
+        }
       }
       l = warp_sum(l);
       if (lane == 0) sRed[kStepWarps + warp] = l;
       __syncthreads();
-      l = 0.f;
-#pragma unroll
-      for (int w = 0; w < kStepWarps; ++w) l += sRed[kStepWarps + w];
+      if (tid < L.Hk) {
+        float lh = 0.f;
+        for (int k = 0; k < wph; ++k) lh += sRed[kStepWarps + tid * wph + k];
+        sHm[L.Hk + tid] = lh;
+      }
+      __syncthreads();
+      // pooled probabilities of the prefix tokens, their mean over heads (scoring.py:76-78)
       const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
       const bool pmax = L.pooling == HC_POOL_MAX;
-      for (int li = pb + tid; li < pe; li += kStepThreads) {
-        float v;
-        if (pad == 0) {
-          v = x[li] / l;
-        } else if (pmax) {
-          // max of e/l over the window equals (max e)/l: the division is monotone
-          v = kNegInf;
-          if (pad <= 7) {
-#pragma unroll
-            for (int o = -7; o <= 7; ++o) {
-              const int u = li + o;
-              if (o >= -pad && o <= pad && u >= 0 && u < S) v = fmaxf(v, x[u]);
-            }
+      for (int li = tid; li < pl.prefix; li += kStepThreads) {
+        float tot = 0.f;
+        for (int hh = 0; hh < L.Hk; ++hh) {
+          const float* x = sEv + hh * ecap;
+          const float lh = sHm[L.Hk + hh];
+          float v;
+          if (pad == 0) {
+            v = x[li] / lh;
+          } else if (pmax) {
+            // max of e/l over the window equals (max e)/l: the division is monotone
+            v = kNegInf;
+            const int ua = max(0, li - pad), ub = min(S - 1, li + pad);
+            for (int u = ua; u <= ub; ++u) v = fmaxf(v, x[u]);
+            v = v / lh;
           } else {
-            for (int u = max(0, li - pad); u <= min(S - 1, li + pad); ++u) v = fmaxf(v, x[u]);
+            v = 0.f;
+            for (int u = max(0, li - pad); u <= min(S - 1, li + pad); ++u) v += x[u] / lh;
+            v /= (float)L.pool_kernel;
           }
-          v = v / l;
-        } else {
-          v = 0.f;
-          for (int u = max(0, li - pad); u <= min(S - 1, li + pad); ++u) v += x[u] / l;
-          v /= (float)L.pool_kernel;
+          tot += v;
         }
-        send(li, v);
+        sKey[li] = fkey(tot / (float)L.Hk);
       }
     } else {
-      for (int li = pb + tid; li < pe; li += kStepThreads) send(li, x[li]);
+      // hot/cold: raw logits summed over the observation rows, averaged over heads (cache.py:68-69)
+      const float inv = 1.f / sqrtf((float)L.D);
+      for (int li = tid; li < pl.prefix; li += kStepThreads) {
+        float tot = 0.f;
+        for (int hh = 0; hh < L.Hk; ++hh) tot += sEv[hh * ecap + li] * inv;
+        sKey[li] = fkey(tot / (float)L.Hk);
+      }
     }
-    cluster.sync();
-
-    // token owners: mean over heads (cache.py:60-64 hot/cold sum; SnapKV head mean)
-    const float inv = 1.f / sqrtf((float)L.D);
-    const bool snap = L.policy == HC_POLICY_SNAPKV;
-    unsigned long long best = ~0ull;
-    for (int i = tid; i < own_n; i += kStepThreads) {
-      const int li = own0 + i;
-      if (li >= pl.prefix) break;
-      float tot = 0.f;
-      for (int hh = 0; hh < L.Hk; ++hh) tot += snap ? sPool[hh * wpc32 + i] : sPool[hh * wpc32 + i] * inv;
-      const uint32_t key = fkey(tot / (float)L.Hk);
-      sKey[li] = key;
-      const unsigned long long c = ((unsigned long long)key << 32) | (0xffffffffu - (uint32_t)li);
-      best = c < best ? c : best;
-    }
+    __syncthreads();
     n_ev = n_ev_plan;
     if (n_ev == 1) {
-      // one token leaves: the lowest key, equal keys evict the higher index. Each warp holding
-      // own tokens sends its candidate to every CTA; unused entries keep their initial maximum.
+      // one token leaves: the lowest key, equal keys evict the higher index
+      unsigned long long best = ~0ull;
+      for (int li = tid; li < pl.prefix; li += kStepThreads) {
+        const unsigned long long c = ((unsigned long long)sKey[li] << 32) | (0xffffffffu - (uint32_t)li);
+        best = c < best ? c : best;
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
         best = y < best ? y : best;
       }
-      if (warp * 32 < own_n && warp < gm.wpc && lane < ncta)
-        cluster.map_shared_rank(sBest, lane)[rank * gm.wpc + warp] = best;
-      cluster.sync();
-      // every warp reduces the candidates itself (a shuffle tree, no further barrier)
-      best = ~0ull;
-      for (int r2 = lane; r2 < ncta * gm.wpc; r2 += 32) best = sBest[r2] < best ? sBest[r2] : best;
+      unsigned long long* sBest = reinterpret_cast<unsigned long long*>(sRed);
+      __syncthreads();  // sRed's statistics are no longer read
+      if (lane == 0) sBest[warp] = best;
+      __syncthreads();
+      best = sBest[0];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
-        best = y < best ? y : best;
-      }
+      for (int w = 1; w < kStepWarps; ++w) best = sBest[w] < best ? sBest[w] : best;
       const int li_ev = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
       ev_slot = phys_of(li_ev);
       ev_li = li_ev;
@@ -878,59 +894,34 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       if (i_ev >= 0 && tid < G) sA[tid * chunk + i_ev] = kNegInf;
       __syncthreads();
     } else {
-      // keys of own tokens to every CTA, then the rank of each own token among the prefix
-      __syncthreads();
-      for (int k = tid; k < ncta * own_n; k += kStepThreads) {
-        const int r2 = k / own_n, i = k - r2 * own_n, li = own0 + i;
-        if (li < pl.prefix && r2 != rank) cluster.map_shared_rank(sKey, r2)[li] = sKey[li];
-      }
-      cluster.sync();
-      int tpt = kStepThreads / (gm.wpc * 32);
-      tpt = tpt >= 32 ? 32 : tpt >= 16 ? 16 : tpt >= 8 ? 8 : tpt >= 4 ? 4 : tpt >= 2 ? 2 : 1;
-      const int tsh = __ffs(tpt) - 1;
-      for (int base = 0; base < own_n * tpt; base += kStepThreads) {
-        const int k = base + tid, tl = k >> tsh, sub = k & (tpt - 1), t = own0 + tl;
-        int cnt = 0;
-        if (tl < own_n && t < pl.prefix) {
+      // rank every prefix token against all prefix keys: kept when fewer than n_top keys are
+      // above it (equal keys: the lower index ranks above); one word of 32 tokens per warp pass
+      for (int wi = warp; wi < nwords; wi += kStepWarps) {
+        const int t = wi * 32 + lane;
+        bool keep = t < S;
+        if (t < pl.prefix) {
           const uint32_t kt = sKey[t];
+          int cnt = 0;
 #pragma unroll 4
-          for (int u = sub; u < pl.prefix; u += tpt) {
+          for (int u = 0; u < pl.prefix; ++u) {
             const uint32_t ku = sKey[u];
             cnt += (ku > kt) || (ku == kt && u < t);
           }
+          keep = cnt < pl.ntop;
         }
-        for (int o = 1; o < tpt; o <<= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-        if (sub == 0 && tl < own_n) sFlag[tl] = (t >= pl.prefix) || (cnt < pl.ntop);
+        const unsigned evw = __ballot_sync(0xffffffffu, t < S && !keep);
+        if (lane == 0) sMask[wi] = evw;
       }
       __syncthreads();
-      for (int wi = warp; wi < nw_own; wi += kStepWarps) {
-        const int t = own0 + wi * 32 + lane;
-        const bool in = t < S;
-        const bool keep = in && sFlag[wi * 32 + lane];
-        const unsigned evw = __ballot_sync(0xffffffffu, in && !keep);
-        const unsigned kpw = __ballot_sync(0xffffffffu, keep);
-        if (lane == 0) {
-          sWord[wi] = evw;
-          atomicAdd(&sMisc[2], __popc(kpw));
-          atomicAdd(&sMisc[3], __popc(evw));
-        }
-      }
-      __syncthreads();
-      const int nb = nw_own + 2;
-      for (int k = tid; k < ncta * nb; k += kStepThreads) {
-        const int r2 = k / nb, j = k - r2 * nb;
-        if (j < nw_own) cluster.map_shared_rank(sMask, r2)[w0 + j] = sWord[j];
-        else cluster.map_shared_rank(sCnt, r2)[2 * rank + (j - nw_own)] = sMisc[2 + j - nw_own];
-      }
-      cluster.sync();
-
+      // kept and evicted tokens before this CTA's words, and all evicted
       int kb = 0, eb = 0, tot_ev = 0;
-      for (int r2 = 0; r2 < ncta; ++r2) {
-        const int kc = sCnt[2 * r2], ec = sCnt[2 * r2 + 1];
-        tot_ev += ec;
-        if (r2 < rank) {
-          kb += kc;
-          eb += ec;
+      for (int w = 0; w < nwords; ++w) {
+        const uint32_t inw = (w < nwords - 1 || (S & 31) == 0) ? 0xffffffffu : ((1u << (S & 31)) - 1u);
+        const uint32_t evw = sMask[w];
+        tot_ev += __popc(evw);
+        if (w < w0) {
+          kb += __popc(inw & ~evw);
+          eb += __popc(evw);
         }
       }
       n_ev = tot_ev;
@@ -1227,7 +1218,7 @@ static cudaError_t step_g(const StepArgs& a, cudaStream_t stream, bool check_onl
 
 cudaError_t launch_step(const hc_layer& L, const void* q, int64_t qss, const void* k, const void* v, int64_t kvss,
                         const void* c, const void* sn, const int64_t* pos, int use_held, void* out, int overflow_nan,
-                        cudaStream_t stream, bool check_only) {
+                        int early, cudaStream_t stream, bool check_only) {
   if (!step_smem_bytes(L, use_held)) return cudaErrorNotSupported;
   StepArgs a{};
   a.L = L;
@@ -1242,6 +1233,7 @@ cudaError_t launch_step(const hc_layer& L, const void* q, int64_t qss, const voi
   a.out = out;
   a.use_held = use_held;
   a.overflow_nan = overflow_nan;
+  a.early = early & (HC_STEP_EARLY_HOT | HC_STEP_EARLY_HELD);
   a.g = layer_geom(L, use_held);
   if (L.dtype == HC_F32 && L.D == 128) return step_g<HC_F32, 128>(a, stream, check_only);
   if (L.dtype == HC_F16 && L.D == 128) return step_g<HC_F16, 128>(a, stream, check_only);

@@ -106,3 +106,50 @@ def attention_case_inputs(seed: int, B: int = 2, Hq: int = 8, Hk: int = 2, S: in
     v = rng.standard_normal((B, Hk, S, D), dtype=np.float32)
     m = rng.random((B, S)) < keep_frac
     return q, k, v, m
+
+
+# the Llama-3.1-8B architecture with random weights (no checkpoint here)
+LLAMA31_8B_MODEL = dict(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                        num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=500000.0,
+                        max_position_embeddings=131072, rms_norm_eps=1e-5, initializer_range=0.02)
+
+
+def llama8b_random(device, seed: int, layers: int = 32, dtype=None):
+    """A random-init Llama-3.1-8B (vocab 128256, hidden 4096, 32/8 heads, head_dim 128, RMSNorm,
+    SwiGLU FFN 14336, RoPE theta 500000; linear and embedding weights N(0, 0.02)) built directly
+    on `device` in `dtype` (fp16 by default), in eval mode."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(seed)
+    cfg = LlamaConfig(**dict(LLAMA31_8B_MODEL, num_hidden_layers=layers))
+    with torch.device(device):
+        model = LlamaForCausalLM._from_config(cfg, dtype=dtype or torch.float16)
+    return model.eval().requires_grad_(False)
+
+
+def plant_key(model, pos: int):
+    """BASELINE config 2's planted key: in the prompt forward, every layer's pre-RoPE key at
+    position `pos`, for each KV head, becomes 4 x the mean over that head's GQA group of the
+    layer's final-token pre-RoPE query heads (forward hooks on q_proj and k_proj; one-token
+    forwards are left alone). Returns the hook handles (call .remove() on each)."""
+    handles = []
+    for layer in model.model.layers:
+        att = layer.self_attn
+        Hq, Hk = att.config.num_attention_heads, att.config.num_key_value_heads
+        D = att.head_dim
+        stash = {}
+
+        def qhook(mod, inp, out, stash=stash):
+            stash["q"] = out
+
+        def khook(mod, inp, out, stash=stash, Hq=Hq, Hk=Hk, D=D):
+            if out.shape[1] <= pos:
+                return out
+            q = stash["q"][:, -1].float().view(out.shape[0], Hk, Hq // Hk, D).mean(2)  # (B, Hk, D)
+            out = out.clone()
+            out[:, pos] = (4.0 * q).reshape(out.shape[0], Hk * D).to(out.dtype)
+            return out
+
+        handles.append(att.q_proj.register_forward_hook(qhook))
+        handles.append(att.k_proj.register_forward_hook(khook))
+    return handles

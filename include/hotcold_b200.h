@@ -306,10 +306,22 @@ HC_API int hc_step_check(const hc_layer* L, int use_held);
  * (CTA = KV head x token part). Same arguments and results as the three calls
  * in sequence; out (n_seq,Hq,D). Returns HC_ERR_UNSUPPORTED (nothing launched)
  * when the layer does not fit one cluster; callers then use the three calls.
+ *
+ * The kernel is launched with programmatic stream serialisation: it may start
+ * while the launch before it on the stream still runs, and waits for that
+ * launch before it reads the step's inputs. `early` lets it read part of this
+ * layer's state before that wait, overlapping those copies with the preceding
+ * launch. The caller sets a bit only when that launch writes none of the state
+ * the bit names: HC_STEP_EARLY_HOT the hot slab rows, logical order and free
+ * stack (true after another layer's step or this layer's hc_retrieve_decode);
+ * HC_STEP_EARLY_HELD the held segment (not after this layer's retrieval). 0 is
+ * always correct.
  */
+#define HC_STEP_EARLY_HOT 1
+#define HC_STEP_EARLY_HELD 2
 HC_API int hc_step(const hc_layer* L, const void* q_pre, int64_t q_stride_seq, const void* k_pre, const void* v,
                    int64_t kv_stride_seq, const void* cos, const void* sin, const int64_t* pos, int use_held,
-                   void* out, int overflow_nan, void* stream);
+                   void* out, int overflow_nan, int early, void* stream);
 
 /*
  * Multi-GPU cold search over a token-range shard: merge of per-shard top-k

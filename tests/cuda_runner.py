@@ -63,7 +63,7 @@ def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused
             ctrl.prefill_chunk(0, q_pre[:, :, c0:c1], q_post[:, :, c0:c1], k_pre[:, :, c0:c1], k_post[:, :, c0:c1],
                                v[:, :, c0:c1], pos[:, c0:c1], last=c1 == chunks[-1])
             hot0.append(ctrl.arenas[0].hot_positions().cpu().numpy())
-    outs, hot, held = [], [], {}
+    outs, hot, held, launched = [], [], {}, set()
     dq, dk, dv = t(inputs["dq"]), t(inputs["dk"]), t(inputs["dv"])
     for i in range(n_steps):
         p = T + i
@@ -74,7 +74,10 @@ def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused
         else:
             c1 = s1 = None
         ready_before = ctrl.dbg["prefetch_ready"]
+        launched_before = ctrl.dbg["retrieval_launched"]
         o = ctrl.decode_layer(0, dq[i], dk[i], dv[i], c1, s1, pd)
+        if ctrl.dbg["retrieval_launched"] != launched_before:
+            launched.add(i + 1)
         outs.append(o.double().cpu().numpy())
         a = ctrl.arenas[0]
         hot.append(a.hot_positions().cpu().numpy())
@@ -83,7 +86,7 @@ def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused
             held[i + 1] = (a.held_pos[:, :R].cpu().numpy(), a.held_valid[:, :R].cpu().numpy().astype(bool),
                            a.held_k[:, :, :R].double().cpu().numpy())
     torch.cuda.synchronize(dev)
-    return dict(outs=np.stack(outs, 0), hot=hot, held=held, hot0=hot0, ctrl=ctrl)
+    return dict(outs=np.stack(outs, 0), hot=hot, held=held, hot0=hot0, launched=launched, ctrl=ctrl)
 
 
 def run_cuda_layers(case, layer_inputs, n_steps, device="cuda:0", fused=True):
@@ -106,7 +109,7 @@ def run_cuda_layers(case, layer_inputs, n_steps, device="cuda:0", fused=True):
     ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
     pos = torch.arange(T, device=dev).unsqueeze(0).expand(B, T)
     cos, sin = rot(torch.empty(1, dtype=dt, device=dev), pos)
-    res = [dict(outs=[], hot=[], held={}, hot0=[], ctrl=ctrl) for _ in range(L)]
+    res = [dict(outs=[], hot=[], held={}, hot0=[], launched=set(), ctrl=ctrl) for _ in range(L)]
     for li, inp in enumerate(layer_inputs):
         q_pre, k_pre, v = t(inp["q_pre"]), t(inp["k_pre"]), t(inp["v"])
         if li == 0:
@@ -125,8 +128,11 @@ def run_cuda_layers(case, layer_inputs, n_steps, device="cuda:0", fused=True):
         c1, s1 = c1.reshape(B, D).contiguous(), s1.reshape(B, D).contiguous()
         ready = [ctrl.dbg["prefetch_ready"]]
         for li in range(L):
+            n0 = ctrl.dbg["retrieval_launched"]
             ctrl.decode_layer(li, dq[i, li], dk[i, li], dv[i, li], c1, s1, pd, out=out[li])
             ready.append(ctrl.dbg["prefetch_ready"])
+            if ctrl.dbg["retrieval_launched"] != n0:
+                res[li]["launched"].add(i + 1)
         o = out.double().cpu().numpy()
         for li in range(L):
             a = ctrl.arenas[li]
@@ -182,12 +188,15 @@ def run_cuda_ragged(case, seq_inputs, budgets, ccaps, n_steps, device="cuda:0", 
     dq = torch.cat([t(inp["dq"]) for inp in seq_inputs], 1)  # (steps, n, Hq, D)
     dk = torch.cat([t(inp["dk"]) for inp in seq_inputs], 1)
     dv = torch.cat([t(inp["dv"]) for inp in seq_inputs], 1)
-    outs, hot, held = [], [], {}
+    outs, hot, held, launched = [], [], {}, set()
     for i in range(n_steps):
         pd = torch.tensor([T + i for T in Ts], device=dev, dtype=torch.long)
         c1, s1 = rot(torch.empty(1, dtype=dt, device=dev), pd[:, None])
         ready = ctrl.dbg["prefetch_ready"]
+        n0 = ctrl.dbg["retrieval_launched"]
         o = ctrl.decode_layer(0, dq[i], dk[i], dv[i], c1.reshape(n, D), s1.reshape(n, D), pd)
+        if ctrl.dbg["retrieval_launched"] != n0:
+            launched.add(i + 1)
         outs.append(o.double().cpu().numpy())
         a = ctrl.arenas[0]
         hot.append([a.hot_pos[b].index_select(0, a.logical_order(b)).cpu().numpy() for b in range(n)])
@@ -196,11 +205,11 @@ def run_cuda_ragged(case, seq_inputs, budgets, ccaps, n_steps, device="cuda:0", 
             held[i + 1] = (a.held_pos[:, :R].cpu().numpy(), a.held_valid[:, :R].cpu().numpy().astype(bool),
                            a.held_k[:, :, :R].double().cpu().numpy())
     torch.cuda.synchronize(dev)
-    return dict(outs=outs, hot=hot, held=held, hot0=hot0, ctrl=ctrl)
+    return dict(outs=outs, hot=hot, held=held, hot0=hot0, launched=launched, ctrl=ctrl)
 
 
 def ragged_seq(res, b):
     """Sequence b of a run_cuda_ragged result in run_cuda_layer's layout (batch of one)."""
     return dict(outs=np.stack([o[b:b + 1] for o in res["outs"]], 0), hot=[h[b][None] for h in res["hot"]],
-                hot0=[res["hot0"][b][None]],
+                hot0=[res["hot0"][b][None]], launched=res["launched"],
                 held={s: (p[b:b + 1], v[b:b + 1], k[b:b + 1]) for s, (p, v, k) in res["held"].items()})

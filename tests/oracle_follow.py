@@ -62,6 +62,10 @@ class FollowCuda:
         return ctop
 
     def hits(self, step, b, sc, ids, ring_pos):
+        if step == 0 and 1 in self.res.get("launched", ()):
+            # the prompt-end retrieval is replaced by the search of decode step 1 before it is
+            # attended: nothing of it is observable in either run
+            return ids
         st = max(step, 1)
         assert st in self.res["held"], f"the CUDA run injected nothing at step {st}"
         pos, valid, _ = self.res["held"][st]

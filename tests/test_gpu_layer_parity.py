@@ -102,7 +102,7 @@ def test_bench_configuration_all_steps():
     res = run_cuda_layers(c, ins, c["steps"], fused=True)
     ctrl = res[0]["ctrl"]
     # one step_kernel per layer-step, one retr_kernel per search, nothing else
-    n_search = c["steps"] // c["window_size"]
+    n_search = (c["steps"] + 1) // c["window_size"]  # the prompt counts as a forward: steps 15, 31, 47, 63
     for li in range(2):
         assert ctrl.arenas[li].launches == c["steps"] + n_search, "the fused kernels did not run"
     for li in range(2):
@@ -112,6 +112,52 @@ def test_bench_configuration_all_steps():
         assert len(layer.compress_log) == 1 + c["steps"]
         for k, v in layer.dbg.items():
             assert ctrl.dbg[k] == 2 * v, (k, ctrl.dbg[k], v)
+    assert ctrl.device_status() == 0
+
+
+def test_back_to_back_steps_of_one_layer():
+    """One layer's decode steps launched back to back, nothing read in between: each fused step
+    may start while the previous one (same layer) still runs, so it must not read that layer's
+    state before its dependency wait. Outputs, hot set, cold ring and held segment equal, bit for
+    bit, those of the same run synchronised after every step (which the tests above check
+    against the oracle)."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import TORCH_DT, cold_positions, rotary, run_cuda_layer
+    c = dict(bench_case(steps=40, T=2048), window_size=8)
+    inp = synth.layer_inputs(c["seed"], 1, 32, 8, 128, c["T"], c["steps"], "float16")
+    ref = run_cuda_layer(c, inp, c["steps"])
+    from cuda_runner import controller_kwargs
+    from hotcold_kv_cache_b200.controller import KVController
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    dev = torch.device("cuda", 0)
+    dt = TORCH_DT["float16"]
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x).astype(np.float32)).to(device=dev, dtype=dt)
+    rot = rotary(32, 128, c["theta"], dev)
+    ctrl = KVController(**controller_kwargs(c))
+    ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
+    q_pre, k_pre, v = t(inp["q_pre"]), t(inp["k_pre"]), t(inp["v"])
+    ctrl._lazy_init(k_pre, n_layers=1)
+    pos = torch.arange(c["T"], device=dev)[None]
+    cos, sin = rot(torch.empty(1, dtype=dt, device=dev), pos)
+    q_post, k_post = apply_rotary_pos_emb(q_pre, k_pre, cos, sin)
+    ctrl.prefill_layer(0, q_pre, q_post, k_pre, k_post, v, pos)
+    dq, dk, dv = t(inp["dq"]), t(inp["dk"]), t(inp["dv"])
+    pd = torch.arange(c["T"], c["T"] + c["steps"], device=dev)
+    cs, sn = rot(torch.empty(1, dtype=dt, device=dev), pd[None])
+    cs, sn = cs[0].contiguous(), sn[0].contiguous()
+    out = torch.empty((c["steps"], 1, 32, 128), dtype=dt, device=dev)
+    torch.cuda.synchronize(dev)
+    for i in range(c["steps"]):
+        ctrl.decode_layer(0, dq[i], dk[i], dv[i], cs[i:i + 1], sn[i:i + 1], pd[i:i + 1], out=out[i])
+    got = out.double().cpu().numpy()
+    assert np.array_equal(got, ref["outs"])
+    a, b = ctrl.arenas[0], ref["ctrl"].arenas[0]
+    assert np.array_equal(a.hot_positions().cpu().numpy(), ref["hot"][-1])
+    assert np.array_equal(cold_positions(ctrl)[0], cold_positions(ref["ctrl"])[0])
+    for name in ("held_k", "held_v", "held_pos", "held_valid"):
+        assert torch.equal(getattr(a, name), getattr(b, name)), name
+    assert ctrl.dbg == ref["ctrl"].dbg
+    assert a.launches == b.launches == c["steps"] + (c["steps"] + 1) // c["window_size"]
     assert ctrl.device_status() == 0
 
 

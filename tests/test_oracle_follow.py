@@ -22,7 +22,8 @@ def _as_cuda(layer, outs, hot, B, T):
     c0 = [e for e in layer.compress_log if e["step"] == 0]
     hot0 = np.stack([c0[b]["keep_pos"] for b in range(B)], 0) if c0 else np.tile(np.arange(T), (B, 1))
     held = {e["step"]: (e["pos"], e["valid"], e["kmem"]) for e in layer.events}
-    return dict(outs=outs, hot=hot, hot0=[hot0], held=held)
+    launched = {e["launched"] for e in layer.events if e["launched"] > 0}
+    return dict(outs=outs, hot=hot, hot0=[hot0], held=held, launched=launched)
 
 
 def test_following_its_own_run_adopts_nothing():
