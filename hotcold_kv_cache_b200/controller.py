@@ -180,6 +180,7 @@ class KVController:
         self._held_active = [False] * L
         self._retrieval_ready_cpu = [None] * L
         self._tails = [dict() for _ in range(L)]
+        self._seen = [0] * L  # tokens each layer has processed (prompt + decode steps)
         self.workspace = Workspace(device)
         self._inited = True
 
@@ -226,6 +227,11 @@ class KVController:
                            else 4096)
             self.arenas[li] = a
         return a
+
+    def seen_tokens(self, layer_idx: int) -> int:
+        """Tokens layer `layer_idx` has processed so far (the next token's absolute position when
+        positions start at 0); the hot tier's physical length is shorter once compressed."""
+        return self._seen[int(layer_idx)] if self._inited else 0
 
     # ------------------------------------------------------------------ cold store
     def cold_size(self, layer_idx: int) -> int:
@@ -450,7 +456,12 @@ class KVController:
         q_obs = q_post if T <= r else q_post[:, :, -r:, :]
         ev = a.compress_prompt(q_obs, k_post, v, k_pre, positions.to(k_post.device, torch.int64))
         self._count_eviction(ev)
+        self._seen[li] = T
         self.dbg["triton_prefill_fallback"] += 1
+        if self.query_pool_size < self.window_size:
+            # the query tail a later chunk of this prompt extends (prefill_chunk)
+            self._tails[li]["chunk"] = q_pre[:, :, -self.query_pool_size:, :] if self.query_pool_size > 0 \
+                else q_pre[:, :, :0, :]
         if self.retrieve_after_prefill:
             self.launch_retrieval_now(li, q_pre[:, :, -self.query_pool_size:, :])
 
@@ -481,15 +492,16 @@ class KVController:
             ev = a.compress_prompt(q_obs, torch.cat([hk, k_post], 2), torch.cat([hv, v], 2),
                                    torch.cat([hp, k_pre], 2), torch.cat([hpos, pos], 1))
         self._count_eviction(ev)
+        self._seen[li] += T
         self.dbg["triton_prefill_fallback"] += 1
         P = self.query_pool_size
         tail = self._tails[li].get("chunk")
         tail = q_pre if tail is None else torch.cat([tail, q_pre], 2)
         self._tails[li]["chunk"] = tail[:, :, -P:, :] if P > 0 else tail[:, :, :0, :]
-        if last:
-            q_tail = self._tails[li].pop("chunk")
-            if self.retrieve_after_prefill:
-                self.launch_retrieval_now(li, q_tail)
+        if last and self.retrieve_after_prefill:
+            # the prompt's last query_pool_size queries so far (the tail is kept: a later chunk
+            # of the same prompt extends it and searches again; its result replaces this one)
+            self.launch_retrieval_now(li, self._tails[li]["chunk"])
 
     def prefill_sequence(self, layer_idx: int, b: int, q_pre, q_post, k_pre, k_post, v, positions):
         """The prompt forward of sequence b of a ragged batch (set_ragged) in one layer:
@@ -527,6 +539,7 @@ class KVController:
         (a contiguous tensor of that shape and the model dtype), else the layer's own buffer."""
         li = int(layer_idx)
         a = self.arena(li, q_pre.shape[1], k_pre.dtype, k_pre.device)
+        self._seen[li] += 1
         hook = self.op_hook or (lambda name, phase: None)
         if self.fused_step:
             res = self._decode_fused(li, a, hook, q_pre, k_pre, v, cos, sin, pos, out)
@@ -654,7 +667,7 @@ class KVController:
             "qpool": [list(q) for q in self._qpool],
             "prompt_qsum": [None if t is None else t.cpu() for t in self._prompt_qsum],
             "staged": list(self._staged), "held_active": list(self._held_active),
-            "dbg": dict(self.dbg), "last_injected_len": self.last_injected_len,
+            "dbg": dict(self.dbg), "last_injected_len": self.last_injected_len, "seen": list(self._seen),
         }
 
     def load_state_dict(self, sd: dict, device) -> None:
@@ -680,6 +693,7 @@ class KVController:
         self._held_active = list(sd["held_active"])
         self.dbg = dict(sd["dbg"])
         self.last_injected_len = sd["last_injected_len"]
+        self._seen = list(sd.get("seen", [0] * self.n_layers))
 
     def device_status(self) -> int:
         """OR of the device status words of every layer (synchronises): HC_DEV_* bits."""

@@ -3,9 +3,11 @@
 Prompt forwards keep the reference's structure: projections, HF RoPE, stock
 causal SDPA over the whole prompt, then the prompt goes into the hot tier
 (compressed, evicted tokens into the cold ring) and the prompt-end retrieval
-runs. A one-token decode forward runs the sm_100a hot path of the layer:
-RoPE + append, the scheduled retrieval, compression, attention over
-[held | hot] — without host synchronisation.
+runs. A further multi-token forward on a non-empty cache (a prompt sent in
+chunks, which the reference rejects) attends to the kept hot tokens and joins
+them (KVController.prefill_chunk). A one-token decode forward runs the sm_100a
+hot path of the layer: RoPE + append, the scheduled retrieval, compression,
+attention over [held | hot] — without host synchronisation.
 """
 
 from __future__ import annotations
@@ -107,25 +109,44 @@ def install_monkeypatch(enable_debug: bool = True):
                 layer.layer_idx = li
         hot_prev_len = int(past_key_values.get_seq_length(li)) if past_key_values is not None else 0
 
+        # absolute positions of this forward's tokens: cache_position, else the tokens this layer has
+        # already seen (the hot tier's physical length is shorter once it has been compressed)
         if cache_position is not None and int(cache_position.numel()) == q_len:
             pos_new = cache_position.reshape(1, -1).expand(bsz, -1).to(device=device, dtype=torch.long)
         else:
-            pos_new = torch.arange(hot_prev_len, hot_prev_len + q_len, device=device,
-                                   dtype=torch.long).unsqueeze(0).expand(bsz, -1)
+            start = kvctrl.seen_tokens(li) if layer is not None else hot_prev_len
+            pos_new = torch.arange(start, start + q_len, device=device, dtype=torch.long).unsqueeze(0).expand(bsz, -1)
         n_rep = num_heads // num_kv_heads
 
         if q_len == 1 and layer is not None:
-            # decode: the sm_100a hot path of this layer
-            attn = kvctrl.decode_layer(li, q_pre[:, :, 0], k_pre[:, :, 0], v[:, :, 0], cos.reshape(bsz, head_dim),
-                                       sin.reshape(bsz, head_dim), pos_new[:, 0].contiguous())
+            # decode: the sm_100a hot path of this layer. RoPE is applied at pos_new from the rotary
+            # module's inv_freq inside the kernel, not from position_embeddings: transformers 5.x
+            # derives a decode step's position ids from get_seq_length(), which is the compressed
+            # (physical) hot length here, as in the reference, so its cos/sin belong to the wrong
+            # position once the prompt has been compressed.
+            attn = kvctrl.decode_layer(li, q_pre[:, :, 0], k_pre[:, :, 0], v[:, :, 0], None, None,
+                                       pos_new[:, 0].contiguous())
             attn_out = attn.reshape(bsz, 1, num_heads * head_dim)
+        elif q_len > 1 and layer is not None and kvctrl.seen_tokens(li) > 0:
+            # a further chunk of a prompt (the reference raises here, patch.py:325-329): RoPE at the
+            # chunk's absolute positions; its queries attend to the kept hot tokens and causally to
+            # each other; then its tokens join the hot tier, which is compressed into the cold store
+            cos_c, sin_c = _rope_cos_sin_for_positions(pos_new, q_pre.dtype, device, head_dim)
+            q_post, k_post = modeling_llama.apply_rotary_pos_emb(q_pre, k_pre, cos_c, sin_c)
+            a = kvctrl.arenas[li]
+            hk, hv, _, _ = a.hot_dense()
+            k_all, v_all = torch.cat([hk, k_post], 2), torch.cat([hv, v], 2)
+            n_prev = int(hk.shape[2])
+            mask = torch.ones((q_len, n_prev + q_len), dtype=torch.bool, device=device)
+            mask[:, n_prev:] = torch.ones((q_len, q_len), dtype=torch.bool, device=device).tril()
+            k_rep = modeling_llama.repeat_kv(k_all, n_rep) if n_rep > 1 else k_all
+            v_rep = modeling_llama.repeat_kv(v_all, n_rep) if n_rep > 1 else v_all
+            attn = F.scaled_dot_product_attention(q_post, k_rep, v_rep, attn_mask=mask[None, None], dropout_p=0.0)
+            kvctrl.prefill_chunk(li, q_pre, q_post, k_pre, k_post, v, pos_new, last=True)
+            attn_out = attn.transpose(1, 2).reshape(bsz, q_len, -1)
         else:
             q_post, k_post = modeling_llama.apply_rotary_pos_emb(q_pre, k_pre, cos, sin)
             if q_len > 1:
-                if hot_prev_len > 0:
-                    raise NotImplementedError(
-                        "multi-token forward on a non-empty hot cache (chunked prefill) "
-                        "is not supported by the hot/cold patch")
                 k_rep = modeling_llama.repeat_kv(k_post, n_rep) if n_rep > 1 else k_post
                 v_rep = modeling_llama.repeat_kv(v, n_rep) if n_rep > 1 else v
                 attn = F.scaled_dot_product_attention(q_post, k_rep, v_rep, attn_mask=attention_mask, dropout_p=0.0,

@@ -515,8 +515,11 @@ def run_tiny_model():
         out = model(input_ids=ids[:, :T], use_cache=True, past_key_values=cache)
         logits.append(out.logits[0, -1].float().numpy())
         for i in range(r["steps"]):
+            # explicit position ids: transformers 5.x would derive them from the cache's
+            # get_seq_length(), the compressed hot length, where 4.57 (the reference's pin) took
+            # them from cache_position
             out = model(input_ids=ids[:, T + i:T + i + 1], cache_position=torch.tensor([T + i]),
-                        past_key_values=cache, use_cache=True)
+                        position_ids=torch.tensor([[T + i]]), past_key_values=cache, use_cache=True)
             logits.append(out.logits[0, -1].float().numpy())
     hotcold_kv.uninstall_monkeypatch()
     hotcold_kv.set_active_kvctrl(None)

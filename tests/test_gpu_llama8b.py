@@ -141,8 +141,11 @@ def _run(model, c, seed, plant=None, record=0):
     return res, inp, ctrl, prompt_state, float(np.median(times))
 
 
-def _check_layer(c, res, inp):
-    layer, o_outs, o_hot, fc = run_following(O, inp, c["steps"], res, **oracle_kwargs(c))
+def _check_layer(c, res, inp, model):
+    # the oracle rotates with the model's own inverse frequencies (computed on the GPU, they can
+    # differ from a CPU computation in the last place)
+    kw = dict(oracle_kwargs(c), inv_freq=model.model.rotary_emb.inv_freq.float().cpu().numpy())
+    layer, o_outs, o_hot, fc = run_following(O, inp, c["steps"], res, **kw)
     assert assert_same_run(res, layer, o_outs, o_hot, c["dtype"], c["steps"], "layer 0") == c["steps"]
     return layer, fc
 
@@ -150,7 +153,7 @@ def _check_layer(c, res, inp):
 def test_config1_llama8b_8k_budget512(model):
     c = _case(1)
     res, inp, ctrl, _, us = _run(model, c, seed=11)
-    layer, _ = _check_layer(c, res, inp)
+    layer, _ = _check_layer(c, res, inp, model)
     assert [e["step"] for e in layer.events] == [15, 31, 47, 63]
     L = model.config.num_hidden_layers
     assert ctrl.dbg["retrieval_launched"] == 4 * L and ctrl.dbg["injection_used"] == (STEPS - 14) * L
@@ -175,7 +178,7 @@ def test_config2_llama8b_planted_key_is_retrieved(model):
         else:
             evicted += 1
             assert p in set(pos[valid].tolist()), f"layer {li} evicted the planted token and did not retrieve it"
-    _check_layer(c, res, inp)
+    _check_layer(c, res, inp, model)
     assert ctrl.device_status() == 0
     print(f"config 2: planted token {p}: kept hot in {kept} layers, evicted and retrieved at step 1 in {evicted}; "
           f"{us:.0f} us per decode token")

@@ -146,3 +146,75 @@ def test_tiny_model_golden():
         assert kv.dbg[k] == v, (k, kv.dbg[k], v)
     assert [kv.cold_size(i) for i in range(cfg["num_hidden_layers"])] == list(g["cold_sizes"])
     assert kv.device_status() == 0
+
+
+def test_chunked_prompt_through_patched_forward():
+    """A prompt sent in three forwards (the reference raises NotImplementedError on the second,
+    patch.py:325-329): each chunk's tokens join the hot tier and the tier is compressed with the
+    chunk's last recent_size queries as the observation window; decode then continues. Layer 0
+    (its q/k/v recorded by hooks) against the oracle's chunked prefill at every step: hot sets
+    after each chunk and each decode step, attention outputs, retrieved sets."""
+    import hotcold_kv_cache_b200 as hc
+    from golden_cases import oracle_kwargs
+    from oracle import hotcold_oracle as O
+    from oracle_follow import assert_same_run, run_following
+    model = _model(SMALL, 3, torch.float32)
+    Hq, Hk, D = SMALL["num_attention_heads"], SMALL["num_key_value_heads"], SMALL["head_dim"]
+    bounds, steps = [0, 120, 250, 300], 12
+    c = dict(B=1, Hq=Hq, Hk=Hk, D=D, T=bounds[-1], steps=steps, dtype="float32", policy="snapkv", cap=64, recent=16,
+             topk_ratio=0.0, pool_kernel=7, ccap=1000, faiss_dim=128, window_size=4, pool=2, R=8, hold=True,
+             rap=True, theta=SMALL["rope_theta"])
+    kv = hc.KVController(max_capacity_prompt=c["cap"], topk_ratio=0.0, recent_size=c["recent"],
+                         cpu_buffer_size=c["ccap"], faiss_dim=128, window_size=c["window_size"], query_pool_size=c["pool"],
+                         lookahead_k=c["R"], hold_retrieved=True, retrieve_after_prefill=True, policy="snapkv",
+                         profile_overlap=False)
+    ids = torch.randint(0, SMALL["vocab_size"], (1, bounds[-1] + steps), generator=torch.Generator().manual_seed(8))
+    ids = ids.cuda()
+    att = model.model.layers[0].self_attn
+    rec = {"q": [], "k": [], "v": [], "o": []}
+    hooks = [att.q_proj.register_forward_hook(lambda m, i, o: rec["q"].append(o.detach().cpu())),
+             att.k_proj.register_forward_hook(lambda m, i, o: rec["k"].append(o.detach().cpu())),
+             att.v_proj.register_forward_hook(lambda m, i, o: rec["v"].append(o.detach().cpu())),
+             att.o_proj.register_forward_pre_hook(lambda m, a: rec["o"].append(a[0].detach().cpu()))]
+    hc.uninstall_monkeypatch()
+    hc.set_active_rotary_emb(model.model.rotary_emb)
+    hc.install_monkeypatch(enable_debug=False)
+    hc.set_active_kvctrl(kv)
+    res = dict(outs=[], hot=[], held={}, hot0=[], launched=set())
+    try:
+        cache = hc.build_hotcold_cache(model, kv)
+        with torch.inference_mode():
+            for c0, c1 in zip(bounds[:-1], bounds[1:]):
+                model(input_ids=ids[:, c0:c1], cache_position=torch.arange(c0, c1, device="cuda"),
+                      past_key_values=cache, use_cache=True, logits_to_keep=1)
+                res["hot0"].append(kv.arenas[0].hot_positions().cpu().numpy())
+            a = kv.arenas[0]
+            for i in range(steps):
+                T = bounds[-1]
+                ready, launched = kv.dbg["prefetch_ready"], kv.dbg["retrieval_launched"]
+                model(input_ids=ids[:, T + i:T + i + 1], cache_position=torch.tensor([T + i], device="cuda"),
+                      past_key_values=cache, use_cache=True, logits_to_keep=1)
+                res["outs"].append(rec["o"][-1].double().view(1, Hq, D).numpy())
+                res["hot"].append(a.hot_positions().cpu().numpy())
+                if kv.dbg["prefetch_ready"] != ready:
+                    R = a.r_max
+                    res["held"][i + 1] = (a.held_pos[:, :R].cpu().numpy(), a.held_valid[:, :R].cpu().numpy().astype(bool),
+                                          a.held_k[:, :, :R].double().cpu().numpy())
+                if kv.dbg["retrieval_launched"] != launched:
+                    res["launched"].add(i + 1)
+    finally:
+        for h in hooks:
+            h.remove()
+        hc.uninstall_monkeypatch()
+        hc.set_active_kvctrl(None)
+    res["outs"] = np.stack(res["outs"], 0)
+    f = lambda ts, H: np.concatenate([t.float().view(1, t.shape[1], H, D).transpose(1, 2).numpy() for t in ts], 2)
+    n_chunks = len(bounds) - 1
+    inp = dict(q_pre=f(rec["q"][:n_chunks], Hq), k_pre=f(rec["k"][:n_chunks], Hk), v=f(rec["v"][:n_chunks], Hk),
+               dq=np.stack([f([t], Hq)[:, :, 0] for t in rec["q"][n_chunks:]], 0),
+               dk=np.stack([f([t], Hk)[:, :, 0] for t in rec["k"][n_chunks:]], 0),
+               dv=np.stack([f([t], Hk)[:, :, 0] for t in rec["v"][n_chunks:]], 0))
+    kw = dict(oracle_kwargs(c), inv_freq=model.model.rotary_emb.inv_freq.float().cpu().numpy())
+    layer, o_outs, o_hot, _ = run_following(O, inp, steps, res, chunks=bounds, **kw)
+    assert assert_same_run(res, layer, o_outs, o_hot, "float32", steps, "layer 0") == steps
+    assert kv.dbg["evicted_tokens"] > 0 and kv.device_status() == 0
