@@ -70,7 +70,8 @@ SIGNATURES = {
     "hc_retrieve_scratch_bytes": (c_size_t, [_P]),
     "hc_retrieve": (c_int, [_P, _P, _I64, _I64, _I64, c_int, c_int, _P, c_int, _P, c_size_t, _P]),
     "hc_retrieve_ex": (c_int, [_P, _P, _I64, _I64, _I64, c_int, c_int, _P, c_int, _P, _P, c_size_t, c_int, _P]),
-    "hc_prompt_query_sum": (c_int, [_P, _P, _I64, _I64, _I64, c_int, _P, _P]),
+    "hc_prompt_query_sum_scratch_bytes": (c_size_t, [_P]),
+    "hc_prompt_query_sum": (c_int, [_P, _P, _I64, _I64, _I64, c_int, _P, _P, c_size_t, _P]),
     "hc_attend_scratch_bytes": (c_size_t, [_P]),
     "hc_attend": (c_int, [_P, _P, _P, c_int, _P, c_int, _P, c_size_t, _P]),
     "hc_shard_merge": (c_int, [_P, _P, c_int, c_int, _P, _P, _P]),

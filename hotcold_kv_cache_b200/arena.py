@@ -569,10 +569,12 @@ class LayerArena:
         return True
 
     def prompt_query_sum(self, q_dense):
+        """Sum over the prompt's positions of its head-mean pre-RoPE queries (n_seq, D) fp32."""
         out = torch.empty((self.n_seq, self.D), dtype=torch.float32, device=self.device)
         qs = q_dense.stride()
+        ws = self.ws.get(size("hc_prompt_query_sum_scratch_bytes", byref(self.L)))
         call("hc_prompt_query_sum", byref(self.L), ptr(q_dense), qs[0], qs[1], qs[2], q_dense.shape[2], ptr(out),
-             self._stream())
+             ptr(ws), ws.numel(), self._stream())
         self._launched("prompt_query_sum")
         return out
 

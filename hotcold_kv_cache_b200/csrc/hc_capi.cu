@@ -234,11 +234,17 @@ int hc_cold_append(const hc_layer* L, const void* k_pre, const void* v, int64_t 
                     "cold_append");
 }
 
+size_t hc_prompt_query_sum_scratch_bytes(const hc_layer* L) {
+  return L ? hc::prompt_query_sum_scratch_bytes(*L) : 0;
+}
+
 int hc_prompt_query_sum(const hc_layer* L, const void* q_dense, int64_t qd_seq, int64_t qd_head, int64_t qd_tok, int P,
-                        float* out_sum, void* stream) {
+                        float* out_sum, void* scratch, size_t scratch_bytes, void* stream) {
   if (int rc = check_layer(L)) return rc;
   if (!q_dense || !out_sum || P <= 0) return fail(HC_ERR_ARG, "bad prompt query arguments");
-  return check_cuda(hc::launch_prompt_query_sum(*L, q_dense, qd_seq, qd_head, qd_tok, P, out_sum,
+  const size_t need = hc::prompt_query_sum_scratch_bytes(*L);
+  if (!scratch || scratch_bytes < need) return fail(HC_ERR_SCRATCH, "scratch %zu < %zu bytes", scratch_bytes, need);
+  return check_cuda(hc::launch_prompt_query_sum(*L, q_dense, qd_seq, qd_head, qd_tok, P, out_sum, scratch,
                                                 reinterpret_cast<cudaStream_t>(stream)),
                     "prompt_query_sum");
 }

@@ -42,7 +42,8 @@ cudaError_t launch_append(const hc_layer& L, const void* q, int64_t qss, const v
 cudaError_t launch_store_prompt(const hc_layer& L, int S, const void* a, const void* b, const void* c, int64_t s0,
                                 int64_t s1, int64_t s2, const int64_t* pos, cudaStream_t st);
 cudaError_t launch_prompt_query_sum(const hc_layer& L, const void* q, int64_t a, int64_t b, int64_t c, int P,
-                                    float* out, cudaStream_t st);
+                                    float* out, void* scratch, cudaStream_t st);
+size_t prompt_query_sum_scratch_bytes(const hc_layer& L);
 cudaError_t launch_compress(const hc_layer& L, const void* q_obs, int64_t qs0, int64_t qs1, int64_t qs2, int tq,
                             int S_dense, const void* sk, const void* sv, const void* skp, int64_t ss0, int64_t ss1,
                             int64_t ss2, const int64_t* spos, void* scratch, int n_evict_hint, cudaStream_t stream);

@@ -771,101 +771,111 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   if (policy) cluster.sync();  // barrier A: every CTA holds the eviction logits of every head
   else __syncthreads();
 
-  // ---- policy, computed by every CTA from the same logits: the same selection everywhere -----
+  // ---- policy: every CTA holds every head's logits; it takes the softmax statistics of all heads
+  //      and scores its own tokens; one exchange of candidates (or keys) gives every CTA the same
+  //      selection -----
   int n_ev = 0;
   int ev_slot = -1, ev_dst = -1, ev_li = -1;  // the single evicted token, when exactly one leaves
   if (policy) {
+    const int own_p = max(0, min(own_n, pl.prefix - own0));  // this CTA's own prefix tokens
     const int wph = kStepWarps / L.Hk;  // warps per head (Hk divides the 16-CTA cluster, so >= 1)
     const int hw = warp / wph, sub = warp - hw * wph;
-    float* sHm = sRed + 2 * kStepWarps;  // per head: max, then sum
-    if (L.policy == HC_POLICY_SNAPKV) {
-      // softmax of every head over the S hot tokens (the single observation row sees every key)
-      float m = kNegInf;
-      if (hw < L.Hk)
-        for (int li = sub * 32 + lane; li < S; li += wph * 32) m = fmaxf(m, sEv[hw * ecap + li] * L.scale);
-      m = warp_max(m);
-      if (lane == 0) sRed[warp] = m;
-      __syncthreads();
-      if (tid < L.Hk) {
-        float mh = kNegInf;
-        for (int k = 0; k < wph; ++k) mh = fmaxf(mh, sRed[tid * wph + k]);
-        sHm[tid] = mh;
-      }
-      __syncthreads();
-      float l = 0.f;
-      if (hw < L.Hk) {
-        const float mh = sHm[hw];
-        for (int li = sub * 32 + lane; li < S; li += wph * 32) {
-          const float e = __expf(sEv[hw * ecap + li] * L.scale - mh);
-          sEv[hw * ecap + li] = e;
-          l += e;
+    const bool snap = L.policy == HC_POLICY_SNAPKV;
+    if (snap) {
+      // each head's softmax statistics over the S hot tokens in one pass (the single observation
+      // row sees every key): per lane a running max and a sum rescaled to it, combined over the
+      // lanes here and over the head's wph warps where a token is scored
+      float m = kNegInf, l = 0.f;
+      for (int li = sub * 32 + lane; li < S; li += wph * 32) {
+        const float x = sEv[hw * ecap + li] * L.scale;
+        if (x > m) {
+          l = (m == kNegInf ? 0.f : l * __expf(m - x)) + 1.f;
+          m = x;
+        } else {
+          l += __expf(x - m);
         }
       }
-      l = warp_sum(l);
-      if (lane == 0) sRed[kStepWarps + warp] = l;
-      __syncthreads();
-      if (tid < L.Hk) {
-        float lh = 0.f;
-        for (int k = 0; k < wph; ++k) lh += sRed[kStepWarps + tid * wph + k];
-        sHm[L.Hk + tid] = lh;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+        const float mx = fmaxf(m, m2);
+        l = (m == kNegInf ? 0.f : l * __expf(m - mx)) + (m2 == kNegInf ? 0.f : l2 * __expf(m2 - mx));
+        m = mx;
+      }
+      if (lane == 0) {
+        sRed[warp] = m;
+        sRed[kStepWarps + warp] = l;
       }
       __syncthreads();
-      // pooled probabilities of the prefix tokens, their mean over heads (scoring.py:76-78)
-      const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
-      const bool pmax = L.pooling == HC_POOL_MAX;
-      for (int li = tid; li < pl.prefix; li += kStepThreads) {
-        float tot = 0.f;
-        for (int hh = 0; hh < L.Hk; ++hh) {
-          const float* x = sEv + hh * ecap;
-          const float lh = sHm[L.Hk + hh];
-          float v;
-          if (pad == 0) {
-            v = x[li] / lh;
-          } else if (pmax) {
-            // max of e/l over the window equals (max e)/l: the division is monotone
-            v = kNegInf;
-            const int ua = max(0, li - pad), ub = min(S - 1, li + pad);
-            for (int u = ua; u <= ub; ++u) v = fmaxf(v, x[u]);
-            v = v / lh;
+    }
+    // keys of this CTA's own prefix tokens: a thread per (token, head), the Hk heads of a token
+    // in consecutive lanes and summed by shuffles (Hk divides 16). SnapKV (scoring.py:72-78):
+    // the max-pooled probability is exp(max logit - M) / L, exp and the division being monotone;
+    // hot/cold (cache.py:68-69): the raw logit / sqrt(D). Then the mean over heads.
+    const int npair = own_p * L.Hk;
+    const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
+    const bool pmax = L.pooling == HC_POOL_MAX;
+    const float inv = 1.f / sqrtf((float)L.D);
+    unsigned long long best = ~0ull;  // lowest (key, higher index) of own tokens
+    for (int base = 0; base < npair; base += kStepThreads) {
+      const int k = base + tid;
+      const bool live = k < npair;
+      const int i = k / L.Hk, hh = k - i * L.Hk;
+      const int li = own0 + i;
+      float v = 0.f;
+      if (live) {
+        const float* x = sEv + hh * ecap;
+        if (snap) {
+          float mh = kNegInf;
+          for (int w = 0; w < wph; ++w) mh = fmaxf(mh, sRed[hh * wph + w]);
+          float lh = 0.f;
+          for (int w = 0; w < wph; ++w) {
+            const float mw = sRed[hh * wph + w];
+            if (mw != kNegInf) lh += sRed[kStepWarps + hh * wph + w] * __expf(mw - mh);
+          }
+          const int ua = max(0, li - pad), ub = min(S - 1, li + pad);
+          if (pad == 0 || pmax) {
+            float mx = kNegInf;
+            for (int u = ua; u <= ub; ++u) mx = fmaxf(mx, x[u]);
+            v = __expf(mx * L.scale - mh) / lh;
           } else {
-            v = 0.f;
-            for (int u = max(0, li - pad); u <= min(S - 1, li + pad); ++u) v += x[u] / lh;
+            for (int u = ua; u <= ub; ++u) v += __expf(x[u] * L.scale - mh) / lh;
             v /= (float)L.pool_kernel;
           }
-          tot += v;
+        } else {
+          v = x[li] * inv;
         }
-        sKey[li] = fkey(tot / (float)L.Hk);
       }
-    } else {
-      // hot/cold: raw logits summed over the observation rows, averaged over heads (cache.py:68-69)
-      const float inv = 1.f / sqrtf((float)L.D);
-      for (int li = tid; li < pl.prefix; li += kStepThreads) {
-        float tot = 0.f;
-        for (int hh = 0; hh < L.Hk; ++hh) tot += sEv[hh * ecap + li] * inv;
-        sKey[li] = fkey(tot / (float)L.Hk);
-      }
-    }
-    __syncthreads();
-    n_ev = n_ev_plan;
-    if (n_ev == 1) {
-      // one token leaves: the lowest key, equal keys evict the higher index
-      unsigned long long best = ~0ull;
-      for (int li = tid; li < pl.prefix; li += kStepThreads) {
-        const unsigned long long c = ((unsigned long long)sKey[li] << 32) | (0xffffffffu - (uint32_t)li);
+      for (int o = L.Hk >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (live && hh == 0) {
+        const uint32_t key = fkey(v / (float)L.Hk);
+        sKey[li] = key;
+        const unsigned long long c = ((unsigned long long)key << 32) | (0xffffffffu - (uint32_t)li);
         best = c < best ? c : best;
       }
+    }
+    n_ev = n_ev_plan;
+    if (n_ev == 1) {
+      // one token leaves: the lowest key, equal keys evict the higher index. Each CTA reduces its
+      // own tokens and hands its candidate to every CTA (barrier C), which all take the lowest.
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
         best = y < best ? y : best;
       }
-      unsigned long long* sBest = reinterpret_cast<unsigned long long*>(sRed);
-      __syncthreads();  // sRed's statistics are no longer read
+      unsigned long long* sBest = reinterpret_cast<unsigned long long*>(sRed + 96);  // per warp
+      unsigned long long* sCand = reinterpret_cast<unsigned long long*>(sRed + 64);  // per CTA
       if (lane == 0) sBest[warp] = best;
       __syncthreads();
-      best = sBest[0];
+      if (tid < ncta) {
+        unsigned long long b = sBest[0];
 #pragma unroll
-      for (int w = 1; w < kStepWarps; ++w) best = sBest[w] < best ? sBest[w] : best;
+        for (int w = 1; w < kStepWarps; ++w) b = sBest[w] < b ? sBest[w] : b;
+        cluster.map_shared_rank(sCand, tid)[rank] = b;
+      }
+      cluster.sync();  // barrier C: every CTA's candidate everywhere
+      best = sCand[0];
+      for (int r2 = 1; r2 < ncta; ++r2) best = sCand[r2] < best ? sCand[r2] : best;
       const int li_ev = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
       ev_slot = phys_of(li_ev);
       ev_li = li_ev;
@@ -894,6 +904,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       if (i_ev >= 0 && tid < G) sA[tid * chunk + i_ev] = kNegInf;
       __syncthreads();
     } else {
+      // every CTA needs every prefix key: own keys to all CTAs (barrier C)
+      __syncthreads();
+      for (int k = tid; k < ncta * own_p; k += kStepThreads) {
+        const int r2 = k / own_p, li = own0 + (k - r2 * own_p);
+        if (r2 != rank) cluster.map_shared_rank(sKey, r2)[li] = sKey[li];
+      }
+      cluster.sync();
       // rank every prefix token against all prefix keys: kept when fewer than n_top keys are
       // above it (equal keys: the lower index ranks above); one word of 32 tokens per warp pass
       for (int wi = warp; wi < nwords; wi += kStepWarps) {

@@ -233,59 +233,87 @@ __global__ void store_prompt_kernel(hc_layer L, int S, const void* sk, const voi
   }
 }
 
-// Sum over prompt positions of the head-mean pre-RoPE query (each mean rounded to the
-// model dtype, as torch's mean over heads returns that dtype), fp32 (n_seq, D). One cluster
-// of kPqsCluster CTAs per sequence; thread group g of CTA r sums positions
-// G, G + NG, G + 2 NG, ... (G = r * groups + g, NG = all groups), then the groups and the CTAs
-// are added in a fixed order (deterministic).
-constexpr int kPqsCluster = 8;
-constexpr int kPqsThreads = 1024;
+// Sum over prompt positions of the head-mean pre-RoPE query (each mean rounded to the model
+// dtype, as torch's mean over heads returns that dtype), fp32 (n_seq, D), in two passes over the
+// whole GPU. Pass 1: CTA b of a sequence takes the contiguous positions [b P / nb, (b+1) P / nb);
+// a lane holds 16 bytes of a row (VE elements) and sums them over the heads in head order, rounds
+// the mean and adds it over its positions; the CTA reduces its lanes in a fixed order into
+// part[s][b][D]. Pass 2 adds the nb partials of a sequence in block order. Deterministic.
+constexpr int kPqsThreads = 256;
+constexpr int kPqsBlocks = 296;  // CTAs per sequence at most (two waves of 148 SMs)
 
-template <int DT, int D>
-__global__ void __launch_bounds__(kPqsThreads) prompt_query_sum_kernel(hc_layer L, const void* q_, int64_t qs,
-                                                                       int64_t qh, int64_t qt, int P, float* out) {
+size_t prompt_query_sum_scratch_bytes(const hc_layer& L) {
+  return (size_t)L.n_seq * kPqsBlocks * L.D * sizeof(float);
+}
+
+template <int DT, int D, bool VEC>
+__global__ void __launch_bounds__(kPqsThreads) pqs_part_kernel(hc_layer L, const void* q_, int64_t qs, int64_t qh,
+                                                                int64_t qt, int P, float* part) {
   using E = Elem<DT>;
   using T = typename E::T;
-  constexpr int GROUPS = kPqsThreads / D;
-  __shared__ float part[GROUPS][D];
-  __shared__ float cta[D];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
-  const int s = blockIdx.y, g = threadIdx.x / D, dd = threadIdx.x % D;
+  constexpr int VE = 16 / sizeof(T);  // elements per 16-byte chunk
+  constexpr int CPR = D / VE;         // chunks per row
+  constexpr int PPW = 32 / CPR;       // positions per warp pass
+  constexpr int NW = kPqsThreads / 32;
+  static_assert(CPR <= 32 && 32 % CPR == 0, "a row must fit one warp");
+  __shared__ float red[NW * PPW][D];
+  const int s = blockIdx.y, b = blockIdx.x, nb = gridDim.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = lane % CPR, sub = lane / CPR;
+  const int p0 = (int)((long)b * P / nb), p1 = (int)((long)(b + 1) * P / nb);
   pdl_wait();
-  const T* q = reinterpret_cast<const T*>(q_) + (size_t)s * qs + dd;
-  const int NG = GROUPS * kPqsCluster;
-  float tot = 0.f;
-  for (int p = rank * GROUPS + g; p < P; p += NG) {
-    // heads in groups of 8: the loads of a group are in flight together, the sum keeps the
-    // head order
-    const T* qp = q + (size_t)p * qt;
-    float acc = 0.f;
+  const T* q = reinterpret_cast<const T*>(q_) + (size_t)s * qs + (size_t)c * VE;
+  float tot[VE];
+#pragma unroll
+  for (int e = 0; e < VE; ++e) tot[e] = 0.f;
+  for (int p = p0 + warp * PPW + sub; p < p1; p += NW * PPW) {
+    const T* row = q + (size_t)p * qt;
+    float acc[VE];
+#pragma unroll
+    for (int e = 0; e < VE; ++e) acc[e] = 0.f;
     int h = 0;
+    // heads in groups of 8: the loads of a group are in flight together, the sum keeps the head order
     for (; h + 8 <= L.Hq; h += 8) {
-      T x[8];
+      float x[8][VE];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) x[u] = qp[(size_t)(h + u) * qh];
+      for (int u = 0; u < 8; ++u) {
+        if constexpr (VEC) {
+          unpack16<DT>(*reinterpret_cast<const uint4*>(row + (size_t)(h + u) * qh), x[u]);
+        } else {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc += E::to_f(x[u]);
+          for (int e = 0; e < VE; ++e) x[u][e] = E::to_f(row[(size_t)(h + u) * qh + e]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int e = 0; e < VE; ++e) acc[e] += x[u][e];
     }
-    for (; h < L.Hq; ++h) acc += E::to_f(qp[(size_t)h * qh]);
-    tot += E::round(acc / (float)L.Hq);
+    for (; h < L.Hq; ++h)
+#pragma unroll
+      for (int e = 0; e < VE; ++e) acc[e] += E::to_f(row[(size_t)h * qh + e]);
+#pragma unroll
+    for (int e = 0; e < VE; ++e) tot[e] += E::round(acc[e] / (float)L.Hq);
   }
-  part[g][dd] = tot;
+#pragma unroll
+  for (int e = 0; e < VE; ++e) red[warp * PPW + sub][c * VE + e] = tot[e];
   __syncthreads();
-  if (g == 0) {
+  for (int dd = threadIdx.x; dd < D; dd += kPqsThreads) {
     float t = 0.f;
-    for (int j = 0; j < GROUPS; ++j) t += part[j][dd];
-    cta[dd] = t;
+    for (int j = 0; j < NW * PPW; ++j) t += red[j][dd];
+    part[((size_t)s * nb + b) * D + dd] = t;
   }
-  cluster.sync();
-  if (rank == 0 && g == 0) {
+}
+
+template <int D>
+__global__ void pqs_sum_kernel(const float* part, int nb, float* out) {
+  const int s = blockIdx.x;
+  pdl_wait();
+  for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
     float t = 0.f;
-    for (int r = 0; r < kPqsCluster; ++r) t += cluster.map_shared_rank(cta, r)[dd];
+    for (int b = 0; b < nb; ++b) t += part[((size_t)s * nb + b) * D + dd];
     out[(size_t)s * D + dd] = t;
   }
-  cluster.sync();  // CTA 0 has read every CTA's sum
 }
 
 template <int DT, int D>
@@ -322,24 +350,23 @@ cudaError_t launch_store_prompt(const hc_layer& L, int S, const void* a, const v
 
 template <int DT, int D>
 static cudaError_t pqs_t(const hc_layer& L, const void* q, int64_t a, int64_t b, int64_t c, int P, float* out,
-                         cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kPqsCluster, L.n_seq);
-  cfg.blockDim = dim3(kPqsThreads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kPqsCluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, prompt_query_sum_kernel<DT, D>, L, q, a, b, c, P, out);
+                         float* part, cudaStream_t st) {
+  using T = typename Elem<DT>::T;
+  const int nb = P < kPqsBlocks * 16 ? (P + 15) / 16 : kPqsBlocks;
+  const bool vec = (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (a * (int64_t)sizeof(T)) % 16 == 0 &&
+                   (b * (int64_t)sizeof(T)) % 16 == 0 && (c * (int64_t)sizeof(T)) % 16 == 0;
+  cudaError_t e = vec ? launch_pdl(pqs_part_kernel<DT, D, true>, dim3(nb, L.n_seq), dim3(kPqsThreads), 0, st, L, q, a,
+                                   b, c, P, part)
+                      : launch_pdl(pqs_part_kernel<DT, D, false>, dim3(nb, L.n_seq), dim3(kPqsThreads), 0, st, L, q,
+                                   a, b, c, P, part);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(pqs_sum_kernel<D>, dim3(L.n_seq), dim3(D), 0, st, (const float*)part, nb, out);
 }
+
 cudaError_t launch_prompt_query_sum(const hc_layer& L, const void* q, int64_t a, int64_t b, int64_t c, int P,
-                                    float* out, cudaStream_t st) {
-  HC_DISPATCH_DT_D(L.dtype, L.D, pqs_t, L, q, a, b, c, P, out, st);
+                                    float* out, void* scratch, cudaStream_t st) {
+  float* part = reinterpret_cast<float*>(scratch);
+  HC_DISPATCH_DT_D(L.dtype, L.D, pqs_t, L, q, a, b, c, P, out, part, st);
 }
 
 }  // namespace hc

@@ -254,10 +254,13 @@ HC_API int hc_retrieve_ex(const hc_layer* L, const void* q_dense, int64_t qd_seq
 
 /*
  * Head-mean prompt queries summed over positions, fp32 (n_seq,D): the prompt's
- * contribution to the query pool when it stays in the pool.
+ * contribution to the query pool when it stays in the pool (update_query_window,
+ * controller.py:240-241, with the pooled mean of controller.py:243-248). Scratch
+ * from hc_prompt_query_sum_scratch_bytes (per-CTA partial sums).
  */
+HC_API size_t hc_prompt_query_sum_scratch_bytes(const hc_layer* L);
 HC_API int hc_prompt_query_sum(const hc_layer* L, const void* q_dense, int64_t qd_seq, int64_t qd_head,
-                        int64_t qd_tok, int P, float* out_sum, void* stream);
+                        int64_t qd_tok, int P, float* out_sum, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
  * Decode attention over [held | hot] (patch.py:263-305 and the Triton kernel
