@@ -52,6 +52,7 @@ _I64 = c_int64
 # name -> (restype, argtypes); mirrors include/hotcold_b200.h
 SIGNATURES = {
     "hc_version": (c_char_p, []),
+    "hc_host_device_pointer": (c_int, [_P, POINTER(c_void_p)]),
     "hc_last_error": (c_char_p, []),
     "hc_attention_dense_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "hc_attention_dense": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int,

@@ -66,9 +66,16 @@ class LayerArena:
     def __init__(self, *, n_seq: int, Hq: int, Hk: int, D: int, F: int, dtype, device, budgets, r_max: int,
                  ccap, p_max: int, policy: str, recent: int, topk_ratio: float, pool_kernel: int = 7,
                  pooling: str = "maxpool", normalize: bool = True, inv_freq: torch.Tensor, rope_scaling: float = 1.0,
-                 workspace: Workspace | None = None, hot_cap_hint: int | None = None):
+                 workspace: Workspace | None = None, hot_cap_hint: int | None = None, cold_payload: str = "device"):
         """hot_cap_hint: initial physical hot slots when below budget + 1 (the slab grows on
-        demand up to budget + 1, so a huge budget does not preallocate)."""
+        demand up to budget + 1, so a huge budget does not preallocate). cold_payload: "device"
+        keeps the cold ring's pre-RoPE keys and values in HBM; "host" keeps them in page-locked
+        host memory that the kernels address directly (evictions write it, retrievals gather
+        their hits from it), for cold stores larger than HBM; the index vectors and positions
+        stay in HBM either way, since every search scans them."""
+        if cold_payload not in ("device", "host"):
+            raise ValueError(f"cold_payload must be 'device' or 'host', not {cold_payload!r}")
+        self.cold_payload = cold_payload
         _lib.load()
         dev = torch.device(device)
         if dev.type != "cuda":
@@ -98,8 +105,12 @@ class LayerArena:
         self.held_valid = torch.zeros((n_seq, R), dtype=torch.uint8, **z)
         self.held_src = torch.full((n_seq, R), -1, dtype=torch.int32, **z)
         self.cold_vec = torch.empty((n_seq, C, F), dtype=torch.float32, **z)
-        self.cold_kpre = torch.empty((n_seq, C, Hk, D), dtype=dtype, **z)
-        self.cold_v = torch.empty((n_seq, C, Hk, D), dtype=dtype, **z)
+        if cold_payload == "host":
+            self.cold_kpre = torch.empty((n_seq, C, Hk, D), dtype=dtype, pin_memory=True)
+            self.cold_v = torch.empty((n_seq, C, Hk, D), dtype=dtype, pin_memory=True)
+        else:
+            self.cold_kpre = torch.empty((n_seq, C, Hk, D), dtype=dtype, **z)
+            self.cold_v = torch.empty((n_seq, C, Hk, D), dtype=dtype, **z)
         self.cold_pos = torch.zeros((n_seq, C), dtype=torch.int64, **z)
         self.qwin = torch.zeros((n_seq, P, D), dtype=dtype, **z)
         self.st = torch.zeros((n_seq, 16), dtype=torch.int32, **z)
@@ -138,8 +149,8 @@ class LayerArena:
             d.held_valid = self.held_valid[s].data_ptr()
             d.held_src = self.held_src[s].data_ptr()
             d.cold_vec = self.cold_vec[s].data_ptr()
-            d.cold_kpre = self.cold_kpre[s].data_ptr()
-            d.cold_v = self.cold_v[s].data_ptr()
+            d.cold_kpre = self._device_address(self.cold_kpre[s])
+            d.cold_v = self._device_address(self.cold_v[s])
             d.cold_pos = self.cold_pos[s].data_ptr()
             d.qwin = self.qwin[s].data_ptr()
             d.st = self.st[s].data_ptr()
@@ -167,6 +178,16 @@ class LayerArena:
         self._caps_np = np.asarray(self.caps, np.int64)
         self._plan_cache = {}
         self._dirty = True
+
+    def _device_address(self, t: torch.Tensor) -> int:
+        """The address kernels use for `t`: its own for device memory, the mapped device address
+        of page-locked host memory."""
+        if t.is_cuda:
+            return t.data_ptr()
+        dev = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            call("hc_host_device_pointer", t.data_ptr(), ctypes.byref(dev))
+        return int(dev.value)
 
     def _encode_kmaps(self):
         """TMA tensor maps of the hot K slab (all sequences as rows of D, 64-row boxes) and the

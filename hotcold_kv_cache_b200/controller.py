@@ -95,12 +95,16 @@ class KVController:
         pool_kernel: int = 7,
         pooling: str = "maxpool",
         overflow_nan: bool = True,
+        cold_payload: str = "device",
     ):
         """Reference arguments (controller.py:15-34) plus:
         policy: "hotcold" (cache.py:37-128) or "snapkv" (SnapKV score, scoring.py:50-132,
             with recent_size as the observation/recent window);
         pool_kernel, pooling: SnapKV pooling (scoring.py:40-47);
-        overflow_nan: reproduce the reference kernel's NaN on fp32 exp overflow."""
+        overflow_nan: reproduce the reference kernel's NaN on fp32 exp overflow;
+        cold_payload: "device" (HBM) or "host": the cold rings' pre-RoPE keys and values in
+            page-locked host RAM that the kernels read and write directly, the reference's CPU
+            cold tier (docs/design.md:59-64) for stores larger than HBM; the index stays in HBM."""
         if policy not in ("hotcold", "snapkv"):
             raise ValueError(f"unknown policy {policy!r}")
         if pooling not in ("maxpool", "avgpool"):
@@ -121,6 +125,9 @@ class KVController:
         self.force_wait_for_prefetch_diagnostic = bool(force_wait_for_prefetch_diagnostic)
         self.policy, self.pool_kernel, self.pooling = policy, int(pool_kernel), pooling
         self.overflow_nan = bool(overflow_nan)
+        if cold_payload not in ("device", "host"):
+            raise ValueError(f"cold_payload must be 'device' or 'host', not {cold_payload!r}")
+        self.cold_payload = cold_payload
 
         self._inited = False
         self.B = self.Hk = self.D = self.n_layers = None
@@ -222,7 +229,7 @@ class KVController:
                            p_max=max(self.query_pool_size, 1), policy=self.policy,
                            recent=self.recent_size, topk_ratio=self.topk_ratio, pool_kernel=self.pool_kernel,
                            pooling=self.pooling, normalize=self.normalize_for_ip, inv_freq=inv_freq,
-                           rope_scaling=sc, workspace=self.workspace,
+                           rope_scaling=sc, workspace=self.workspace, cold_payload=self.cold_payload,
                            hot_cap_hint=None if max(self.seq_budgets or [self.max_capacity_prompt]) < (1 << 16)
                            else 4096)
             self.arenas[li] = a
@@ -408,9 +415,9 @@ class KVController:
         R = a.r_max
         src = a.held_src[:, :R].long()
         valid = a.held_valid[:, :R].bool()
-        idx = src.clamp(min=0)
-        kpre = torch.stack([a.cold_kpre[b].index_select(0, idx[b]) for b in range(a.n_seq)], 0)  # (B,R,Hk,D)
-        vv = torch.stack([a.cold_v[b].index_select(0, idx[b]) for b in range(a.n_seq)], 0)
+        idx = src.clamp(min=0).to(a.cold_kpre.device)
+        kpre = torch.stack([a.cold_kpre[b].index_select(0, idx[b]) for b in range(a.n_seq)], 0).to(a.device)
+        vv = torch.stack([a.cold_v[b].index_select(0, idx[b]) for b in range(a.n_seq)], 0).to(a.device)
         m = valid[:, :, None, None]
         kpre = torch.where(m, kpre, torch.zeros_like(kpre)).permute(0, 2, 1, 3).contiguous()
         vv = torch.where(m, vv, torch.zeros_like(vv)).permute(0, 2, 1, 3).contiguous()

@@ -59,6 +59,18 @@ void set_last_error(const char* msg) { snprintf(g_err, sizeof(g_err), "%s", msg)
 extern "C" {
 
 const char* hc_version(void) { return "hotcold_b200 1.0 (sm_100a)"; }
+
+int hc_host_device_pointer(const void* host, void** dev) {
+  if (!host || !dev) return fail(HC_ERR_ARG, "NULL pointer argument");
+  cudaPointerAttributes attr{};
+  cudaError_t e = cudaPointerGetAttributes(&attr, host);
+  if (e != cudaSuccess || attr.type != cudaMemoryTypeHost) {
+    (void)cudaGetLastError();
+    return fail(HC_ERR_ARG, "not page-locked host memory registered with CUDA");
+  }
+  e = cudaHostGetDevicePointer(dev, const_cast<void*>(host), 0);
+  return check_cuda(e, "host_device_pointer");
+}
 const char* hc_last_error(void) { return g_err; }
 
 size_t hc_attention_dense_scratch_bytes(int B, int Hq, int Hk, int S, int D) {

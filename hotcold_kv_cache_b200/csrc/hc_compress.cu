@@ -914,8 +914,13 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
     return;
   }
 
-  // exact top-n_top of the prefix
-  block_topk_flags([&](int i) { return tok[i]; }, pl.prefix, pl.ntop, sel, sh);
+  // exact top-n_top of the prefix. Up to kRangeMax tokens per thread, each thread takes a
+  // contiguous range (a few block-wide steps in all); longer prompts keep the coalesced passes
+  // over blockDim-token chunks (per-thread loops over long ranges serialise their loads)
+  constexpr int kRangeMax = 8;
+  const int per = (S + (int)blockDim.x - 1) / (int)blockDim.x;
+  if (per <= kRangeMax) block_topk_ranges([&](int i) { return tok[i]; }, pl.prefix, pl.ntop, sel, sh);
+  else block_topk_flags([&](int i) { return tok[i]; }, pl.prefix, pl.ntop, sel, sh);
 
   // order-preserving compaction. keep: selected prefix tokens and the tail; evict: the rest
   int kept = 0, evicted = 0;
@@ -923,6 +928,52 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
   const int ccap = d.ccap;
   const int cold_head = st->cold_head, cold_count = st->cold_count;
   const int n_free0 = DENSE ? 0 : st->n_free;
+  if (per <= kRangeMax) {
+    // thread t owns tokens [t * per, (t + 1) * per): counts, one block scan of (kept | evicted
+    // << 16) when both fit 16 bits (else two scans), then the thread writes its run in order
+    // (the slab's order table is read into registers first)
+    const int r0 = min(S, tid * per), r1 = min(S, r0 + per);
+    int nk = 0, ne = 0;
+    int phys[kRangeMax];
+    for (int i = r0; i < r1; ++i) {
+      const bool keep = (i >= pl.prefix) || sel[i];
+      nk += keep;
+      ne += !keep;
+      if (!DENSE) phys[i - r0] = d.hot_ord[i];
+    }
+    int kb, eb, tk, te;
+    if (S < 65536) {
+      int tot;
+      const int b = block_exclusive_scan(nk | (ne << 16), sh + 256, tot);
+      kb = b & 0xffff;
+      eb = b >> 16;
+      tk = tot & 0xffff;
+      te = tot >> 16;
+    } else {
+      kb = block_exclusive_scan(nk, sh + 256, tk);
+      eb = block_exclusive_scan(ne, sh + 256, te);
+    }
+    // the scans end with a barrier: every order-table read above is done before the writes
+    for (int i = r0; i < r1; ++i) {
+      const bool keep = (i >= pl.prefix) || sel[i];
+      const int ph = DENSE ? -1 : phys[i - r0];
+      if (keep) {
+        if (DENSE) a.keep_src[(size_t)s * a.S_max + kb] = i;
+        else d.hot_ord[kb] = ph;
+        ++kb;
+      } else {
+        const int j = eb++;
+        a.ev_src[(size_t)s * a.S_max + j] = DENSE ? i : ph;
+        // ring slot of the j-th evicted token; a batch larger than the ring keeps its last ccap
+        a.ev_dst[(size_t)s * a.S_max + j] =
+            (j >= n_evict_total - ccap) ? (int)(((long)cold_head + cold_count + j) % ccap) : -1;
+        if (!DENSE && n_free0 + j < d.cap) d.hot_free[n_free0 + j] = ph;
+      }
+    }
+    kept = tk;
+    evicted = te;
+    __syncthreads();
+  } else
   for (int base = 0; base < S; base += blockDim.x) {
     const int t = base + tid;
     int keep = 0, ev = 0, phys = -1;

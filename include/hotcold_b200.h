@@ -118,6 +118,14 @@ typedef struct hc_layer {
 
 /* Library and error reporting. */
 HC_API const char* hc_version(void);
+
+/*
+ * The device address of page-locked host memory (cudaHostGetDevicePointer): where a cold ring's
+ * payload lives in host RAM (KVController(cold_payload="host"); no counterpart in the reference,
+ * whose cold tier is host memory that the GPU never reads directly), the descriptors point
+ * the kernels at it. HC_ERR_ARG when `host` is not page-locked memory known to CUDA.
+ */
+HC_API int hc_host_device_pointer(const void* host, void** dev);
 HC_API const char* hc_last_error(void);
 
 /*

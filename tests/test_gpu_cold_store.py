@@ -104,3 +104,44 @@ def test_padding_entries_are_skipped_and_order_is_by_score():
     sc = vecs @ q[0]
     sc[3] = -np.inf
     assert got == list(np.argsort(-sc, kind="stable")[:6])
+
+
+@pytest.mark.parametrize("dtype,fused", [("float16", True), ("float16", False), ("float32", False)])
+def test_cold_payload_in_host_memory(dtype, fused):
+    """The cold ring's payload in page-locked host memory (cold_payload="host", the reference's
+    CPU cold tier for stores larger than HBM): kernels write evicted tokens there and gather
+    retrieved hits from it. Same outputs, hot sets, held segments and cold ring as the payload
+    in HBM, bit for bit, through a wrapping ring and a search every 3 steps; and the oracle."""
+    import numpy as np
+    import torch
+    from golden_cases import oracle_kwargs
+    from hotcold_kv_cache_b200 import synth
+    from oracle import hotcold_oracle as O
+    from oracle_follow import assert_same_run, run_following
+    import cuda_runner
+    c = dict(B=2, Hq=8, Hk=2, D=128, T=400, steps=24, dtype=dtype, policy="snapkv", cap=64, recent=16,
+             topk_ratio=0.0, pool_kernel=7, ccap=350, faiss_dim=128, window_size=3, pool=2, R=16, hold=True,
+             rap=True, theta=500000.0, seed=606)
+    inp = synth.layer_inputs(c["seed"], 2, 8, 2, 128, c["T"], c["steps"], dtype)
+    dev_run = cuda_runner.run_cuda_layer(c, inp, c["steps"], fused=fused)
+    kw = cuda_runner.controller_kwargs
+    try:
+        cuda_runner.controller_kwargs = lambda case: dict(kw(case), cold_payload="host")
+        host_run = cuda_runner.run_cuda_layer(c, inp, c["steps"], fused=fused)
+    finally:
+        cuda_runner.controller_kwargs = kw
+    a_h, a_d = host_run["ctrl"].arenas[0], dev_run["ctrl"].arenas[0]
+    assert not a_h.cold_kpre.is_cuda and a_h.cold_kpre.is_pinned() and a_d.cold_kpre.is_cuda
+    assert (a_h.cold_pushed > a_h.ccaps[0]).all(), "the ring did not wrap"
+    assert np.array_equal(host_run["outs"], dev_run["outs"])
+    for i in range(c["steps"]):
+        assert np.array_equal(host_run["hot"][i], dev_run["hot"][i])
+    assert sorted(host_run["held"]) == sorted(dev_run["held"])
+    for st in host_run["held"]:
+        for x, y in zip(host_run["held"][st], dev_run["held"][st]):
+            assert np.array_equal(x, y)
+    assert torch.equal(a_h.cold_kpre.cuda(), a_d.cold_kpre) and torch.equal(a_h.cold_v.cuda(), a_d.cold_v)
+    assert torch.equal(a_h.cold_pos, a_d.cold_pos) and torch.equal(a_h.cold_vec, a_d.cold_vec)
+    layer, o_outs, o_hot, _ = run_following(O, inp, c["steps"], host_run, **oracle_kwargs(c))
+    assert assert_same_run(host_run, layer, o_outs, o_hot, dtype, c["steps"]) == c["steps"]
+    assert host_run["ctrl"].device_status() == 0
