@@ -69,6 +69,46 @@ __device__ __forceinline__ void unpack16(const uint4& u, float* f) {
   }
 }
 
+// Unpack N consecutive elements (N * element size a multiple of 4 bytes, naturally aligned).
+template <int DT, int N>
+__device__ __forceinline__ void unpack_n(const void* p, float* f) {
+  if constexpr (DT == HC_F32) {
+    if constexpr (N % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < N; i += 4) {
+        const float4 x = reinterpret_cast<const float4*>(p)[i / 4];
+        f[i] = x.x; f[i + 1] = x.y; f[i + 2] = x.z; f[i + 3] = x.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; i += 2) {
+        const float2 x = reinterpret_cast<const float2*>(p)[i / 2];
+        f[i] = x.x; f[i + 1] = x.y;
+      }
+    }
+  } else {
+    static_assert(N % 2 == 0, "pairs of 16-bit elements");
+    uint32_t w[N / 2];
+    if constexpr (N % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < N / 2; i += 2) {
+        const uint2 x = reinterpret_cast<const uint2*>(p)[i / 2];
+        w[i] = x.x; w[i + 1] = x.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) w[i] = reinterpret_cast<const uint32_t*>(p)[i];
+    }
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      float2 t;
+      if constexpr (DT == HC_F16) t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      else t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      f[2 * i] = t.x; f[2 * i + 1] = t.y;
+    }
+  }
+}
+
 // RoPE on one element pair, rounded like HF's apply_rotary_pos_emb in the model dtype:
 // out = round(round(x*c) + round(rot*s)), each product and the sum a separate op.
 template <int DT>
@@ -294,6 +334,9 @@ __device__ __forceinline__ void cluster_arrive_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+// Arrival that releases this thread's prior (distributed) shared memory writes to the threads
+// that pass the matching cluster_wait.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void set_status(hc_seq_state* st, int bits) {
   if (st) atomicOr(&st->status, bits);

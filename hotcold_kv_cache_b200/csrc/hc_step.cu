@@ -8,23 +8,27 @@
 // cluster owns KV head h and part p of P = 16/Hk parts of head h's rows in PHYSICAL order,
 // [held rows 0..r_max) ++ [slab slots 0..cap): order does not matter to attention, and
 // physical order makes each part contiguous in HBM.
-//   1. Right after the dependency wait one thread starts TMA bulk copies of the part's K and
-//      V rows (at most two copies each); meanwhile the CTA reads the counters, maps its slots
-//      to logical indices (free slots stay unmapped and are masked), and RoPEs the new token's
-//      query heads of its group and, if the new slot is its own, the new key.
-//   2. Scoring on the CUDA cores (packed f32x2 FMAs, 8 lanes per row): G attention logits
-//      and the eviction logit (GQA-mean query . k) per row. Eviction logits go, by logical
-//      index, to every CTA of head h through distributed shared memory (cluster barrier 1).
-//   3. Policy: the SnapKV softmax and pooling (or the raw hot/cold logit) of head h are
-//      computed by the CTAs of that head, each for its share of the prefix, and sent to the
-//      CTA owning the token's 32-token word (barrier 2). Owners take the mean over heads. A
-//      single evicted token (the steady state) is the minimum over the owners' candidates
-//      (barrier 3); more evictions rank every owned token against all prefix keys (barriers
-//      3 and 4). Exact top-k with ties to the lower index; no CTA works alone.
-//   4. Each CTA masks evicted rows, computes its flash-decode partial (max, sum, P.V) and
-//      sends each column block to the CTA of head h that finalizes it (last barrier). Owners of
-//      words compact the logical order, push freed slots and copy evicted payloads into the
-//      cold ring with their index vectors; the last CTA pushes the query pool.
+//   1. Warp 0 starts TMA copies of the part's K rows (tensor boxes into the swizzled MMA layout)
+//      and V rows (bulk copies) — before the dependency wait when the launch before this one
+//      left the layer's state alone — while the CTA reads the counters and order table, maps
+//      its slots to logical indices (free slots stay unmapped and are masked), and RoPEs the new
+//      token's query heads of its group and, if the new slot is its own, the new key.
+//   2. Scoring with tcgen05 (16-bit types; CUDA cores for f32): G attention logits and the
+//      eviction logit (GQA-mean query . k) per row. Eviction logits go, by logical index, to
+//      every CTA of the cluster, with every warp's softmax statistics of them (barrier A).
+//   3. While barrier A completes, every warp computes its flash-decode partial (max, sum, P.V)
+//      over its 32 rows.
+//   4. Policy: every CTA combines each head's statistics, scores every prefix token (SnapKV
+//      softmax and pooling, or the raw hot/cold logit; mean over heads) and takes the lowest
+//      (ties: the higher index) — the same arithmetic on the same data, so every CTA selects
+//      the same token with no further exchange. The warp holding the evicted row subtracts it
+//      from its partial (or recomputes without it where the row carried most of the mass).
+//      More than one eviction ranks every prefix token against all keys (one more exchange)
+//      and the warps recompute their partials.
+//   5. The warps' partials are combined per column and each column block goes to the CTA of
+//      head h that finalizes it (last barrier). Owners of 32-token words compact the logical
+//      order and push freed slots; evicted payloads are copied into the cold ring with their
+//      index vectors; the last CTA pushes the query pool.
 // The result equals hc_append + hc_compress + hc_attend on the same state.
 
 #include <cooperative_groups.h>
@@ -80,7 +84,7 @@ struct StepArgs {
 };
 
 struct StepSmem {
-  size_t k, qb, v, q, knew, a, inv, ord, fre, held, ev, key, red, mask, evl, o, ml, qp, misc, tmem, bars, total;
+  size_t k, qb, v, q, knew, vn, a, inv, ord, fre, held, ev, stat, key, red, mask, evl, o, ml, qp, misc, tmem, bars, total;
 };
 
 __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -92,21 +96,23 @@ __host__ __device__ inline StepSmem step_smem(int D, int esz, int G, int Hk, int
   size_t o = 0;
   auto take = [&](size_t b) { size_t r = o; o += al16(b); return r; };
   // K rows of this CTA's part (16-bit: D/64 planes of 128-byte swizzled rows, 1024-aligned);
-  // after scoring the same area holds the P.V partial sums
+  // after scoring the same area holds the warps' P.V partials, probabilities and statistics
   const size_t kb = (size_t)g.krows * D * esz;
-  const size_t rb = (size_t)kStepWarps * G * D * 4;
+  const size_t rb = (size_t)kStepWarps * G * (D + 32 + 2) * 4;
   m.k = take(kb > rb ? kb : rb);
   o = (o + 1023) & ~size_t(1023);
   m.qb = take((size_t)16 * D * esz);  // MMA query operand: G heads, the mean, zero rows (N = 16)
   m.v = take((size_t)g.chunk * D * esz);
   m.q = take((size_t)(G + 1) * D * 4);       // RoPE'd query heads and their GQA mean
   m.knew = take((size_t)D * esz);            // the new key after RoPE
+  m.vn = take((size_t)D * esz);              // the new value
   m.a = take((size_t)G * g.chunk * 4);       // attention logits, then probabilities
   m.inv = take((size_t)g.chunk * 4);         // logical index of each row, -1 when not attended
   m.ord = take((size_t)g.s_cap * 4);         // logical order (physical slot per logical index)
   m.fre = take((size_t)g.s_cap * 4);         // free-slot stack
   m.held = take((size_t)(max_r > 0 ? max_r : 1) * 4);  // held rows attended this step
   m.ev = take((size_t)Hk * g.s_cap * 4);     // eviction logits of every head, by logical index
+  m.stat = take((size_t)kStepMaxCluster * kStepWarps * 2 * 4);  // softmax partials of every warp
   m.key = take((size_t)g.s_cap * 4);         // policy score keys of the prefix, by logical index
   m.red = take((size_t)(4 * kStepMaxCluster + 4 * kStepWarps) * 8);
   m.mask = take(step_words(g.s_cap) * 4);    // evicted tokens, one bit per logical index
@@ -293,12 +299,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   T* sV = reinterpret_cast<T*>(smem + M.v);
   float* sQ = reinterpret_cast<float*>(smem + M.q);
   T* sKnew = reinterpret_cast<T*>(smem + M.knew);
+  T* sVn = reinterpret_cast<T*>(smem + M.vn);
   float* sA = reinterpret_cast<float*>(smem + M.a);
   int* sInv = reinterpret_cast<int*>(smem + M.inv);
   int* sOrd = reinterpret_cast<int*>(smem + M.ord);
   int* sFree = reinterpret_cast<int*>(smem + M.fre);
   int* sHeld = reinterpret_cast<int*>(smem + M.held);
   float* sEv = reinterpret_cast<float*>(smem + M.ev);  // [Hk][s_cap]
+  float* sStat = reinterpret_cast<float*>(smem + M.stat);  // [cluster rank][warp] (max, sum)
   uint32_t* sKey = reinterpret_cast<uint32_t*>(smem + M.key);
   float* sRed = reinterpret_cast<float*>(smem + M.red);  // per-warp partials and per-head statistics
   uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + M.mask);
@@ -394,10 +402,49 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const bool hv_ok = a.use_held && tid < d.r_max;
   uint8_t hval = 0;
   int64_t hpos = 0;
-  if (early_hot) load_order();
-  if (early_held && hv_ok) {
-    hval = d.held_valid[tid];
-    hpos = d.held_pos[tid];
+  auto row_of_slot = [&](int slot) { return (slot >= sb && slot < sb + ns) ? nh + slot - sb : -1; };
+  // the hot tier's counters, order table and free stack into registers and shared memory, and the
+  // logical index of every own slot row (free slots stay -1 and are masked)
+  hc_seq_state* st = d.st;
+  int n_hot = 0, n_free = 0, qwin_head = 0, cold_head = 0, cold_count = 0, held_len = 0;
+  auto stage_hot = [&]() {
+    n_hot = st->n_hot;
+    n_free = st->n_free;
+    qwin_head = st->qwin_head;
+    cold_head = st->cold_head;
+    cold_count = st->cold_count;
+    load_order();
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int i = tid + j * kStepThreads;
+      if (i < cap) {
+        sOrd[i] = ov[j];
+        sFree[i] = fv[j];
+      }
+    }
+    for (int i = tid + kPre * kStepThreads; i < cap; i += kStepThreads) {
+      sOrd[i] = d.hot_ord[i];
+      sFree[i] = d.hot_free[i];
+    }
+    for (int i = tid; i < chunk; i += kStepThreads) sInv[i] = -1;
+    __syncthreads();
+    for (int li = tid; li < min(n_hot, cap); li += kStepThreads) {
+      const int slot = sOrd[li];
+      if (slot < 0 || slot >= cap) {
+        set_status(st, HC_DEV_INDEX);
+        continue;
+      }
+      const int i = row_of_slot(slot);
+      if (i >= 0) sInv[i] = li;
+    }
+  };
+  if (early_hot) stage_hot();
+  if (early_held) {
+    held_len = st->held_len;
+    if (hv_ok) {
+      hval = d.held_valid[tid];
+      hpos = d.held_pos[tid];
+    }
   }
   // L2 prefetch of the state that is read after the wait (the launch before this one may still
   // write it: a prefetch only warms L2, which is safe for such lines)
@@ -456,15 +503,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     if (!early_held) issue_rows(true);
     if (!early_hot) issue_rows(false);
   }
-  if (!early_hot) load_order();
-  if (!early_held && hv_ok) {
-    hval = d.held_valid[tid];
-    hpos = d.held_pos[tid];
+  if (!early_held) {
+    held_len = st->held_len;
+    if (hv_ok) {
+      hval = d.held_valid[tid];
+      hpos = d.held_pos[tid];
+    }
   }
-  // ---- one round trip: counters and the new token's inputs ----
-  hc_seq_state* st = d.st;
-  const int n_hot = st->n_hot, n_free = st->n_free, held_len = st->held_len;
-  const int qwin_head = st->qwin_head, cold_head = st->cold_head, cold_count = st->cold_count;
+  // ---- the new token's inputs (with the hot tier's state, when it is read after the wait, in
+  //      the same round trip) ----
   const int64_t cur_pos = a.pos[s];
   const T* __restrict__ qp = reinterpret_cast<const T*>(a.q_pre) + (size_t)s * a.qss;
   const T* __restrict__ kp = reinterpret_cast<const T*>(a.k_pre) + (size_t)s * a.kvss + (size_t)h * D;
@@ -494,6 +541,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     }
   }
   const T vnew = tid < D ? vp[tid] : E::from_f(0.f);
+  if (!early_hot) stage_hot();
   // the last CTA stages the query rows for the query-pool push
   const bool qpush = rank == ncta - 1 && d.p_max > 0;
   constexpr int kQP = 16;
@@ -515,18 +563,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       }
     }
   }
-#pragma unroll
-  for (int j = 0; j < kPre; ++j) {
-    const int i = tid + j * kStepThreads;
-    if (i < cap) {
-      sOrd[i] = ov[j];
-      sFree[i] = fv[j];
-    }
-  }
-  for (int i = tid + kPre * kStepThreads; i < cap; i += kStepThreads) {
-    sOrd[i] = d.hot_ord[i];
-    sFree[i] = d.hot_free[i];
-  }
   if (hv_ok) sHeld[tid] = hval != 0 && hpos <= cur_pos;
   if (qpush) {
 #pragma unroll
@@ -538,7 +574,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     for (int t = tid + kStepThreads; t < d.r_max; t += kStepThreads)
       sHeld[t] = d.held_valid[t] != 0 && d.held_pos[t] <= cur_pos;
   if (tid == 0) sMisc[4] = 0;
-  for (int i = tid; i < chunk; i += kStepThreads) sInv[i] = -1;
   __syncthreads();
 
   const int n_held = a.use_held ? max(0, min(held_len, d.r_max)) : 0;
@@ -571,18 +606,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     reinterpret_cast<T*>(d.qwin)[(size_t)qwin_slot * D + tid] = E::from_f(acc / (float)L.Hq);
   }
   auto phys_of = [&](int li) { return li < n_hot ? sOrd[li] : new_slot; };
-  auto row_of_slot = [&](int slot) { return (slot >= sb && slot < sb + ns) ? nh + slot - sb : -1; };
-
-  // ---- logical index of every own slot row; free slots stay -1 and are masked --------------
-  for (int li = tid; li < n_hot; li += kStepThreads) {
-    const int slot = sOrd[li];
-    if (slot < 0 || slot >= cap) {
-      set_status(st, HC_DEV_INDEX);
-      continue;
-    }
-    const int i = row_of_slot(slot);
-    if (i >= 0) sInv[i] = li;
-  }
   const int i_new = row_of_slot(new_slot);
   if (tid == 0 && i_new >= 0) sInv[i_new] = n_hot;
 
@@ -622,7 +645,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       reinterpret_cast<T*>(d.hot_kpre)[off + H] = E::from_f(rx[j][1]);
     }
   }
-  if (i_new >= 0 && tid < D) reinterpret_cast<T*>(d.hot_v)[((size_t)h * cap + new_slot) * D + tid] = vnew;
+  if (i_new >= 0 && tid < D) {
+    reinterpret_cast<T*>(d.hot_v)[((size_t)h * cap + new_slot) * D + tid] = vnew;
+    sVn[tid] = vnew;
+  }
   __syncthreads();
   // GQA-mean query of this KV head, rounded to the dtype (cache.py:60-64 / scoring.py:17-26)
   for (int dd = tid; dd < D; dd += kStepThreads) {
@@ -658,6 +684,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   // ---- scoring: G attention logits + the eviction logit (GQA-mean query . k) per row --------
   cluster_wait();  // every CTA of the cluster has started
   const int ecap = gm.s_cap;
+  const bool snap = L.policy == HC_POLICY_SNAPKV;
+  // running softmax statistics (max, sum rescaled to it) of the scaled eviction logits of the
+  // rows this thread scores (SnapKV: the single observation row sees every key)
+  float em = kNegInf, el = 0.f;
   auto emit = [&](int i, const float* tot) {
     const int u = u0 + i;
     bool valid;
@@ -677,6 +707,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       for (int r2 = 0; r2 < ncta; ++r2) {
         float* dst = r2 == rank ? sEv : cluster.map_shared_rank(sEv, r2);
         dst[h * ecap + li] = e;
+      }
+      if (snap) {
+        const float x = e * L.scale;
+        if (x > em) {
+          el = (em == kNegInf ? 0.f : el * __expf(em - x)) + 1.f;
+          em = x;
+        } else {
+          el += __expf(x - em);
+        }
       }
     }
   };
@@ -708,8 +747,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     }
     if (ntiles > 0 && !__syncthreads_and(mbar_wait(&bars[2], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
     tc_fence_after();
-    const int mt = warp >> 2, q4 = warp & 3;
-    if (mt < ntiles) {
+    // warp w reads lane quarter w % 4 of tiles w / 4, w / 4 + 4, ...: rows 32 w + 512 k + lane
+    for (int mt = warp >> 2; mt < ntiles; mt += kStepWarps / 4) {
+      const int q4 = warp & 3;
       float v[NL];
 #pragma unroll
       for (int c = 0; c < NL; c += 8) tmem_ld_x8(tbase + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mt * N8 + c), v + c);
@@ -768,114 +808,208 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       if (sub == 0 && i < nrows) emit(i, tot);
     }
   }
-  if (policy) cluster.sync();  // barrier A: every CTA holds the eviction logits of every head
-  else __syncthreads();
+  // each warp's statistics partial to every CTA (the arrival at barrier A follows in the
+  // attention partials, which run while the exchange completes)
+  if (policy) {
+    if (snap) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, em, o), l2 = __shfl_xor_sync(0xffffffffu, el, o);
+        const float mx = fmaxf(em, m2);
+        el = (em == kNegInf ? 0.f : el * __expf(em - mx)) + (m2 == kNegInf ? 0.f : l2 * __expf(m2 - mx));
+        em = mx;
+      }
+      if (lane < ncta) {
+        float* dst = lane == rank ? sStat : cluster.map_shared_rank(sStat, lane);
+        dst[2 * (rank * kStepWarps + warp)] = em;
+        dst[2 * (rank * kStepWarps + warp) + 1] = el;
+      }
+    }
+  }
 
-  // ---- policy: every CTA holds every head's logits; it takes the softmax statistics of all heads
-  //      and scores its own tokens; one exchange of candidates (or keys) gives every CTA the same
-  //      selection -----
+  // ---- flash-decode partial of every warp over its rows -------------------------------------
+  // warp w takes rows [w rpw, (w + 1) rpw) + k 16 rpw (rpw = ceil(nrows / 16), at most 32): the
+  // rows are spread evenly over the warps whatever lane quarter of TMEM scored them
+  const int rpw = min(32, (nrows + kStepWarps - 1) / kStepWarps);
+  auto row_warp = [&](int i) { return (i / rpw) % kStepWarps; };
+  // V rows landed (this barrier also publishes every warp's logits); the warp whose rows hold
+  // the new slot puts the new value in place, each lane its own columns, the ones it reads
+  if (!__syncthreads_and(mbar_wait(&bars[1], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
+  constexpr int CW = D / 32;  // V columns per lane
+  const int col0 = lane * CW;
+  if (i_new >= 0 && row_warp(i_new) == warp)
+#pragma unroll
+    for (int c = 0; c < CW; ++c) sV[(size_t)i_new * D + col0 + c] = sVn[col0 + c];
+  // the K rows are no longer read: their area holds the warp partials [warp][G][D], the
+  // probabilities of each warp's rows [warp][32][G] and the warps' (max, sum) [warp][G][2]
+  float* red = reinterpret_cast<float*>(smem + M.k);
+  float* sPw = red + (size_t)kStepWarps * G * D;
+  float* sWml = sPw + (size_t)kStepWarps * 32 * G;
+  float wm[G], wl[G];
+  float2 acc[G][CW / 2];
+  // arrive_a: arrive at barrier A after the maxima, so that the release of this thread's
+  // distributed shared memory stores completes while the P.V runs
+  auto warp_partial = [&](bool arrive_a) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      wm[g] = kNegInf;
+      wl[g] = 0.f;
+#pragma unroll
+      for (int c = 0; c < CW / 2; ++c) acc[g][c] = make_float2(0.f, 0.f);
+    }
+    for (int b = warp * rpw; b < nrows; b += kStepWarps * rpw)
+      if (lane < rpw && b + lane < nrows)
+#pragma unroll
+        for (int g = 0; g < G; ++g) wm[g] = fmaxf(wm[g], sA[g * chunk + b + lane]);
+#pragma unroll
+    for (int g = 0; g < G; ++g) wm[g] = warp_max(wm[g]);
+    if (arrive_a) cluster_arrive();  // barrier A
+    float* pw = sPw + (size_t)warp * 32 * G;
+    for (int b = warp * rpw; b < nrows; b += kStepWarps * rpw) {
+      const int i = b + lane;
+      const bool in = lane < rpw && i < nrows;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float x = in ? sA[g * chunk + i] : kNegInf;
+        const float pr = x == kNegInf ? 0.f : __expf(x - wm[g]);
+        pw[lane * G + g] = pr;
+        wl[g] += pr;
+      }
+      // rows read: not a free slot or an unattended held row (their V is never read)
+      const unsigned live = __ballot_sync(0xffffffffu, in && sInv[i] != -1);
+      __syncwarp();
+      const int nr = min(rpw, nrows - b);
+#pragma unroll 4
+      for (int r = 0; r < nr; ++r) {
+        // branch-free: a row not read contributes p = 0 times v = 0 (its V may hold anything)
+        const bool on = (live >> r) & 1u;
+        float pv[G], vf[CW];
+        if constexpr (G % 4 == 0) {
+#pragma unroll
+          for (int g = 0; g < G; g += 4) {
+            const float4 t = reinterpret_cast<const float4*>(pw + r * G)[g / 4];
+            pv[g] = t.x; pv[g + 1] = t.y; pv[g + 2] = t.z; pv[g + 3] = t.w;
+          }
+        } else if constexpr (G == 2) {
+          const float2 t = *reinterpret_cast<const float2*>(pw + r * G);
+          pv[0] = t.x; pv[1] = t.y;
+        } else {
+          pv[0] = pw[r];
+        }
+        unpack_n<DT, CW>(sV + (size_t)(b + r) * D + col0, vf);
+#pragma unroll
+        for (int c = 0; c < CW; ++c) vf[c] = on ? vf[c] : 0.f;
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+          for (int c = 0; c < CW / 2; ++c)
+            acc[g][c] = __ffma2_rn(make_float2(pv[g], pv[g]), make_float2(vf[2 * c], vf[2 * c + 1]), acc[g][c]);
+      }
+      __syncwarp();
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) wl[g] = warp_sum(wl[g]);
+  };
+  warp_partial(policy);
+
+  // ---- policy: every CTA holds every head's eviction logits and statistics partials and ranks
+  //      the prefix itself, so every CTA makes the same selection -----------------------------
   int n_ev = 0;
   int ev_slot = -1, ev_dst = -1, ev_li = -1;  // the single evicted token, when exactly one leaves
   if (policy) {
-    const int own_p = max(0, min(own_n, pl.prefix - own0));  // this CTA's own prefix tokens
-    const int wph = kStepWarps / L.Hk;  // warps per head (Hk divides the 16-CTA cluster, so >= 1)
-    const int hw = warp / wph, sub = warp - hw * wph;
-    const bool snap = L.policy == HC_POLICY_SNAPKV;
+    cluster_wait();  // barrier A
+    float* sC = sRed;  // per head: the softmax max and the reciprocal of the sum
     if (snap) {
-      // each head's softmax statistics over the S hot tokens in one pass (the single observation
-      // row sees every key): per lane a running max and a sum rescaled to it, combined over the
-      // lanes here and over the head's wph warps where a token is scored
-      float m = kNegInf, l = 0.f;
-      for (int li = sub * 32 + lane; li < S; li += wph * 32) {
-        const float x = sEv[hw * ecap + li] * L.scale;
-        if (x > m) {
-          l = (m == kNegInf ? 0.f : l * __expf(m - x)) + 1.f;
-          m = x;
-        } else {
-          l += __expf(x - m);
+      // each head's statistics over its S hot tokens from its P CTAs' warp partials
+      if (warp < L.Hk) {
+        const int np = P * kStepWarps;
+        float m = kNegInf, l = 0.f;
+        for (int j = lane; j < np; j += 32) {
+          const int r2 = warp * P + j / kStepWarps, w = j % kStepWarps;
+          const float m2 = sStat[2 * (r2 * kStepWarps + w)], l2 = sStat[2 * (r2 * kStepWarps + w) + 1];
+          const float mx = fmaxf(m, m2);
+          l = (m == kNegInf ? 0.f : l * __expf(m - mx)) + (m2 == kNegInf ? 0.f : l2 * __expf(m2 - mx));
+          m = mx;
         }
-      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
-        const float mx = fmaxf(m, m2);
-        l = (m == kNegInf ? 0.f : l * __expf(m - mx)) + (m2 == kNegInf ? 0.f : l2 * __expf(m2 - mx));
-        m = mx;
-      }
-      if (lane == 0) {
-        sRed[warp] = m;
-        sRed[kStepWarps + warp] = l;
+        for (int o = 16; o > 0; o >>= 1) {
+          const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+          const float mx = fmaxf(m, m2);
+          l = (m == kNegInf ? 0.f : l * __expf(m - mx)) + (m2 == kNegInf ? 0.f : l2 * __expf(m2 - mx));
+          m = mx;
+        }
+        if (lane == 0) {
+          sC[2 * warp] = m;
+          sC[2 * warp + 1] = 1.f / l;
+        }
       }
       __syncthreads();
     }
-    // keys of this CTA's own prefix tokens: a thread per (token, head), the Hk heads of a token
-    // in consecutive lanes and summed by shuffles (Hk divides 16). SnapKV (scoring.py:72-78):
-    // the max-pooled probability is exp(max logit - M) / L, exp and the division being monotone;
-    // hot/cold (cache.py:68-69): the raw logit / sqrt(D). Then the mean over heads.
-    const int npair = own_p * L.Hk;
+    // the key of prefix token li. SnapKV (scoring.py:72-78): the max-pooled probability is
+    // exp(max logit - M) / L, exp and the division being monotone; hot/cold (cache.py:68-69): the
+    // raw logit / sqrt(D). Then the mean over heads.
     const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
     const bool pmax = L.pooling == HC_POOL_MAX;
     const float inv = 1.f / sqrtf((float)L.D);
-    unsigned long long best = ~0ull;  // lowest (key, higher index) of own tokens
-    for (int base = 0; base < npair; base += kStepThreads) {
-      const int k = base + tid;
-      const bool live = k < npair;
-      const int i = k / L.Hk, hh = k - i * L.Hk;
-      const int li = own0 + i;
+    auto token_key = [&](int li) {
+      const int ua = max(0, li - pad), ub = min(S - 1, li + pad);
       float v = 0.f;
-      if (live) {
+      if (snap && pmax && pad == 3) {
+        // the configured 7-wide max pool: indices clamped into [0, S), repeats leave the max alone
+        int uu[7];
+#pragma unroll
+        for (int k = 0; k < 7; ++k) uu[k] = min(max(li - 3 + k, 0), S - 1);
+#pragma unroll 4
+        for (int hh = 0; hh < L.Hk; ++hh) {
+          const float* x = sEv + hh * ecap;
+          float mx = x[uu[0]];
+#pragma unroll
+          for (int k = 1; k < 7; ++k) mx = fmaxf(mx, x[uu[k]]);
+          v += __expf(mx * L.scale - sC[2 * hh]) * sC[2 * hh + 1];
+        }
+        return fkey(v / (float)L.Hk);
+      }
+      for (int hh = 0; hh < L.Hk; ++hh) {
         const float* x = sEv + hh * ecap;
+        float t;
         if (snap) {
-          float mh = kNegInf;
-          for (int w = 0; w < wph; ++w) mh = fmaxf(mh, sRed[hh * wph + w]);
-          float lh = 0.f;
-          for (int w = 0; w < wph; ++w) {
-            const float mw = sRed[hh * wph + w];
-            if (mw != kNegInf) lh += sRed[kStepWarps + hh * wph + w] * __expf(mw - mh);
-          }
-          const int ua = max(0, li - pad), ub = min(S - 1, li + pad);
+          const float mh = sC[2 * hh], rl = sC[2 * hh + 1];
           if (pad == 0 || pmax) {
             float mx = kNegInf;
+#pragma unroll 8
             for (int u = ua; u <= ub; ++u) mx = fmaxf(mx, x[u]);
-            v = __expf(mx * L.scale - mh) / lh;
+            t = __expf(mx * L.scale - mh) * rl;
           } else {
-            for (int u = ua; u <= ub; ++u) v += __expf(x[u] * L.scale - mh) / lh;
-            v /= (float)L.pool_kernel;
+            t = 0.f;
+            for (int u = ua; u <= ub; ++u) t += __expf(x[u] * L.scale - mh) * rl;
+            t /= (float)L.pool_kernel;
           }
         } else {
-          v = x[li] * inv;
+          t = x[li] * inv;
         }
+        v += t;
       }
-      for (int o = L.Hk >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (live && hh == 0) {
-        const uint32_t key = fkey(v / (float)L.Hk);
-        sKey[li] = key;
-        const unsigned long long c = ((unsigned long long)key << 32) | (0xffffffffu - (uint32_t)li);
-        best = c < best ? c : best;
-      }
-    }
+      return fkey(v / (float)L.Hk);
+    };
     n_ev = n_ev_plan;
     if (n_ev == 1) {
-      // one token leaves: the lowest key, equal keys evict the higher index. Each CTA reduces its
-      // own tokens and hands its candidate to every CTA (barrier C), which all take the lowest.
+      // one token leaves: the lowest key, equal keys evict the higher index
+      unsigned long long best = ~0ull;
+      for (int li = tid; li < pl.prefix; li += kStepThreads) {
+        const unsigned long long c = ((unsigned long long)token_key(li) << 32) | (0xffffffffu - (uint32_t)li);
+        best = c < best ? c : best;
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
         best = y < best ? y : best;
       }
       unsigned long long* sBest = reinterpret_cast<unsigned long long*>(sRed + 96);  // per warp
-      unsigned long long* sCand = reinterpret_cast<unsigned long long*>(sRed + 64);  // per CTA
       if (lane == 0) sBest[warp] = best;
       __syncthreads();
-      if (tid < ncta) {
-        unsigned long long b = sBest[0];
+      best = sBest[0];
 #pragma unroll
-        for (int w = 1; w < kStepWarps; ++w) b = sBest[w] < b ? sBest[w] : b;
-        cluster.map_shared_rank(sCand, tid)[rank] = b;
-      }
-      cluster.sync();  // barrier C: every CTA's candidate everywhere
-      best = sCand[0];
-      for (int r2 = 1; r2 < ncta; ++r2) best = sCand[r2] < best ? sCand[r2] : best;
+      for (int w = 1; w < kStepWarps; ++w) best = sBest[w] < best ? sBest[w] : best;
       const int li_ev = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
       ev_slot = phys_of(li_ev);
       ev_li = li_ev;
@@ -900,11 +1034,38 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         if (li > li_ev) d.hot_ord[li - 1] = ph;
         else if (li == li_ev && n_free - 1 < cap) d.hot_free[n_free - 1] = ph;
       }
-      const int i_ev = row_of_slot(phys_of(li_ev));
-      if (i_ev >= 0 && tid < G) sA[tid * chunk + i_ev] = kNegInf;
-      __syncthreads();
+      // the warp whose partial holds the evicted row takes it out again; where that row carried
+      // most of a head's mass (the difference would cancel) the warp recomputes without it
+      const int i_ev = row_of_slot(ev_slot);
+      if (i_ev >= 0 && row_warp(i_ev) == warp) {
+        float pe[G];
+        bool redo = false;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float x = sA[g * chunk + i_ev];
+          pe[g] = x == kNegInf ? 0.f : __expf(x - wm[g]);
+          redo |= !(wl[g] - pe[g] >= 0.25f * wl[g]);
+        }
+        if (redo) {
+          if (lane < G) sA[lane * chunk + i_ev] = kNegInf;
+          __syncwarp();
+          warp_partial(false);
+        } else {
+          float vf[CW];
+          unpack_n<DT, CW>(sV + (size_t)i_ev * D + col0, vf);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int c = 0; c < CW / 2; ++c)
+              acc[g][c] = __ffma2_rn(make_float2(-pe[g], -pe[g]), make_float2(vf[2 * c], vf[2 * c + 1]), acc[g][c]);
+            wl[g] -= pe[g];
+          }
+        }
+      }
     } else {
       // every CTA needs every prefix key: own keys to all CTAs (barrier C)
+      const int own_p = max(0, min(own_n, pl.prefix - own0));  // this CTA's own prefix tokens
+      for (int li = own0 + tid; li < own0 + own_p; li += kStepThreads) sKey[li] = token_key(li);
       __syncthreads();
       for (int k = tid; k < ncta * own_p; k += kStepThreads) {
         const int r2 = k / own_p, li = own0 + (k - r2 * own_p);
@@ -951,22 +1112,23 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
           const bool in = t < S;
           const bool ev = in && ((sMask[w0 + wi] >> lane) & 1u);
           const bool keep = in && !ev;
-          const unsigned km = __ballot_sync(0xffffffffu, keep), em = __ballot_sync(0xffffffffu, ev);
+          const unsigned km = __ballot_sync(0xffffffffu, keep), em2 = __ballot_sync(0xffffffffu, ev);
           const int ph = in ? phys_of(t) : -1;
           if (keep) d.hot_ord[kb + __popc(km & lt)] = ph;
           if (ev) {
-            const int j = eb + __popc(em & lt), jl = nloc + __popc(em & lt);
+            const int j = eb + __popc(em2 & lt), jl = nloc + __popc(em2 & lt);
             if (n_free - 1 + j < cap) d.hot_free[n_free - 1 + j] = ph;
             sEvl[3 * jl] = ph;
             sEvl[3 * jl + 1] = (j >= n_ev - d.ccap) ? (int)(((long)cold_head + cold_count + j) % d.ccap) : -1;
             sEvl[3 * jl + 2] = t;
           }
           kb += __popc(km);
-          eb += __popc(em);
-          nloc += __popc(em);
+          eb += __popc(em2);
+          nloc += __popc(em2);
         }
         if (lane == 0) sMisc[4] = nloc;
       }
+      // the evicted rows leave the attention: every warp recomputes its partial
       for (int i = tid; i < nrows; i += kStepThreads) {
         const int li = sInv[i];
         if (li >= 0 && ((sMask[li >> 5] >> (li & 31)) & 1u))
@@ -974,108 +1136,53 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
           for (int g = 0; g < G; ++g) sA[g * chunk + i] = kNegInf;
       }
       __syncthreads();
+      warp_partial(false);
     }
   }
 
-  // ---- flash-decode partial over this part's rows -------------------------------------------
-  float* sPm = sRed + 4 * kStepMaxCluster;              // per-warp maxima
-  float* sLw = sRed + 4 * kStepMaxCluster + kStepWarps;  // per-warp probability sums [warp][g]
-  {
-    constexpr int WPG = kStepWarps / G;
-    const int g = warp % G, sl = warp / G;
-    float m = kNegInf;
-    for (int i = sl * 32 + lane; i < nrows; i += WPG * 32) m = fmaxf(m, sA[g * chunk + i]);
-    m = warp_max(m);
-    if (lane == 0) sPm[warp] = m;
-  }
-  __syncthreads();
-  float mg[G];
+  // ---- warp partials combined per column, each column block sent to the CTA of head h that
+  //      finalizes it ---------------------------------------------------------------------------
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float m = kNegInf;
+    float* dst = red + ((size_t)warp * G + g) * D + col0;
+    if constexpr (CW % 4 == 0) {
 #pragma unroll
-    for (int sl = 0; sl < kStepWarps / G; ++sl) m = fmaxf(m, sPm[sl * G + g]);
-    mg[g] = m;
+      for (int c = 0; c < CW / 2; c += 2)
+        reinterpret_cast<float4*>(dst)[c / 2] = make_float4(acc[g][c].x, acc[g][c].y, acc[g][c + 1].x, acc[g][c + 1].y);
+    } else {
+#pragma unroll
+      for (int c = 0; c < CW / 2; ++c) reinterpret_cast<float2*>(dst)[c] = acc[g][c];
+    }
   }
-  {
-    float ls[G];
+  if (lane == 0)
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      ls[g] = 0.f;
-      for (int i = tid; i < nrows; i += kStepThreads) {
-        const float x = sA[g * chunk + i];
-        const float pr = (x == kNegInf) ? 0.f : __expf(x - mg[g]);
-        sA[g * chunk + i] = pr;
-        ls[g] += pr;
-      }
+      sWml[2 * (warp * G + g)] = wm[g];
+      sWml[2 * (warp * G + g) + 1] = wl[g];
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float v = warp_sum(ls[g]);
-      if (lane == 0) sLw[warp * G + g] = v;
-    }
-  }
-  // V rows landed: the new value replaces the stale copy of its slot
-  if (!__syncthreads_and(mbar_wait(&bars[1], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
-  if (i_new >= 0 && tid < D) sV[(size_t)i_new * D + tid] = vnew;
   __syncthreads();
-  float* red = reinterpret_cast<float*>(smem + M.k);  // the K rows are no longer needed
-  {
-    const int c = tid % KCH, grp = tid / KCH, ngrp = kStepThreads / KCH;
-    float2 o[G][VE / 2];
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-      for (int e = 0; e < VE / 2; ++e) o[g][e] = make_float2(0.f, 0.f);
-    for (int i = grp; i < nrows; i += ngrp) {
-      if (sInv[i] == -1) continue;  // free slot or unattended held row: never read its V
-      float vf[VE];
-      unpack16<DT>(*reinterpret_cast<const uint4*>(sV + (size_t)i * D + c * VE), vf);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float pr = sA[g * chunk + i];
-        const float2 p2 = make_float2(pr, pr);
-#pragma unroll
-        for (int e = 0; e < VE / 2; ++e) o[g][e] = __ffma2_rn(p2, make_float2(vf[2 * e], vf[2 * e + 1]), o[g][e]);
-      }
-    }
-    for (int off = KCH; off < 32; off <<= 1) {
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int e = 0; e < VE / 2; ++e) {
-          o[g][e].x += __shfl_xor_sync(0xffffffffu, o[g][e].x, off);
-          o[g][e].y += __shfl_xor_sync(0xffffffffu, o[g][e].y, off);
-        }
-    }
-    if (lane < KCH) {
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int e = 0; e < VE / 2; ++e)
-          *reinterpret_cast<float2*>(red + ((size_t)warp * G + g) * D + c * VE + 2 * e) = o[g][e];
-    }
-  }
-  __syncthreads();
-  // ---- each column block goes to the CTA of head h that finalizes it ------------------------
   const int DB = D / P;
   for (int k = tid; k < G * D; k += kStepThreads) {
     const int g = k / D, dd = k - g * D;
-    float v = 0.f;
+    float Mx = kNegInf;
 #pragma unroll
-    for (int w = 0; w < kStepWarps; ++w) v += red[((size_t)w * G + g) * D + dd];
+    for (int w = 0; w < kStepWarps; ++w) Mx = fmaxf(Mx, sWml[2 * (w * G + g)]);
+    float v = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kStepWarps; ++w) {
+      const float mw = sWml[2 * (w * G + g)];
+      const float e = mw == kNegInf ? 0.f : __expf(mw - Mx);
+      v = fmaf(red[((size_t)w * G + g) * D + dd], e, v);
+      l = fmaf(sWml[2 * (w * G + g) + 1], e, l);
+    }
     const int q = dd / DB, col = dd - q * DB;
     float* dst = q == p ? sO : cluster.map_shared_rank(sO, h * P + q);
     dst[((size_t)p * G + g) * DB + col] = v;
-  }
-  if (tid < G * P) {
-    const int g = tid % G, q = tid / G;
-    float l = 0.f;
-#pragma unroll
-    for (int w = 0; w < kStepWarps; ++w) l += sLw[w * G + g];
-    float* dst = q == p ? sML : cluster.map_shared_rank(sML, h * P + q);
-    dst[2 * (p * G + g)] = mg[g];
-    dst[2 * (p * G + g) + 1] = l;
+    if (col == 0) {
+      float* dml = q == p ? sML : cluster.map_shared_rank(sML, h * P + q);
+      dml[2 * (p * G + g)] = Mx;
+      dml[2 * (p * G + g) + 1] = l;
+    }
   }
   cluster.sync();  // last barrier: no distributed shared memory access after this point
   T* outp = reinterpret_cast<T*>(a.out) + ((size_t)s * L.Hq + (size_t)h * G) * D + (size_t)p * DB;
