@@ -190,19 +190,20 @@ class LayerArena:
         return int(dev.value)
 
     def _encode_kmaps(self):
-        """TMA tensor maps of the hot K slab (all sequences as rows of D, 64-row boxes) and the
-        held K rows (8-row boxes) for the fused step's 16-bit path; 0 when unavailable."""
+        """TMA tensor maps for the fused step's 16-bit path, all sequences as rows of D: the hot
+        K slab (64-row boxes), the held K rows (8-row boxes), the hot V slab (16-row boxes) and
+        the held V rows (8-row boxes); 0 when unavailable."""
         self.kmaps = None
         if self.dtype not in (torch.float16, torch.bfloat16):
             return 0
-        buf = (ctypes.c_uint8 * 256)()
+        buf = (ctypes.c_uint8 * 512)()
         code = _lib.dtype_code(self.dtype)
         lib = _lib.load()
-        rc = lib.hc_encode_kmap(ctypes.addressof(buf), self.hot_k.data_ptr(), code,
-                                self.hot_k.numel() // self.D, self.D, 64)
-        if rc == 0:
-            rc = lib.hc_encode_kmap(ctypes.addressof(buf) + 128, self.held_k.data_ptr(), code,
-                                    self.held_k.numel() // self.D, self.D, 8)
+        rc = 0
+        for i, (t, box) in enumerate(((self.hot_k, 64), (self.held_k, 8), (self.hot_v, 16), (self.held_v, 8))):
+            if rc == 0:
+                rc = lib.hc_encode_kmap(ctypes.addressof(buf) + 128 * i, t.data_ptr(), code, t.numel() // self.D,
+                                        self.D, box)
         if rc != 0:
             return 0
         self.kmaps = torch.frombuffer(bytearray(bytes(buf)), dtype=torch.uint8).to(self.device)

@@ -206,6 +206,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this CTA's shared
+// memory to the same-offset buffer of cluster CTA `rank`, completing on that CTA's mbarrier at
+// the offset of `bar` (distributed shared memory through the TMA engine).
+__device__ __forceinline__ void bulk_s2cluster(void* buf, uint32_t bytes, uint64_t* bar, uint32_t rank) {
+  uint32_t dst, rbar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(smem_u32(buf)), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(smem_u32(bar)), "r"(rank));
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(smem_u32(buf)), "r"(bytes), "r"(rbar)
+               : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -302,6 +313,17 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
   d |= (uint64_t)1u << 16;                           // leading byte offset (unused by this layout)
   d |= (uint64_t)(1024u >> 4) << 32;                 // stride byte offset: next 8-row atom
+  d |= (uint64_t)1u << 46;                           // descriptor version
+  d |= (uint64_t)2u << 61;                           // 128-byte swizzle
+  return d;
+}
+// Descriptor of an MN-major operand in the 128-byte swizzle layout: 8-row (K) atoms of 128-byte
+// rows holding 64 MN-contiguous elements, 8-row groups 1024 bytes apart (stride byte offset), the
+// next 64 elements of MN `lbo` bytes further (leading byte offset); atoms 1024-aligned.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;       // leading byte offset: next 64 MN elements
+  d |= (uint64_t)(1024u >> 4) << 32;                 // stride byte offset: next 8 K rows
   d |= (uint64_t)1u << 46;                           // descriptor version
   d |= (uint64_t)2u << 61;                           // 128-byte swizzle
   return d;

@@ -50,11 +50,13 @@ struct StepGeom {
   int krows;  // rows of the K area: with tensor-core scoring, whole 128-row tiles and the slack of
               // the last 64-row TMA box
   int r8;     // held rows in the physical order, a multiple of 8 (rows past r_max are masked)
+  int vrows;  // rows of the V area: with tensor-core P.V, the 16-row boxes' slack included
+  int xs;     // floats per CTA in the exchange: its rows' eviction logits, then 16 warps' statistics
   int s_cap;  // hot tokens at most
   int wpc;    // 32-token words a CTA owns at most
 };
 
-__host__ __device__ inline StepGeom step_geom(int Hk, int max_cap, int max_r, int use_held, bool mma) {
+__host__ __device__ inline StepGeom step_geom(int Hk, int max_cap, int max_r, int use_held, bool mma, bool pv_mma) {
   StepGeom g{};
   g.P = (Hk >= 1 && Hk <= kStepMaxCluster && kStepMaxCluster % Hk == 0) ? kStepMaxCluster / Hk : 0;
   if (!g.P) return g;
@@ -63,6 +65,8 @@ __host__ __device__ inline StepGeom step_geom(int Hk, int max_cap, int max_r, in
   const int rows = g.r8 + max_cap;
   g.chunk = (((rows + g.P - 1) / g.P) + 7) & ~7;
   g.krows = mma ? ((g.chunk + 64 + 127) & ~127) : g.chunk;
+  g.vrows = pv_mma ? g.chunk + 16 : g.chunk;
+  g.xs = g.chunk + 2 * kStepWarps;
   g.wpc = ((max_cap + 31) / 32 + kStepMaxCluster - 1) / kStepMaxCluster;
   return g;
 }
@@ -84,7 +88,8 @@ struct StepArgs {
 };
 
 struct StepSmem {
-  size_t k, qb, v, q, knew, vn, a, inv, ord, fre, held, ev, stat, key, red, mask, evl, o, ml, qp, misc, tmem, bars, total;
+  size_t k, qb, v, q, knew, vn, a, inv, ord, fre, held, xch, loc, wst, key, red, mask, evl, o, ml, misc, tmem, bars,
+      total;
 };
 
 __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -102,7 +107,10 @@ __host__ __device__ inline StepSmem step_smem(int D, int esz, int G, int Hk, int
   m.k = take(kb > rb ? kb : rb);
   o = (o + 1023) & ~size_t(1023);
   m.qb = take((size_t)16 * D * esz);  // MMA query operand: G heads, the mean, zero rows (N = 16)
-  m.v = take((size_t)g.chunk * D * esz);
+  // V rows: 16-bit, D/64 planes of 128-byte swizzled rows (1024-aligned) read by the P.V MMAs;
+  // f32, plain rows
+  m.v = take((size_t)g.vrows * D * esz);
+  o = (o + 1023) & ~size_t(1023);
   m.q = take((size_t)(G + 1) * D * 4);       // RoPE'd query heads and their GQA mean
   m.knew = take((size_t)D * esz);            // the new key after RoPE
   m.vn = take((size_t)D * esz);              // the new value
@@ -111,18 +119,19 @@ __host__ __device__ inline StepSmem step_smem(int D, int esz, int G, int Hk, int
   m.ord = take((size_t)g.s_cap * 4);         // logical order (physical slot per logical index)
   m.fre = take((size_t)g.s_cap * 4);         // free-slot stack
   m.held = take((size_t)(max_r > 0 ? max_r : 1) * 4);  // held rows attended this step
-  m.ev = take((size_t)Hk * g.s_cap * 4);     // eviction logits of every head, by logical index
-  m.stat = take((size_t)kStepMaxCluster * kStepWarps * 2 * 4);  // softmax partials of every warp
+  // exchange: every CTA's eviction logits by physical row and its warps' softmax statistics
+  m.xch = take((size_t)kStepMaxCluster * g.xs * 4);
+  m.loc = take((size_t)g.s_cap * 4);  // where each hot token's row sits in a head's exchange
+  m.wst = take((size_t)2 * kStepWarps * G * 4);  // each warp's attention-logit maxima and sums
   m.key = take((size_t)g.s_cap * 4);         // policy score keys of the prefix, by logical index
   m.red = take((size_t)(4 * kStepMaxCluster + 4 * kStepWarps) * 8);
   m.mask = take(step_words(g.s_cap) * 4);    // evicted tokens, one bit per logical index
   m.evl = take((size_t)3 * g.wpc * 32 * 4);  // evicted tokens of the words this CTA owns
   m.o = take((size_t)G * D * 4);             // partials of this CTA's column block from every part
   m.ml = take((size_t)2 * G * kStepMaxCluster * 4);
-  m.qp = take((size_t)G * Hk * D * esz);  // the new token's pre-RoPE query rows (query-pool push)
   m.misc = take(64);
   m.tmem = take(16);
-  m.bars = take(32);
+  m.bars = take(48);
   m.total = o + 1024;  // room to align the dynamic shared memory base to 1024 bytes
   return m;
 }
@@ -275,6 +284,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   constexpr int N8 = 16;                      // MMA N (M = 128 takes N in steps of 16): heads + mean, padded
   constexpr int NL = ((G + 1 + 7) / 8) * 8;   // accumulator columns read back
   constexpr int PL = D / 64;                  // 128-byte planes of a K row
+  // P.V on the tensor cores (16-bit, D = 128: M = D = 128 lanes of O^T, N = 16 query columns):
+  // V arrives in the swizzled planes the MMA reads as its MN-major A operand
+  constexpr bool PVMMA = MMA && D == 128;
+  constexpr uint32_t kFmt = DT == HC_BF16 ? 1u : 0u;
+  // instruction descriptor: f32 accumulate, A and B of the layer's type, N = 16, M = 128, K-major
+  constexpr uint32_t kIdesc = (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((uint32_t)(N8 >> 3) << 17) |
+                              ((uint32_t)(128 >> 4) << 24);
   static_assert(KCH % 8 == 0, "rows must be a multiple of 128 bytes");
   static_assert(G + 1 <= 16, "query heads per KV head");
   cg::cluster_group cluster = cg::this_cluster();
@@ -286,9 +302,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const int s = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int chunk = gm.chunk;
-
-  // arrival: this CTA has started; waited on before the first distributed shared memory store
-  cluster_arrive_relaxed();
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -305,8 +318,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   int* sOrd = reinterpret_cast<int*>(smem + M.ord);
   int* sFree = reinterpret_cast<int*>(smem + M.fre);
   int* sHeld = reinterpret_cast<int*>(smem + M.held);
-  float* sEv = reinterpret_cast<float*>(smem + M.ev);  // [Hk][s_cap]
-  float* sStat = reinterpret_cast<float*>(smem + M.stat);  // [cluster rank][warp] (max, sum)
+  float* sX = reinterpret_cast<float*>(smem + M.xch);  // [cluster rank][xs]
+  int* sLoc = reinterpret_cast<int*>(smem + M.loc);     // [logical index]: part * xs + row
+  float* sWst = reinterpret_cast<float*>(smem + M.wst);    // [warp][G] maxima, then [warp][G] sums
   uint32_t* sKey = reinterpret_cast<uint32_t*>(smem + M.key);
   float* sRed = reinterpret_cast<float*>(smem + M.red);  // per-warp partials and per-head statistics
   uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + M.mask);
@@ -314,7 +328,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   float* sO = reinterpret_cast<float*>(smem + M.o);
   float* sML = reinterpret_cast<float*>(smem + M.ml);
   int* sMisc = reinterpret_cast<int*>(smem + M.misc);
-  T* sQP = reinterpret_cast<T*>(smem + M.qp);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + M.bars);
 
   // the descriptor is written once when the layer is set up, so it is read before the wait
@@ -334,22 +347,27 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const bool early_hot = (a.early & HC_STEP_EARLY_HOT) != 0;    // slab K/V, order table, free stack
   const bool early_held = (a.early & HC_STEP_EARLY_HELD) != 0;  // held K/V rows and their flags
 
-  // ---- copies of this part's K rows (TMA tensor boxes into the swizzled MMA layout for 16-bit
-  //      types, else bulk copies) and V rows (bulk copies), issued by warp 0 ----
-  const int nhb = nh >> 3, nsb = (ns + 63) >> 6;  // 8-row held boxes, 64-row slot boxes
+  // ---- copies of this part's K and V rows, issued by warp 0: for 16-bit types TMA tensor boxes
+  //      into the swizzled layout the MMAs read (K: 64-row slot boxes; V: 16-row slot boxes, so
+  //      that the V area needs little slack; 8-row boxes for held rows), for f32 bulk copies ----
+  const int nhb = nh >> 3, nsb = (ns + 63) >> 6, nsv = (ns + 15) >> 4;
   if (warp == 0) {
     if (lane == 0) {
       mbar_init(&bars[0], 1);
       mbar_init(&bars[1], 1);
       mbar_init(&bars[2], 1);
+      mbar_init(&bars[3], 1);
+      mbar_init(&bars[4], 1);  // the exchange: peers' copies complete on it
       fence_mbar_init();
       const uint32_t vbytes = (uint32_t)((nhr + ns) * ROWB);
-      if constexpr (MMA) mbar_arrive_expect_tx(&bars[0], (uint32_t)((nh + 64 * nsb) * 128 * PL));
-      else mbar_arrive_expect_tx(&bars[0], vbytes);
-      mbar_arrive_expect_tx(&bars[1], vbytes);
+      mbar_arrive_expect_tx(&bars[0], MMA ? (uint32_t)((nh + 64 * nsb) * 128 * PL) : vbytes);
+      mbar_arrive_expect_tx(&bars[1], PVMMA ? (uint32_t)((nh + 16 * nsv) * 128 * PL) : vbytes);
     }
     __syncwarp();
   }
+  // arrival: this CTA has started and initialised its barriers; waited on before the first
+  // distributed shared memory access
+  cluster_arrive_relaxed();
   auto issue_rows = [&](bool held) {
     // warp 0 only: the K boxes of the held rows or of the slab slots, then their V copy
     if constexpr (MMA) {
@@ -363,6 +381,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         if (held) tma_load_2d(plane + (size_t)j * 8 * 128, kmaps + 128, pl * 64, y_held + 8 * j, &bars[0]);
         else tma_load_2d(plane + (size_t)(nh + 64 * j) * 128, kmaps, pl * 64, y_hot + 64 * j, &bars[0]);
       }
+      if constexpr (PVMMA) {
+        const int nbv = held ? nhb : nsv;
+        for (int b = lane; b < nbv * PL; b += 32) {
+          const int pl = b / nbv, j = b - pl * nbv;
+          unsigned char* plane = reinterpret_cast<unsigned char*>(sV) + (size_t)pl * gm.vrows * 128;
+          if (held) tma_load_2d(plane + (size_t)j * 8 * 128, kmaps + 384, pl * 64, y_held + 8 * j, &bars[1]);
+          else tma_load_2d(plane + (size_t)(nh + 16 * j) * 128, kmaps + 256, pl * 64, y_hot + 16 * j, &bars[1]);
+        }
+      }
     } else {
       if (lane == 1 && held && nhr > 0)
         bulk_g2s(sK, reinterpret_cast<const T*>(d.held_k) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
@@ -371,18 +398,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         bulk_g2s(sK + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_k) + ((size_t)h * d.cap + sb) * D,
                  (uint32_t)(ns * ROWB), &bars[0]);
     }
-    if (lane == 3 && held && nhr > 0)
-      bulk_g2s(sV, reinterpret_cast<const T*>(d.held_v) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
-               &bars[1]);
-    if (lane == 4 && !held && ns > 0)
-      bulk_g2s(sV + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_v) + ((size_t)h * d.cap + sb) * D,
-               (uint32_t)(ns * ROWB), &bars[1]);
+    if constexpr (!PVMMA) {
+      if (lane == 3 && held && nhr > 0)
+        bulk_g2s(sV, reinterpret_cast<const T*>(d.held_v) + ((size_t)h * d.r_max + hb) * D, (uint32_t)(nhr * ROWB),
+                 &bars[1]);
+      if (lane == 4 && !held && ns > 0)
+        bulk_g2s(sV + (size_t)nh * D, reinterpret_cast<const T*>(d.hot_v) + ((size_t)h * d.cap + sb) * D,
+                 (uint32_t)(ns * ROWB), &bars[1]);
+    }
   };
   if (warp == 0) {
-    if (MMA && lane == 31) {
-      prefetch_tensormap(L.kmaps);  // both maps: the hot K slab and the held K rows
-      prefetch_tensormap(reinterpret_cast<const char*>(L.kmaps) + 128);
-    }
+    // the four maps: hot K slab, held K rows, hot V slab, held V rows
+    if (MMA && lane >= 28) prefetch_tensormap(reinterpret_cast<const char*>(L.kmaps) + 128 * (lane - 28));
     if (early_held) issue_rows(true);
     if (early_hot) issue_rows(false);
   }
@@ -403,6 +430,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   uint8_t hval = 0;
   int64_t hpos = 0;
   auto row_of_slot = [&](int slot) { return (slot >= sb && slot < sb + ns) ? nh + slot - sb : -1; };
+  // the exchange entry of a slot within a head's P parts: part * xs + row in the part
+  auto loc_of_slot = [&](int slot) {
+    const int u = R + slot, q = u / chunk;
+    return q * gm.xs + (u - q * chunk);
+  };
   // the hot tier's counters, order table and free stack into registers and shared memory, and the
   // logical index of every own slot row (free slots stay -1 and are masked)
   hc_seq_state* st = d.st;
@@ -432,10 +464,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       const int slot = sOrd[li];
       if (slot < 0 || slot >= cap) {
         set_status(st, HC_DEV_INDEX);
+        sLoc[li] = 0;
         continue;
       }
       const int i = row_of_slot(slot);
       if (i >= 0) sInv[i] = li;
+      sLoc[li] = loc_of_slot(slot);
     }
   };
   if (early_hot) stage_hot();
@@ -544,12 +578,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   if (!early_hot) stage_hot();
   // the last CTA stages the query rows for the query-pool push
   const bool qpush = rank == ncta - 1 && d.p_max > 0;
-  constexpr int kQP = 16;
-  T tq[kQP];
-  if (qpush)
-#pragma unroll
-    for (int j = 0; j < kQP; ++j)
-      if (tid + j * kStepThreads < L.Hq * D) tq[j] = qp[tid + j * kStepThreads];
+  float qsum = 0.f;  // this thread's column of the query pool's new entry (the last CTA)
+  if (qpush && tid < D)
+    for (int hh = 0; hh < L.Hq; ++hh) qsum += E::to_f(qp[(size_t)hh * D + tid]);
 #pragma unroll
   for (int j = 0; j < RP; ++j) {
     if (tid + j * kStepThreads < (G + 1) * H) {
@@ -564,12 +595,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     }
   }
   if (hv_ok) sHeld[tid] = hval != 0 && hpos <= cur_pos;
-  if (qpush) {
-#pragma unroll
-    for (int j = 0; j < kQP; ++j)
-      if (tid + j * kStepThreads < L.Hq * D) sQP[tid + j * kStepThreads] = tq[j];
-    for (int k = tid + kQP * kStepThreads; k < L.Hq * D; k += kStepThreads) sQP[k] = qp[k];
-  }
   if (a.use_held)
     for (int t = tid + kStepThreads; t < d.r_max; t += kStepThreads)
       sHeld[t] = d.held_valid[t] != 0 && d.held_pos[t] <= cur_pos;
@@ -593,6 +618,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const Plan pl = step_plan(L, d.budget, S);
   const int n_ev_plan = pl.active ? pl.prefix - pl.ntop : 0;
   const bool policy = pl.active && n_ev_plan > 0;
+  // the exchange brings one block from every other CTA of the cluster
+  if (policy && tid == 0) mbar_arrive_expect_tx(&bars[4], (uint32_t)((ncta - 1) * gm.xs * 4));
   const int nwords = (S + 31) >> 5;
   // CTA r owns the 32-token words w with w * ncta / nwords == r: it writes their entries of the
   // order table and free stack and copies their evicted tokens into the cold ring
@@ -600,14 +627,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   const int own0 = w0 * 32, own_n = max(0, min(w1 * 32, S) - own0), nw_own = w1 - w0;
   const int qwin_slot = d.p_max > 0 ? ((qwin_head % d.p_max) + d.p_max) % d.p_max : 0;
   // query pool push: mean over all query heads of the pre-RoPE query (controller.py:240-241)
-  if (qpush && tid < D) {
-    float acc = 0.f;
-    for (int hh = 0; hh < L.Hq; ++hh) acc += E::to_f(sQP[hh * D + tid]);
-    reinterpret_cast<T*>(d.qwin)[(size_t)qwin_slot * D + tid] = E::from_f(acc / (float)L.Hq);
-  }
+  if (qpush && tid < D) reinterpret_cast<T*>(d.qwin)[(size_t)qwin_slot * D + tid] = E::from_f(qsum / (float)L.Hq);
   auto phys_of = [&](int li) { return li < n_hot ? sOrd[li] : new_slot; };
   const int i_new = row_of_slot(new_slot);
-  if (tid == 0 && i_new >= 0) sInv[i_new] = n_hot;
+  if (tid == 0) {
+    if (i_new >= 0) sInv[i_new] = n_hot;
+    sLoc[n_hot] = loc_of_slot(new_slot);
+  }
 
   // ---- RoPE of the new token (patch.py:161-162) while the copies are in flight --------------
 #pragma unroll
@@ -683,7 +709,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 
   // ---- scoring: G attention logits + the eviction logit (GQA-mean query . k) per row --------
   cluster_wait();  // every CTA of the cluster has started
-  const int ecap = gm.s_cap;
   const bool snap = L.policy == HC_POLICY_SNAPKV;
   // running softmax statistics (max, sum rescaled to it) of the scaled eviction logits of the
   // rows this thread scores (SnapKV: the single observation row sees every key)
@@ -702,12 +727,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 #pragma unroll
     for (int g = 0; g < G; ++g) sA[g * chunk + i] = valid ? tot[g] * L.scale : kNegInf;
     if (policy && li >= 0) {
-      // every CTA of the cluster receives every head's eviction logits (barrier A)
+      // this CTA's block of the exchange, by physical row
       const float e = tot[G];
-      for (int r2 = 0; r2 < ncta; ++r2) {
-        float* dst = r2 == rank ? sEv : cluster.map_shared_rank(sEv, r2);
-        dst[h * ecap + li] = e;
-      }
+      sX[rank * gm.xs + i] = e;
       if (snap) {
         const float x = e * L.scale;
         if (x > em) {
@@ -719,21 +741,23 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       }
     }
   };
+  // TMEM: the scoring tiles' accumulators, then (tensor-core P.V) the 16 columns of O^T
+  uint32_t tbase = 0, tcols = 0;
+  int colO = 0;
   if constexpr (MMA) {
     // tcgen05: one thread issues, per 128-row tile, D/16 MMAs of 128 x N8 x 16 into TMEM; warps
     // then read their lane quarter of each tile with tcgen05.ld
     const int ntiles = (nrows + 127) >> 7;
     const int need = gm.krows / 128 * N8;
-    const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : 256u;
-    if (warp == 0) tmem_alloc(sTmem, ncols);
+    colO = need;
+    const int want = need + (PVMMA ? N8 : 0);
+    tcols = want <= 32 ? 32u : want <= 64 ? 64u : want <= 128 ? 128u : want <= 256 ? 256u : 512u;
+    if (warp == 0) tmem_alloc(sTmem, tcols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tbase = *sTmem;
+    tbase = *sTmem;
     if (tid == 0 && ntiles > 0) {
-      constexpr uint32_t fmt = DT == HC_BF16 ? 1u : 0u;
-      constexpr uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(N8 >> 3) << 17) |
-                                 ((uint32_t)(128 >> 4) << 24);
       const uint32_t a0 = smem_u32(sK), b0 = smem_u32(sQb);
       for (int mt = 0; mt < ntiles; ++mt)
 #pragma unroll
@@ -741,24 +765,40 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
           const uint32_t pl = ks >> 2, kin = ks & 3;
           const uint32_t aa = a0 + pl * (uint32_t)gm.krows * 128u + (uint32_t)mt * 128u * 128u + kin * 32u;
           const uint32_t bb = b0 + pl * (uint32_t)N8 * 128u + kin * 32u;
-          umma_f16(tbase + (uint32_t)(mt * N8), umma_desc_k_sw128(aa), umma_desc_k_sw128(bb), idesc, ks > 0);
+          umma_f16(tbase + (uint32_t)(mt * N8), umma_desc_k_sw128(aa), umma_desc_k_sw128(bb), kIdesc, ks > 0);
         }
       umma_commit(&bars[2]);
     }
     if (ntiles > 0 && !__syncthreads_and(mbar_wait(&bars[2], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
     tc_fence_after();
-    // warp w reads lane quarter w % 4 of tiles w / 4, w / 4 + 4, ...: rows 32 w + 512 k + lane
+    // warp w reads lane quarter w % 4 of tiles w / 4, w / 4 + 4, ...: rows 32 w + 512 k + lane;
+    // with tensor-core P.V it also takes the maxima of its rows' attention logits
+    float xm[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) xm[g] = kNegInf;
     for (int mt = warp >> 2; mt < ntiles; mt += kStepWarps / 4) {
       const int q4 = warp & 3;
       float v[NL];
 #pragma unroll
       for (int c = 0; c < NL; c += 8) tmem_ld_x8(tbase + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mt * N8 + c), v + c);
       const int i = mt * 128 + q4 * 32 + lane;
-      if (i < nrows) emit(i, v);
+      if (i < nrows) {
+        emit(i, v);
+        if constexpr (PVMMA)
+#pragma unroll
+          for (int g = 0; g < G; ++g) xm[g] = fmaxf(xm[g], sA[g * chunk + i]);
+      }
+    }
+    if constexpr (PVMMA) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        xm[g] = warp_max(xm[g]);
+        if (lane == 0) sWst[warp * G + g] = xm[g];
+      }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tbase, ncols);
+    if (!PVMMA && warp == 0) tmem_dealloc(tbase, tcols);
   } else
   {
     const int sub = lane & 7, tk = lane >> 3;
@@ -808,8 +848,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
       if (sub == 0 && i < nrows) emit(i, tot);
     }
   }
-  // each warp's statistics partial to every CTA (the arrival at barrier A follows in the
-  // attention partials, which run while the exchange completes)
+  // each warp's statistics partial into this CTA's block of the exchange, which goes to every
+  // CTA of the cluster as one bulk copy each once the block is complete
   if (policy) {
     if (snap) {
 #pragma unroll
@@ -819,12 +859,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         el = (em == kNegInf ? 0.f : el * __expf(em - mx)) + (m2 == kNegInf ? 0.f : l2 * __expf(m2 - mx));
         em = mx;
       }
-      if (lane < ncta) {
-        float* dst = lane == rank ? sStat : cluster.map_shared_rank(sStat, lane);
-        dst[2 * (rank * kStepWarps + warp)] = em;
-        dst[2 * (rank * kStepWarps + warp) + 1] = el;
+      if (lane == 0) {
+        sX[rank * gm.xs + chunk + 2 * warp] = em;
+        sX[rank * gm.xs + chunk + 2 * warp + 1] = el;
       }
     }
+    fence_proxy_async_smem();  // the bulk copies read the block through the async proxy
   }
 
   // ---- flash-decode partial of every warp over its rows -------------------------------------
@@ -835,11 +875,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   // V rows landed (this barrier also publishes every warp's logits); the warp whose rows hold
   // the new slot puts the new value in place, each lane its own columns, the ones it reads
   if (!__syncthreads_and(mbar_wait(&bars[1], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
+  if (policy && warp == 1 && lane < ncta && lane != rank)
+    bulk_s2cluster(sX + (size_t)rank * gm.xs, (uint32_t)gm.xs * 4u, &bars[4], (uint32_t)lane);
   constexpr int CW = D / 32;  // V columns per lane
   const int col0 = lane * CW;
-  if (i_new >= 0 && row_warp(i_new) == warp)
+  if constexpr (!PVMMA)
+    if (i_new >= 0 && row_warp(i_new) == warp)
 #pragma unroll
-    for (int c = 0; c < CW; ++c) sV[(size_t)i_new * D + col0 + c] = sVn[col0 + c];
+      for (int c = 0; c < CW; ++c) sV[(size_t)i_new * D + col0 + c] = sVn[col0 + c];
   // the K rows are no longer read: their area holds the warp partials [warp][G][D], the
   // probabilities of each warp's rows [warp][32][G] and the warps' (max, sum) [warp][G][2]
   float* red = reinterpret_cast<float*>(smem + M.k);
@@ -847,9 +890,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
   float* sWml = sPw + (size_t)kStepWarps * 32 * G;
   float wm[G], wl[G];
   float2 acc[G][CW / 2];
-  // arrive_a: arrive at barrier A after the maxima, so that the release of this thread's
-  // distributed shared memory stores completes while the P.V runs
-  auto warp_partial = [&](bool arrive_a) {
+  auto warp_partial = [&]() {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       wm[g] = kNegInf;
@@ -863,7 +904,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         for (int g = 0; g < G; ++g) wm[g] = fmaxf(wm[g], sA[g * chunk + b + lane]);
 #pragma unroll
     for (int g = 0; g < G; ++g) wm[g] = warp_max(wm[g]);
-    if (arrive_a) cluster_arrive();  // barrier A
     float* pw = sPw + (size_t)warp * 32 * G;
     for (int b = warp * rpw; b < nrows; b += kStepWarps * rpw) {
       const int i = b + lane;
@@ -910,14 +950,98 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 #pragma unroll
     for (int g = 0; g < G; ++g) wl[g] = warp_sum(wl[g]);
   };
-  warp_partial(policy);
+
+  // ---- tensor-core P.V (16-bit, D = 128): the probabilities are the B operand (N8 query-head
+  //      rows x rows of this part, K-major, 128-byte swizzle, in the K area), V^T the MN-major A
+  //      operand straight from the TMA's planes, O^T (D lanes x N8 columns) accumulates in TMEM ---
+  const int kext = PVMMA ? (nrows + 15) & ~15 : 0;  // rows the MMAs reduce over, 16 per instruction
+  unsigned char* sPo = smem + M.k;
+  unsigned char* sVb = reinterpret_cast<unsigned char*>(sV);
+  float mg[G];
+  uint32_t pv_phase = 0;
+  // remax: take the maxima again from the logits (after rows left the attention)
+  auto build_pv = [&](bool remax) {
+    if (remax) {
+      float xm[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) xm[g] = kNegInf;
+      for (int i = tid; i < nrows; i += kStepThreads)
+#pragma unroll
+        for (int g = 0; g < G; ++g) xm[g] = fmaxf(xm[g], sA[g * chunk + i]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        xm[g] = warp_max(xm[g]);
+        if (lane == 0) sWst[warp * G + g] = xm[g];
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float m = kNegInf;
+#pragma unroll
+      for (int w = 0; w < kStepWarps; ++w) m = fmaxf(m, sWst[w * G + g]);
+      mg[g] = m;
+    }
+    float ls[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) ls[g] = 0.f;
+    for (int i = tid; i < kext; i += kStepThreads) {
+      const bool att = i < nrows && sInv[i] != -1;
+      const int c = (i & 63) >> 3;
+      unsigned char* prow = sPo + (size_t)(i >> 6) * (N8 * 128) + (i & 7) * 2;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float x = att ? sA[g * chunk + i] : kNegInf;
+        const float pr = x == kNegInf ? 0.f : __expf(x - mg[g]);
+        ls[g] += pr;
+        *reinterpret_cast<T*>(prow + (size_t)g * 128 + ((c ^ (g & 7)) << 4)) = E::from_f(pr);
+      }
+      if (!att)  // a row not attended: its V may hold anything, and the MMA multiplies it by 0
+#pragma unroll
+        for (int pl = 0; pl < PL; ++pl)
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            reinterpret_cast<uint4*>(sVb + (size_t)pl * gm.vrows * 128 + (size_t)i * 128)[q] = make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      ls[g] = warp_sum(ls[g]);
+      if (lane == 0) sWst[kStepWarps * G + warp * G + g] = ls[g];
+    }
+    fence_proxy_async_smem();  // generic writes above are read by the tensor cores
+    __syncthreads();
+    if (tid == kStepThreads - 32 && kext > 0) {  // a thread of the last warp, which ranks the fewest tokens
+      tc_fence_after();
+      constexpr uint32_t idesc = kIdesc | (1u << 15);  // A (V^T) MN-major
+      const uint32_t a0 = smem_u32(sVb), b0 = smem_u32(sPo), lbo = (uint32_t)gm.vrows * 128u;
+      for (int ks = 0; ks < kext / 16; ++ks) {
+        const uint32_t aa = a0 + (uint32_t)ks * 2048u;
+        const uint32_t bb = b0 + (uint32_t)(ks >> 2) * (N8 * 128u) + (uint32_t)(ks & 3) * 32u;
+        umma_f16(tbase + (uint32_t)colO, umma_desc_mn_sw128(aa, lbo), umma_desc_k_sw128(bb), idesc, ks > 0);
+      }
+      umma_commit(&bars[3]);
+    }
+  };
+  if constexpr (PVMMA) {
+    // the new value into its swizzled row, before the MMAs read V
+    if (i_new >= 0 && tid < D) {
+      const int c = (tid & 63) >> 3;
+      *reinterpret_cast<T*>(sVb + (size_t)(tid >> 6) * gm.vrows * 128 + (size_t)i_new * 128 + ((c ^ (i_new & 7)) << 4) +
+                            (tid & 7) * 2) = sVn[tid];
+    }
+    build_pv(false);
+  } else {
+    warp_partial();
+  }
+  float pe[G];      // probabilities of the evicted row, when its term is subtracted
+  int fix_ev = -1;  // that row (tensor-core P.V)
 
   // ---- policy: every CTA holds every head's eviction logits and statistics partials and ranks
   //      the prefix itself, so every CTA makes the same selection -----------------------------
   int n_ev = 0;
   int ev_slot = -1, ev_dst = -1, ev_li = -1;  // the single evicted token, when exactly one leaves
   if (policy) {
-    cluster_wait();  // barrier A
+    if (!mbar_wait(&bars[4], 0)) set_status(st, HC_DEV_TIMEOUT);  // every other CTA's block landed
     float* sC = sRed;  // per head: the softmax max and the reciprocal of the sum
     if (snap) {
       // each head's statistics over its S hot tokens from its P CTAs' warp partials
@@ -926,7 +1050,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         float m = kNegInf, l = 0.f;
         for (int j = lane; j < np; j += 32) {
           const int r2 = warp * P + j / kStepWarps, w = j % kStepWarps;
-          const float m2 = sStat[2 * (r2 * kStepWarps + w)], l2 = sStat[2 * (r2 * kStepWarps + w) + 1];
+          const float* st2 = sX + (size_t)r2 * gm.xs + chunk + 2 * w;
+          const float m2 = st2[0], l2 = st2[1];
           const float mx = fmaxf(m, m2);
           l = (m == kNegInf ? 0.f : l * __expf(m - mx)) + (m2 == kNegInf ? 0.f : l2 * __expf(m2 - mx));
           m = mx;
@@ -951,6 +1076,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
     const int pad = L.pool_kernel > 1 ? L.pool_kernel / 2 : 0;
     const bool pmax = L.pooling == HC_POOL_MAX;
     const float inv = 1.f / sqrtf((float)L.D);
+    // head hh's logit of token u: sX[hh * P * xs + sLoc[u]] (the part and row of u's slot)
+    const int hstride = P * gm.xs;
     auto token_key = [&](int li) {
       const int ua = max(0, li - pad), ub = min(S - 1, li + pad);
       float v = 0.f;
@@ -958,10 +1085,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         // the configured 7-wide max pool: indices clamped into [0, S), repeats leave the max alone
         int uu[7];
 #pragma unroll
-        for (int k = 0; k < 7; ++k) uu[k] = min(max(li - 3 + k, 0), S - 1);
+        for (int k = 0; k < 7; ++k) uu[k] = sLoc[min(max(li - 3 + k, 0), S - 1)];
 #pragma unroll 4
         for (int hh = 0; hh < L.Hk; ++hh) {
-          const float* x = sEv + hh * ecap;
+          const float* x = sX + (size_t)hh * hstride;
           float mx = x[uu[0]];
 #pragma unroll
           for (int k = 1; k < 7; ++k) mx = fmaxf(mx, x[uu[k]]);
@@ -970,22 +1097,21 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         return fkey(v / (float)L.Hk);
       }
       for (int hh = 0; hh < L.Hk; ++hh) {
-        const float* x = sEv + hh * ecap;
+        const float* x = sX + (size_t)hh * hstride;
         float t;
         if (snap) {
           const float mh = sC[2 * hh], rl = sC[2 * hh + 1];
           if (pad == 0 || pmax) {
             float mx = kNegInf;
-#pragma unroll 8
-            for (int u = ua; u <= ub; ++u) mx = fmaxf(mx, x[u]);
+            for (int u = ua; u <= ub; ++u) mx = fmaxf(mx, x[sLoc[u]]);
             t = __expf(mx * L.scale - mh) * rl;
           } else {
             t = 0.f;
-            for (int u = ua; u <= ub; ++u) t += __expf(x[u] * L.scale - mh) * rl;
+            for (int u = ua; u <= ub; ++u) t += __expf(x[sLoc[u]] * L.scale - mh) * rl;
             t /= (float)L.pool_kernel;
           }
         } else {
-          t = x[li] * inv;
+          t = x[sLoc[li]] * inv;
         }
         v += t;
       }
@@ -1034,11 +1160,34 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         if (li > li_ev) d.hot_ord[li - 1] = ph;
         else if (li == li_ev && n_free - 1 < cap) d.hot_free[n_free - 1] = ph;
       }
-      // the warp whose partial holds the evicted row takes it out again; where that row carried
-      // most of a head's mass (the difference would cancel) the warp recomputes without it
+      // the evicted row leaves the attention partial that holds it: its term is subtracted, or,
+      // where that row carried most of a head's mass (the difference would cancel), the partial
+      // is recomputed without it
       const int i_ev = row_of_slot(ev_slot);
-      if (i_ev >= 0 && row_warp(i_ev) == warp) {
-        float pe[G];
+      if constexpr (PVMMA) {
+        if (i_ev >= 0) {  // the same in every thread of the CTA
+          bool redo = false;
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            float l = 0.f;
+#pragma unroll
+            for (int w = 0; w < kStepWarps; ++w) l += sWst[kStepWarps * G + w * G + g];
+            const float x = sA[g * chunk + i_ev];
+            pe[g] = x == kNegInf ? 0.f : __expf(x - mg[g]);
+            redo |= !(l - pe[g] >= 0.25f * l);
+          }
+          if (redo) {
+            // the first MMAs read the operands until they complete
+            if (!__syncthreads_and(mbar_wait(&bars[3], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
+            if (tid < G) sA[tid * chunk + i_ev] = kNegInf;
+            __syncthreads();
+            build_pv(true);
+            pv_phase = 1;
+          } else {
+            fix_ev = i_ev;
+          }
+        }
+      } else if (i_ev >= 0 && row_warp(i_ev) == warp) {
         bool redo = false;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -1049,7 +1198,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         if (redo) {
           if (lane < G) sA[lane * chunk + i_ev] = kNegInf;
           __syncwarp();
-          warp_partial(false);
+          warp_partial();
         } else {
           float vf[CW];
           unpack_n<DT, CW>(sV + (size_t)i_ev * D + col0, vf);
@@ -1128,63 +1277,120 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
         }
         if (lane == 0) sMisc[4] = nloc;
       }
-      // the evicted rows leave the attention: every warp recomputes its partial
+      // the evicted rows leave the attention: the partials are recomputed
       for (int i = tid; i < nrows; i += kStepThreads) {
         const int li = sInv[i];
         if (li >= 0 && ((sMask[li >> 5] >> (li & 31)) & 1u))
 #pragma unroll
           for (int g = 0; g < G; ++g) sA[g * chunk + i] = kNegInf;
       }
-      __syncthreads();
-      warp_partial(false);
+      if constexpr (PVMMA) {
+        // the first MMAs read the operands until they complete
+        if (kext > 0 && !__syncthreads_and(mbar_wait(&bars[3], 0)) && tid == 0) set_status(st, HC_DEV_TIMEOUT);
+        __syncthreads();
+        build_pv(true);
+        pv_phase = 1;
+      } else {
+        __syncthreads();
+        warp_partial();
+      }
     }
   }
 
-  // ---- warp partials combined per column, each column block sent to the CTA of head h that
+  // ---- the part's partial per column, each column block sent to the CTA of head h that
   //      finalizes it ---------------------------------------------------------------------------
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float* dst = red + ((size_t)warp * G + g) * D + col0;
-    if constexpr (CW % 4 == 0) {
-#pragma unroll
-      for (int c = 0; c < CW / 2; c += 2)
-        reinterpret_cast<float4*>(dst)[c / 2] = make_float4(acc[g][c].x, acc[g][c].y, acc[g][c + 1].x, acc[g][c + 1].y);
-    } else {
-#pragma unroll
-      for (int c = 0; c < CW / 2; ++c) reinterpret_cast<float2*>(dst)[c] = acc[g][c];
-    }
-  }
-  if (lane == 0)
+  const int DB = D / P;
+  if constexpr (PVMMA) {
+    // warps 0-3 read O^T from TMEM (lane = column d, column g = query head), subtract the evicted
+    // row's term where it is taken out here, and send
+    float lg[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      sWml[2 * (warp * G + g)] = wm[g];
-      sWml[2 * (warp * G + g) + 1] = wl[g];
-    }
-  __syncthreads();
-  const int DB = D / P;
-  for (int k = tid; k < G * D; k += kStepThreads) {
-    const int g = k / D, dd = k - g * D;
-    float Mx = kNegInf;
+      float l = 0.f;
 #pragma unroll
-    for (int w = 0; w < kStepWarps; ++w) Mx = fmaxf(Mx, sWml[2 * (w * G + g)]);
-    float v = 0.f, l = 0.f;
-#pragma unroll
-    for (int w = 0; w < kStepWarps; ++w) {
-      const float mw = sWml[2 * (w * G + g)];
-      const float e = mw == kNegInf ? 0.f : __expf(mw - Mx);
-      v = fmaf(red[((size_t)w * G + g) * D + dd], e, v);
-      l = fmaf(sWml[2 * (w * G + g) + 1], e, l);
+      for (int w = 0; w < kStepWarps; ++w) l += sWst[kStepWarps * G + w * G + g];
+      lg[g] = fix_ev >= 0 ? l - pe[g] : l;
     }
-    const int q = dd / DB, col = dd - q * DB;
-    float* dst = q == p ? sO : cluster.map_shared_rank(sO, h * P + q);
-    dst[((size_t)p * G + g) * DB + col] = v;
-    if (col == 0) {
-      float* dml = q == p ? sML : cluster.map_shared_rank(sML, h * P + q);
-      dml[2 * (p * G + g)] = Mx;
-      dml[2 * (p * G + g) + 1] = l;
+    if (warp < 4) {
+      float o[8];
+      if (kext > 0) {
+        if (!mbar_wait(&bars[3], pv_phase)) set_status(st, HC_DEV_TIMEOUT);
+        tc_fence_after();
+        tmem_ld_x8(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)colO, o);
+      } else {
+#pragma unroll
+        for (int g = 0; g < 8; ++g) o[g] = 0.f;
+      }
+      const int dd = warp * 32 + lane;
+      if (fix_ev >= 0) {
+        const int c = (dd & 63) >> 3;
+        const float ve = E::to_f(*reinterpret_cast<const T*>(sVb + (size_t)(dd >> 6) * gm.vrows * 128 +
+                                                             (size_t)fix_ev * 128 + ((c ^ (fix_ev & 7)) << 4) + (dd & 7) * 2));
+#pragma unroll
+        for (int g = 0; g < G; ++g) o[g] = fmaf(-E::round(pe[g]), ve, o[g]);
+      }
+      const int q = dd / DB, col = dd - q * DB;
+      float* dst = q == p ? sO : cluster.map_shared_rank(sO, h * P + q);
+#pragma unroll
+      for (int g = 0; g < G; ++g) dst[((size_t)p * G + g) * DB + col] = o[g];
+      if (col == 0) {
+        float* dml = q == p ? sML : cluster.map_shared_rank(sML, h * P + q);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          dml[2 * (p * G + g)] = mg[g];
+          dml[2 * (p * G + g) + 1] = lg[g];
+        }
+      }
+    }
+    tc_fence_before();
+  } else {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float* dst = red + ((size_t)warp * G + g) * D + col0;
+      if constexpr (CW % 4 == 0) {
+#pragma unroll
+        for (int c = 0; c < CW / 2; c += 2)
+          reinterpret_cast<float4*>(dst)[c / 2] = make_float4(acc[g][c].x, acc[g][c].y, acc[g][c + 1].x, acc[g][c + 1].y);
+      } else {
+#pragma unroll
+        for (int c = 0; c < CW / 2; ++c) reinterpret_cast<float2*>(dst)[c] = acc[g][c];
+      }
+    }
+    if (lane == 0)
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        sWml[2 * (warp * G + g)] = wm[g];
+        sWml[2 * (warp * G + g) + 1] = wl[g];
+      }
+    __syncthreads();
+    for (int k = tid; k < G * D; k += kStepThreads) {
+      const int g = k / D, dd = k - g * D;
+      float Mx = kNegInf;
+#pragma unroll
+      for (int w = 0; w < kStepWarps; ++w) Mx = fmaxf(Mx, sWml[2 * (w * G + g)]);
+      float v = 0.f, l = 0.f;
+#pragma unroll
+      for (int w = 0; w < kStepWarps; ++w) {
+        const float mw = sWml[2 * (w * G + g)];
+        const float e = mw == kNegInf ? 0.f : __expf(mw - Mx);
+        v = fmaf(red[((size_t)w * G + g) * D + dd], e, v);
+        l = fmaf(sWml[2 * (w * G + g) + 1], e, l);
+      }
+      const int q = dd / DB, col = dd - q * DB;
+      float* dst = q == p ? sO : cluster.map_shared_rank(sO, h * P + q);
+      dst[((size_t)p * G + g) * DB + col] = v;
+      if (col == 0) {
+        float* dml = q == p ? sML : cluster.map_shared_rank(sML, h * P + q);
+        dml[2 * (p * G + g)] = Mx;
+        dml[2 * (p * G + g) + 1] = l;
+      }
     }
   }
   cluster.sync();  // last barrier: no distributed shared memory access after this point
+  if (PVMMA && warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, tcols);
+  }
   T* outp = reinterpret_cast<T*>(a.out) + ((size_t)s * L.Hq + (size_t)h * G) * D + (size_t)p * DB;
   for (int k = tid; k < G * DB; k += kStepThreads) {
     const int g = k / DB, col = k - g * DB;
@@ -1258,7 +1464,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepArgs a) {
 int step_parts(int Hk) { return (Hk >= 1 && Hk <= kStepMaxCluster && kStepMaxCluster % Hk == 0) ? kStepMaxCluster / Hk : 0; }
 
 static StepGeom layer_geom(const hc_layer& L, int use_held) {
-  return step_geom(L.Hk, L.max_cap, L.max_r, use_held, L.dtype != HC_F32);
+  return step_geom(L.Hk, L.max_cap, L.max_r, use_held, L.dtype != HC_F32, L.dtype != HC_F32 && L.D == 128);
 }
 
 size_t step_smem_bytes(const hc_layer& L, int use_held) {

@@ -110,10 +110,12 @@ typedef struct hc_layer {
   int32_t max_ccap;        /* max cold ring capacity over sequences */
   float scale;             /* attention scale, 1/sqrt(D) */
   float rope_scaling;      /* rotary attention_scaling */
-  const void* kmaps;       /* optional device array of two 128-byte TMA tensor maps written by
-                              hc_encode_kmap (f16/bf16): [0] the hot K slab of all sequences as
-                              rows of D elements, box 64 x 64 rows; [1] the held K rows, box
-                              64 x 8 rows. hc_step needs them for 16-bit dtypes. */
+  const void* kmaps;       /* optional device array of four 128-byte TMA tensor maps written by
+                              hc_encode_kmap (f16/bf16), each over all sequences as rows of D
+                              elements: [0] the hot K slab, box 64 x 64 rows; [1] the held K
+                              rows, box 64 x 8 rows; [2] the hot V slab, box 64 x 16 rows; [3]
+                              the held V rows, box 64 x 8 rows. hc_step needs them for 16-bit
+                              dtypes. */
 } hc_layer;                /* 104 bytes */
 
 /* Library and error reporting. */
