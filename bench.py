@@ -72,6 +72,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", default="decode", choices=["decode", "ragged", "cold-shard", "prefill", "model"])
     p.add_argument("--seqs", type=int, default=64)
+    p.add_argument("--retrieval", default="async", choices=["sync", "async"],
+                   help="decode-step searches in the decode stream before the step (sync), or on side "
+                        "streams after it, attended from the next step (async: KVController(async_retrieval=True))")
     p.add_argument("--no-partitioned", action="store_true",
                    help="skip the ragged-batch and sharded-cold-store sub-results of the default line")
     return p.parse_args()
@@ -82,7 +85,8 @@ def config(a):
     ratio = 0.0 if a.policy == "snapkv" else max(0.05, 0.75 - recent / (a.budget or 512))  # run_baselines.py:86-87
     return dict(Hq=32, Hk=8, D=128, theta=500000.0, layers=a.layers, prompt=a.prompt or 8192, budget=a.budget or 512,
                 policy=a.policy, recent=recent, topk_ratio=ratio, pool_kernel=7, ccap=32768, faiss_dim=128,
-                window_size=16, query_pool_size=4, lookahead_k=64, hold=True, dtype="float16")
+                window_size=16, query_pool_size=4, lookahead_k=64, hold=True, dtype="float16",
+                async_retrieval=getattr(a, "retrieval", "async") == "async")
 
 
 def workload_config(c, extra=None):
@@ -90,6 +94,8 @@ def workload_config(c, extra=None):
          "layers": c["layers"], "prompt_tokens": c["prompt"], "budget": c["budget"], "policy": c["policy"],
          "recent": c["recent"], "lookahead_k": c["lookahead_k"], "retrieval_every": c["window_size"],
          "hold_retrieved": c["hold"], "cold_ring": c["ccap"], "batch": 1, "heads": "32q/8kv", "head_dim": 128,
+         "retrieval": ("async: side streams after the step, attended from the next step" if c.get("async_retrieval")
+                       else "sync: in the decode stream before the step, attended at once"),
          "l2": "flushed (256 MiB write) before every timed step"}
     if extra:
         d.update(extra)
@@ -276,7 +282,7 @@ class Workload:
                                  window_size=c["window_size"], query_pool_size=c["query_pool_size"],
                                  lookahead_k=c["lookahead_k"], hold_retrieved=c["hold"],
                                  retrieve_after_prefill=False, policy=c["policy"], pool_kernel=c["pool_kernel"],
-                                 profile_overlap=False)
+                                 profile_overlap=False, async_retrieval=c.get("async_retrieval", False))
         self.ctrl.set_rotary(self.rot.inv_freq, self.rot.attention_scaling)
         pos = torch.arange(T, device=device)[None]
         cos, sin = self.rot(torch.empty(1, dtype=dt, device=device), pos)
@@ -304,6 +310,9 @@ class Workload:
         need = max(size("hc_attend_scratch_bytes", byref(a0.L)), size("hc_retrieve_scratch_bytes", byref(a0.L)),
                    size("hc_compress_scratch_bytes", byref(a0.L), a0.max_cap, 1))
         self.ctrl.workspace.get(need)
+        if self.ctrl.async_retrieval:
+            for li in range(min(L, 4)):
+                self.ctrl._side_stream(li, device)[1].get(need)
         torch.cuda.synchronize(device)
 
     def step(self, i):

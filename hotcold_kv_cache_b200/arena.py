@@ -509,10 +509,11 @@ class LayerArena:
         self._cold_push(ev)
         return ev
 
-    def retrieve(self, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0, qvec=None):
-        """Search + gather + re-RoPE into the held segment."""
+    def retrieve(self, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0, qvec=None, ws=None):
+        """Search + gather + re-RoPE into the held segment. `ws`: the Workspace of the stream it
+        runs on, when that is not the arena's (a side stream)."""
         nbytes = size("hc_retrieve_scratch_bytes", byref(self.L))
-        ws = self.ws.get(nbytes)
+        ws = (ws or self.ws).get(nbytes)
         qd = (0, 0, 0)
         P = 0
         if q_dense is not None:

@@ -11,8 +11,12 @@ Schedule. A retrieval that fires at a decode step (every `window_size` forward
 calls, controller.py:314-342) is attended at that same step; the prompt-end
 retrieval (patch.py:231-233) is attended at decode step 1. The reference's
 asynchronous thread makes that step nondeterministic; this is the
-deterministic order its synchronous path would give. Nothing here blocks the
-host: every op is an asynchronous launch on the current stream.
+deterministic order its synchronous path would give. With async_retrieval the
+search instead runs on a side stream after the step's compression, overlapping
+the next layers, and is attended from the layer's next step (another order the
+thread can give, as deterministic). Nothing here blocks the host: every op is an
+asynchronous launch on the current stream (or, for those searches, a side
+stream joined by events).
 """
 
 from __future__ import annotations
@@ -96,6 +100,7 @@ class KVController:
         pooling: str = "maxpool",
         overflow_nan: bool = True,
         cold_payload: str = "device",
+        async_retrieval: bool = False,
     ):
         """Reference arguments (controller.py:15-34) plus:
         policy: "hotcold" (cache.py:37-128) or "snapkv" (SnapKV score, scoring.py:50-132,
@@ -104,7 +109,12 @@ class KVController:
         overflow_nan: reproduce the reference kernel's NaN on fp32 exp overflow;
         cold_payload: "device" (HBM) or "host": the cold rings' pre-RoPE keys and values in
             page-locked host RAM that the kernels read and write directly, the reference's CPU
-            cold tier (docs/design.md:59-64) for stores larger than HBM; the index stays in HBM."""
+            cold tier (docs/design.md:59-64) for stores larger than HBM; the index stays in HBM;
+        async_retrieval: a decode-step search runs on a side stream after that step's
+            compression, while the following layers decode, and is attended from the layer's
+            next step (the reference's worker thread, controller.py:314-342, in one of its
+            orders); False searches before the step and attends the hits at once. Searches
+            through a sharded cold index (cold_search) stay on the decode stream."""
         if policy not in ("hotcold", "snapkv"):
             raise ValueError(f"unknown policy {policy!r}")
         if pooling not in ("maxpool", "avgpool"):
@@ -128,6 +138,9 @@ class KVController:
         if cold_payload not in ("device", "host"):
             raise ValueError(f"cold_payload must be 'device' or 'host', not {cold_payload!r}")
         self.cold_payload = cold_payload
+        self.async_retrieval = bool(async_retrieval)
+        self._pending: List[Optional[torch.cuda.Event]] = []  # per layer: its search on a side stream
+        self._side = None  # [(stream, workspace)] of the side streams, made on first use
 
         self._inited = False
         self.B = self.Hk = self.D = self.n_layers = None
@@ -188,6 +201,7 @@ class KVController:
         self._retrieval_ready_cpu = [None] * L
         self._tails = [dict() for _ in range(L)]
         self._seen = [0] * L  # tokens each layer has processed (prompt + decode steps)
+        self._pending = [None] * L
         self.workspace = Workspace(device)
         self._inited = True
 
@@ -342,14 +356,52 @@ class KVController:
                 n_pool += 1
         return n_pool, (self._prompt_qsum[li] if extra_n else None), extra_n
 
-    def _retrieve(self, li: int, **kw):
+    def _retrieve(self, li: int, side: bool = False, **kw):
+        a = self.arenas[li]
         if self.cold_search is not None:
-            self.arenas[li].retrieve_sharded(self.cold_search, **kw)
+            a.retrieve_sharded(self.cold_search, **kw)
+        elif side:
+            # on a side stream, after everything this stream has launched; the layer's next
+            # step waits for it (_wait_search)
+            stream, ws = self._side_stream(li, a.device)
+            fork = torch.cuda.Event()
+            fork.record(torch.cuda.current_stream(a.device))
+            stream.wait_event(fork)
+            with torch.cuda.stream(stream):
+                a.retrieve(ws=ws, **kw)
+            done = torch.cuda.Event()
+            done.record(stream)
+            self._pending[li] = done
         else:
-            self.arenas[li].retrieve(**kw)
+            a.retrieve(**kw)
         self.dbg["retrieval_ready_cpu"] += 1   # some sequence has a non-empty ring: hits are valid
         self.dbg["prefetch_launched"] += 1
         self._staged[li] = True
+
+    def _side_stream(self, li: int, device):
+        """(stream, workspace) for layer li's searches in async_retrieval mode: four side
+        streams taken round robin over the layers, so that searches of different layers run at
+        the same time, each with its own scratch."""
+        if self._side is None:
+            self._side = [(torch.cuda.Stream(device=device), Workspace(device)) for _ in range(4)]
+        return self._side[li % len(self._side)]
+
+    def _wait_search(self, li: int):
+        """The current stream waits for the search layer li launched at its previous step."""
+        ev = self._pending[li] if self._pending else None
+        if ev is not None:
+            a = self.arenas[li]
+            torch.cuda.current_stream(a.device).wait_event(ev)
+            a._dirty = True  # its held segment was written on another stream: no early reads
+            self._pending[li] = None
+
+    def join_searches(self):
+        """Make the current stream wait for every search still running on a side stream. The
+        last layer's decode_layer does this every step, so a step captured as a CUDA graph
+        rejoins its side streams; call it before reading a layer's held segment on the host
+        between layers."""
+        for li in range(len(self._pending)):
+            self._wait_search(li)
 
     def launch_retrieval_now(self, layer_idx: int, q_pre: torch.Tensor):
         """controller.py:295-312: one retrieval from the given pre-RoPE queries
@@ -364,9 +416,10 @@ class KVController:
         self.dbg["retrieval_launched"] += 1
         self.dbg["retrieval_launched_prefill"] += 1
 
-    def maybe_launch_async_retrieval(self, layer_idx: int):
+    def maybe_launch_async_retrieval(self, layer_idx: int, deferred: bool = False):
         """controller.py:314-342: count the forward call; every window_size calls search
-        the cold store with the pooled queries."""
+        the cold store with the pooled queries. `deferred`: called after the step's attention
+        in async_retrieval mode, the search runs on a side stream."""
         if self.lookahead_k <= 0:
             return
         li = int(layer_idx)
@@ -381,7 +434,7 @@ class KVController:
         n_pool, extra, extra_n = self._pool(li)
         if n_pool == 0 and extra_n == 0:
             return
-        self._retrieve(li, n_pool=n_pool, extra_sum=extra, extra_n=extra_n)
+        self._retrieve(li, side=deferred, n_pool=n_pool, extra_sum=extra, extra_n=extra_n)
         self.dbg["retrieval_launched"] += 1
 
     def maybe_prefetch_to_gpu(self, layer_idx: int, device=None, dtype=None):
@@ -546,19 +599,22 @@ class KVController:
         (a contiguous tensor of that shape and the model dtype), else the layer's own buffer."""
         li = int(layer_idx)
         a = self.arena(li, q_pre.shape[1], k_pre.dtype, k_pre.device)
+        self._wait_search(li)
         self._seen[li] += 1
         hook = self.op_hook or (lambda name, phase: None)
         if self.fused_step:
             res = self._decode_fused(li, a, hook, q_pre, k_pre, v, cos, sin, pos, out)
             if res is not None:
+                self._end_of_layer(li)
                 return res
         hook("append", "begin")
         q_post = a.append(q_pre, k_pre, v, cos, sin, pos)
         hook("append", "end")
         self._qpool[li].append(1)
-        hook("retrieve", "begin")
-        self.maybe_launch_async_retrieval(li)
-        hook("retrieve", "end")
+        if not self.async_retrieval:
+            hook("retrieve", "begin")
+            self.maybe_launch_async_retrieval(li)
+            hook("retrieve", "end")
         hook("compress", "begin")
         ev = a.compress_decode(q_post.view(a.n_seq, a.Hq, 1, a.D))
         self._count_eviction(ev)
@@ -569,14 +625,22 @@ class KVController:
         hook("attend", "begin")
         res = a.attend(q_post, pos, use_held, self.overflow_nan, out=out)
         hook("attend", "end")
+        if self.async_retrieval:
+            self.maybe_launch_async_retrieval(li, deferred=True)
+        self._end_of_layer(li)
         return res
+
+    def _end_of_layer(self, li: int):
+        """After the model's last layer: the decode stream rejoins the side streams' searches."""
+        if self.async_retrieval and li == self.n_layers - 1:
+            self.join_searches()
 
     def _decode_fused(self, li, a, hook, q_pre, k_pre, v, cos, sin, pos, out=None):
         """The decode step as one hc_step launch, preceded on search steps by one fused
         retrieval launch whose pooled query takes this step's q_pre as the newest entry (its
         query-pool push happens inside hc_step). Returns None, with nothing launched and no
         counter changed, when the fused kernels do not fit; the caller then runs the split ops."""
-        fires = self._retrieval_fires(li)
+        fires = not self.async_retrieval and self._retrieval_fires(li)
         if fires and self.cold_search is not None:
             return None  # the sharded search runs with the split ops
         if fires:
@@ -606,7 +670,8 @@ class KVController:
             return None
         self._qpool[li].append(1)
         if not fires:
-            self.maybe_launch_async_retrieval(li)  # counts the call; no search fires here
+            # counts the call; in async_retrieval mode a search that fires runs on a side stream
+            self.maybe_launch_async_retrieval(li, deferred=self.async_retrieval)
         o, ev = res
         self._count_eviction(ev, a.last_ev)
         self._count_injection(a, use_held)
@@ -665,6 +730,7 @@ class KVController:
         The result can go through torch.save. Synchronises."""
         if not self._inited:
             raise RuntimeError("KVController not initialized")
+        self.join_searches()
         return {
             "dims": dict(B=self.B, Hk=self.Hk, D=self.D, n_layers=self.n_layers),
             "seq_budgets": self.seq_budgets, "seq_ccaps": self.seq_ccaps,

@@ -346,13 +346,17 @@ class OracleLayer:
     hot tier of cache.py:37-151 and the cold tier of controller.py:190-442, with
     the retrieval worker run synchronously and its result staged at once, so a
     retrieval launched at step t is attended at step t (the rule the CUDA path
-    implements). Positions of prompt tokens are 0..T-1.
+    implements). With retrieval_lag=1 a decode-step retrieval instead searches the
+    cold store after step t's compression and is attended from step t+1: one of
+    the orders the reference's asynchronous worker (controller.py:314-342) can
+    take, the one the CUDA path's async_retrieval mode implements. Positions of
+    prompt tokens are 0..T-1.
     """
 
     def __init__(self, *, Hq, Hk, D, dtype, inv_freq, attention_scaling=1.0,
                  policy: Policy, cpu_buffer_size=8192, faiss_dim=64, normalize_for_ip=True,
                  window_size=16, query_pool_size=4, lookahead_k=32, hold_retrieved=False,
-                 retrieve_after_prefill=False):
+                 retrieve_after_prefill=False, retrieval_lag=0):
         self.Hq, self.Hk, self.D, self.dt = Hq, Hk, D, dtype
         self.inv_freq = np.asarray(inv_freq, np.float32)
         self.att_scale = float(attention_scaling)
@@ -365,6 +369,9 @@ class OracleLayer:
         self.lookahead_k = int(lookahead_k)
         self.hold = bool(hold_retrieved)
         self.retrieve_after_prefill = bool(retrieve_after_prefill)
+        if retrieval_lag not in (0, 1):
+            raise ValueError("retrieval_lag is 0 or 1")
+        self.retrieval_lag = int(retrieval_lag)
         self.scale = 1.0 / math.sqrt(D)
         self.dbg = {k: 0 for k in DBG_KEYS}
         self.step_count = 0
@@ -557,13 +564,17 @@ class OracleLayer:
         q_post = apply_rope(q_pre, cos, sin, self.dt)
         k_post = apply_rope(k_pre, cos, sin, self.dt)
         self.qwin.append(q_pre)
+        deferred = False
         if self.lookahead_k > 0:
             self.step_count += 1
             if self.step_count % self.window_size == 0:
                 if self.cold_size() == 0:
                     self.dbg["retrieval_skipped_no_cold"] += 1
                 elif len(self.qwin):
-                    self._retrieve(self._pooled_rows(), step=step)
+                    if self.retrieval_lag:
+                        deferred = True  # searched after this step's compression, attended next step
+                    else:
+                        self._retrieve(self._pooled_rows(), step=step)
                     self.dbg["retrieval_launched"] += 1
         # hot update (append then compress)
         self.K = np.concatenate([self.K, k_post], axis=2)
@@ -599,7 +610,10 @@ class OracleLayer:
             Vc = np.concatenate([mem[1], Vc], axis=2)
             mask = np.concatenate([keep_mem, mask], axis=1)
         self._next_pos = cur + 1
-        return decode_attention(q_post[:, :, 0], Kc, Vc, mask, self.scale, self.dt)
+        out = decode_attention(q_post[:, :, 0], Kc, Vc, mask, self.scale, self.dt)
+        if deferred:
+            self._retrieve(self._pooled_rows(), step=step + 1)
+        return out
 
     def start_decode(self, T: int):
         self._next_pos = T

@@ -30,7 +30,8 @@ def oracle_kwargs(case):
                               topk_ratio=c["topk_ratio"], pool_kernel=c["pool_kernel"]),
                 cpu_buffer_size=c["ccap"], faiss_dim=c["faiss_dim"], normalize_for_ip=True,
                 window_size=c["window_size"], query_pool_size=c["pool"], lookahead_k=c["R"],
-                hold_retrieved=c["hold"], retrieve_after_prefill=c["rap"])
+                hold_retrieved=c["hold"], retrieve_after_prefill=c["rap"],
+                retrieval_lag=1 if c.get("async") else 0)
 
 
 def inputs(case):

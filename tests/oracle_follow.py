@@ -67,6 +67,8 @@ class FollowCuda:
             # attended: nothing of it is observable in either run
             return ids
         st = max(step, 1)
+        if st not in self.res["held"] and st > len(self.res["hot"]):
+            return ids  # a search attended only after the last compared step (one-step lag)
         assert st in self.res["held"], f"the CUDA run injected nothing at step {st}"
         pos, valid, _ = self.res["held"][st]
         cpos = pos[b][valid[b]]

@@ -115,6 +115,32 @@ def test_bench_configuration_all_steps():
     assert ctrl.device_status() == 0
 
 
+def test_bench_configuration_async_retrieval():
+    """bench.py's layer configuration with async_retrieval: each decode-step search runs on a
+    side stream after the step's compression and is attended from the next step. Two layers,
+    63 steps, every step against the oracle run with the same one-step lag (searches at steps
+    15, 31, 47, 63 attended at 16, 32, 48; the last falls after the run)."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import run_cuda_layers
+    c = dict(bench_case(), **{"async": True})
+    ins = [synth.layer_inputs(c["seed"] + li, 1, 32, 8, 128, c["T"], c["steps"], "float16") for li in range(2)]
+    res = run_cuda_layers(c, ins, c["steps"], fused=True)
+    ctrl = res[0]["ctrl"]
+    n_search = (c["steps"] + 1) // c["window_size"]
+    for li in range(2):
+        a = ctrl.arenas[li]
+        per_search = 1 if a._retr_fused() else 4
+        assert a.launches == c["steps"] + n_search * per_search, "the fused step did not run"
+        assert sorted(res[li]["launched"]) == [15, 31, 47, 63]
+    for li in range(2):
+        layer, o_outs, o_hot, fc = _oracle(c, ins[li], res[li])
+        assert assert_same_run(res[li], layer, o_outs, o_hot, "float16", c["steps"], f"layer {li}") == 63
+        assert [e["step"] for e in layer.events] == [16, 32, 48]
+        for k, v in layer.dbg.items():
+            assert ctrl.dbg[k] == 2 * v, (k, ctrl.dbg[k], v)
+    assert ctrl.device_status() == 0
+
+
 def test_back_to_back_steps_of_one_layer():
     """One layer's decode steps launched back to back, nothing read in between: each fused step
     may start while the previous one (same layer) still runs, so it must not read that layer's
