@@ -684,7 +684,8 @@ def run_cold_shard(a, rank, world):
     rot = _rotary(Hq, Hk, D, 500000.0, dev)
     ctrl = KVController(max_capacity_prompt=budget, topk_ratio=0.0, recent_size=32, cpu_buffer_size=T + 1024,
                         faiss_dim=128, window_size=1, query_pool_size=8, lookahead_k=R, hold_retrieved=True,
-                        retrieve_after_prefill=False, policy="snapkv", pool_kernel=7, profile_overlap=False)
+                        retrieve_after_prefill=False, policy="snapkv", pool_kernel=7, profile_overlap=False,
+                        async_retrieval=getattr(a, "retrieval", "async") == "async")
     ctrl.set_rotary(rot.inv_freq, rot.attention_scaling)
     ctrl.cold_search = ShardedColdSearch()
     g = torch.Generator(device=dev).manual_seed(a.seed)  # the same draws on every rank: replicas
@@ -728,6 +729,8 @@ def run_cold_shard(a, rank, world):
                        "index_rows_scanned_per_rank": -(-n_cold // world),
                        "parallelism": f"cold index by token range over {world} ranks, NCCL all-gather of "
                                       f"{world}x{R} candidates, decode replicated",
+                       "retrieval": ("async: side streams after the step, attended from the next step"
+                                     if ctrl.async_retrieval else "sync: before the step, attended at once"),
                        "l2": "flushed before every timed step"},
             "gpu_launches": int(launches), "ops_us_per_layer_step": ops}
 

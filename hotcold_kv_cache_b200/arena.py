@@ -509,11 +509,13 @@ class LayerArena:
         self._cold_push(ev)
         return ev
 
-    def retrieve(self, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0, qvec=None, ws=None):
-        """Search + gather + re-RoPE into the held segment. `ws`: the Workspace of the stream it
-        runs on, when that is not the arena's (a side stream)."""
+    def retrieve(self, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0, qvec=None, ws=None,
+                 stream=None):
+        """Search + gather + re-RoPE into the held segment. `stream` (a torch.cuda.Stream) and its
+        Workspace `ws`: where it runs when that is not the current stream (a side stream)."""
         nbytes = size("hc_retrieve_scratch_bytes", byref(self.L))
         ws = (ws or self.ws).get(nbytes)
+        sh = stream.cuda_stream if stream is not None else self._stream()
         qd = (0, 0, 0)
         P = 0
         if q_dense is not None:
@@ -521,19 +523,20 @@ class LayerArena:
             P = q_dense.shape[2]
         mc = int(self.cold_count.max())
         call("hc_retrieve_ex", byref(self.L), ptr(q_dense), qd[0], qd[1], qd[2], P, int(n_pool), ptr(extra_sum),
-             int(extra_n), ptr(qvec), ptr(ws), ws.numel(), mc, self._stream())
-        self._launched("retrieve")
+             int(extra_n), ptr(qvec), ptr(ws), ws.numel(), mc, sh)
+        self._launched("retrieve", sh)
         self.launches += 1 if self._retr_fused() else (3 if qvec is not None else 4)
 
     def retrieve_sharded(self, searcher, q_dense=None, n_pool: int = 0, extra_sum=None, extra_n: int = 0,
-                         qvec=None):
+                         qvec=None, ws=None):
         """hc_retrieve with the scan divided by token range over the ranks of `searcher` (a
         shard.ShardedColdSearch): pooled query (hc_retrieve_query), this rank's range of every
         sequence's cold entries scored and cut to its top R (hc_cold_topk), the all-gather and
         merge to the global top R, then the same splice on every rank (hc_splice_hits). A
         token range is a range of ages (0 = the oldest live entry); on a ring that has wrapped
         it covers at most two runs of contiguous slots (shard.age_runs), searched separately
-        and merged on this rank before the exchange."""
+        and merged on this rank before the exchange. `ws`: the Workspace of the stream it runs on,
+        when that is not the arena's (a side stream)."""
         if qvec is None:
             qvec = torch.empty((self.n_seq, self.F), dtype=torch.float32, device=self.device)
             qd, P = (0, 0, 0), 0
@@ -551,7 +554,7 @@ class LayerArena:
             runs.append([(self.cold_vec[s, s0:s0 + cnt], age0)
                          for s0, cnt, age0 in age_runs(int(heads[s]), self.ccaps[s], lo, hi)])
             n.append(c)
-        searcher.ws = self.ws
+        searcher.ws = ws or self.ws
         k = max(self.r_max, 1)
         ids = searcher.search(runs, n, qvec, k)
         call("hc_splice_hits", byref(self.L), ptr(ids), k, self._stream())

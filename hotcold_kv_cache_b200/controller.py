@@ -113,8 +113,7 @@ class KVController:
         async_retrieval: a decode-step search runs on a side stream after that step's
             compression, while the following layers decode, and is attended from the layer's
             next step (the reference's worker thread, controller.py:314-342, in one of its
-            orders); False searches before the step and attends the hits at once. Searches
-            through a sharded cold index (cold_search) stay on the decode stream."""
+            orders); False searches before the step and attends the hits at once."""
         if policy not in ("hotcold", "snapkv"):
             raise ValueError(f"unknown policy {policy!r}")
         if pooling not in ("maxpool", "avgpool"):
@@ -141,6 +140,8 @@ class KVController:
         self.async_retrieval = bool(async_retrieval)
         self._pending: List[Optional[torch.cuda.Event]] = []  # per layer: its search on a side stream
         self._side = None  # [(stream, workspace)] of the side streams, made on first use
+        self._events = None  # per layer: (fork, done) events of its searches on a side stream
+        self._n_pending = 0
 
         self._inited = False
         self.B = self.Hk = self.D = self.n_layers = None
@@ -202,6 +203,8 @@ class KVController:
         self._tails = [dict() for _ in range(L)]
         self._seen = [0] * L  # tokens each layer has processed (prompt + decode steps)
         self._pending = [None] * L
+        self._n_pending = 0
+        self._side = self._events = None
         self.workspace = Workspace(device)
         self._inited = True
 
@@ -358,20 +361,24 @@ class KVController:
 
     def _retrieve(self, li: int, side: bool = False, **kw):
         a = self.arenas[li]
-        if self.cold_search is not None:
-            a.retrieve_sharded(self.cold_search, **kw)
-        elif side:
+        if side:
             # on a side stream, after everything this stream has launched; the layer's next
-            # step waits for it (_wait_search)
+            # step waits for it (_wait_search). A sharded search's collective runs there too:
+            # every rank launches its layers, hence their searches, in the same order
             stream, ws = self._side_stream(li, a.device)
-            fork = torch.cuda.Event()
+            fork, done = self._events[li]
             fork.record(torch.cuda.current_stream(a.device))
             stream.wait_event(fork)
-            with torch.cuda.stream(stream):
-                a.retrieve(ws=ws, **kw)
-            done = torch.cuda.Event()
+            if self.cold_search is not None:
+                with torch.cuda.stream(stream):
+                    a.retrieve_sharded(self.cold_search, ws=ws, **kw)
+            else:
+                a.retrieve(ws=ws, stream=stream, **kw)
             done.record(stream)
             self._pending[li] = done
+            self._n_pending += 1
+        elif self.cold_search is not None:
+            a.retrieve_sharded(self.cold_search, **kw)
         else:
             a.retrieve(**kw)
         self.dbg["retrieval_ready_cpu"] += 1   # some sequence has a non-empty ring: hits are valid
@@ -384,24 +391,28 @@ class KVController:
         the same time, each with its own scratch."""
         if self._side is None:
             self._side = [(torch.cuda.Stream(device=device), Workspace(device)) for _ in range(4)]
+            # per layer, reused: each layer's next search comes after its last one was waited for
+            self._events = [(torch.cuda.Event(), torch.cuda.Event()) for _ in range(self.n_layers)]
         return self._side[li % len(self._side)]
 
     def _wait_search(self, li: int):
         """The current stream waits for the search layer li launched at its previous step."""
-        ev = self._pending[li] if self._pending else None
+        ev = self._pending[li] if self._n_pending else None
         if ev is not None:
             a = self.arenas[li]
             torch.cuda.current_stream(a.device).wait_event(ev)
             a._dirty = True  # its held segment was written on another stream: no early reads
             self._pending[li] = None
+            self._n_pending -= 1
 
     def join_searches(self):
         """Make the current stream wait for every search still running on a side stream. The
         last layer's decode_layer does this every step, so a step captured as a CUDA graph
         rejoins its side streams; call it before reading a layer's held segment on the host
         between layers."""
-        for li in range(len(self._pending)):
-            self._wait_search(li)
+        if self._n_pending:
+            for li in range(len(self._pending)):
+                self._wait_search(li)
 
     def launch_retrieval_now(self, layer_idx: int, q_pre: torch.Tensor):
         """controller.py:295-312: one retrieval from the given pre-RoPE queries

@@ -161,3 +161,33 @@ def test_sharded_retrieval_on_wrapped_ring(dtype):
         assert np.array_equal(single["outs"][i], sharded["outs"][i]), i
     assert np.array_equal(a.cold_head(), a.device_state()[:, 2])
     assert sharded["ctrl"].device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", ["float16", "float32"])
+def test_async_sharded_retrieval_vs_oracle(dtype):
+    """async_retrieval with the sharded search (3 emulated ranks) on a ring that wraps, a search
+    every 3 steps on a side stream attended from the next step: the same held segments, hot
+    sets and outputs as the async run with the single-device search, and that run step by step
+    against the oracle with the one-step lag."""
+    from hotcold_kv_cache_b200 import synth
+    from cuda_runner import run_cuda_layer
+    c = dict(B=2, Hq=8, Hk=2, D=128, T=300, steps=40, dtype=dtype, policy="snapkv", cap=64, recent=16,
+             topk_ratio=0.0, pool_kernel=7, ccap=250, faiss_dim=128, window_size=3, pool=4, R=16,
+             hold=True, rap=True, theta=500000.0, seed=4712, **{"async": True})
+    inp = synth.layer_inputs(c["seed"], 2, 8, 2, 128, c["T"], c["steps"], dtype)
+    single = run_cuda_layer(c, inp, c["steps"], fused=False)
+    sharded = run_cuda_layer(c, inp, c["steps"], fused=False,
+                             searcher=lambda ctrl: _EmulatedRanks(3, lambda: ctrl.arenas[0]))
+    a = sharded["ctrl"].arenas[0]
+    assert (a.cold_pushed > a.ccaps[0]).all(), "the ring did not wrap"
+    assert sorted(single["held"]) == sorted(sharded["held"])
+    for st in single["held"]:
+        for x, y in zip(single["held"][st], sharded["held"][st]):
+            assert np.array_equal(x, y), st
+    for i in range(c["steps"]):
+        assert np.array_equal(single["hot"][i], sharded["hot"][i]), i
+        assert np.array_equal(single["outs"][i], sharded["outs"][i]), i
+    layer, o_outs, o_hot, _ = run_following(O, inp, c["steps"], single, **oracle_kwargs(c))
+    assert assert_same_run(single, layer, o_outs, o_hot, dtype, c["steps"]) == c["steps"]
+    assert [e["step"] for e in layer.events][:3] == [1, 3, 6]
+    assert sharded["ctrl"].device_status() == 0 and single["ctrl"].device_status() == 0
