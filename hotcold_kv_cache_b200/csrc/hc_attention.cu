@@ -446,8 +446,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
     for (int b4 = warp * 4; b4 < nt; b4 += 16) {
       const int t = b4 + tk;
       float acc[G];
+      float2 acc2[G];  // packed fp32 FMAs over element pairs, the pair added at the end
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = 0.f;
+      for (int g = 0; g < G; ++g) acc2[g] = make_float2(0.f, 0.f);
       if (t < nt) {
         const T* row = bk + (size_t)t * D;
 #pragma unroll
@@ -458,9 +459,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pipe_kernel(AttnArgs a) {
 #pragma unroll
           for (int g = 0; g < G; ++g)
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) acc[g] = fmaf(qr[g][jj * VEC + e], kf[e], acc[g]);
+            for (int e = 0; e < VEC; e += 2)
+              acc2[g] = __ffma2_rn(make_float2(qr[g][jj * VEC + e], qr[g][jj * VEC + e + 1]),
+                                   make_float2(kf[e], kf[e + 1]), acc2[g]);
         }
       }
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = acc2[g].x + acc2[g].y;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 4);
