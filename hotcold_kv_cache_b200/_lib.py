@@ -124,11 +124,18 @@ def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_RAW_STREAM = []  # torch's raw current-stream getter, looked up once (None when absent)
+
+
 def stream_of(device) -> int:
     """The raw handle of the current CUDA stream of `device`."""
     import torch
-    idx = device.index if getattr(device, "index", None) is not None else torch.cuda.current_device()
-    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if not _RAW_STREAM:
+        _RAW_STREAM.append(getattr(torch._C, "_cuda_getCurrentRawStream", None))
+    idx = getattr(device, "index", None)
+    if idx is None:
+        idx = torch.cuda.current_device()
+    raw = _RAW_STREAM[0]
     if raw is not None:
         return raw(idx)
     return torch.cuda.current_stream(device).cuda_stream

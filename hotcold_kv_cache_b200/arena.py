@@ -266,6 +266,8 @@ class LayerArena:
     def _stream(self):
         return _lib.stream_of(self.device)
 
+    _hc_step = None  # the library's hc_step, looked up once
+
     def _launched(self, op: str, stream=None):
         """Record that `op` of this arena was the last launch on the stream."""
         _LAST_OP[stream if stream is not None else self._stream()] = (id(self), op)
@@ -291,8 +293,9 @@ class LayerArena:
 
     def _step_plan(self):
         """Evictions of every sequence when each holds one more token than now (the host
-        mirror of the fused step's compression), cached by the hot lengths: (ev, total,
-        total capped by the cold capacities)."""
+        mirror of the fused step's compression), cached by the hot lengths (the cache is reset
+        when the capacities change): (ev, total, total capped by the cold capacities, whether
+        every sequence has a free slot for the new token, the hot lengths after the step)."""
         key = self.n_hot.tobytes()
         e = self._plan_cache.get(key)
         if e is None:
@@ -301,7 +304,8 @@ class LayerArena:
                 p = self.plan(s, int(self.n_hot[s]) + 1)
                 if p is not None:
                     ev[s] = p[0] - p[1]
-            e = (ev, int(ev.sum()), int(np.minimum(ev, np.asarray(self.ccaps)).sum()))
+            fits = not bool((self.n_hot >= self._caps_np).any())
+            e = (ev, int(ev.sum()), int(np.minimum(ev, np.asarray(self.ccaps)).sum()), fits, self.n_hot + 1 - ev)
             if len(self._plan_cache) < 4096:
                 self._plan_cache[key] = e
         return e
@@ -438,7 +442,8 @@ class LayerArena:
         in one launch (hc_step). Returns (output (n_seq,Hq,D), evicted counts), or None when
         the fused kernel does not fit this layer (nothing launched; use append/compress/attend).
         `out`, when given, is a contiguous (n_seq,Hq,D) tensor of the layer dtype to write."""
-        if (self.n_hot >= self._caps_np).any() or not self.step_supported(use_held):
+        plan = self._step_plan()
+        if not plan[3] or not self.step_supported(use_held):
             return None
         q, qss = self._fast_rows(q_pre, self.Hq)
         k, kss = self._fast_rows(k_pre, self.Hk)
@@ -452,9 +457,11 @@ class LayerArena:
             sin = sin.reshape(self.n_seq, self.D).contiguous()
         o = self.out if out is None else out
         stream = self._stream()
-        rc = _lib.load().hc_step(self._Lref, q.data_ptr(), qss, k.data_ptr(), vv.data_ptr(), kss, ptr(cos), ptr(sin),
-                                 pos.data_ptr(), 1 if use_held else 0, o.data_ptr(), 1 if overflow_nan else 0,
-                                 self._early_bits(stream), stream)
+        fn = self._hc_step
+        if fn is None:
+            fn = self._hc_step = _lib.load().hc_step
+        rc = fn(self._Lref, q.data_ptr(), qss, k.data_ptr(), vv.data_ptr(), kss, ptr(cos), ptr(sin), pos.data_ptr(),
+                1 if use_held else 0, o.data_ptr(), 1 if overflow_nan else 0, self._early_bits(stream), stream)
         if rc == 3:  # HC_ERR_UNSUPPORTED: nothing was launched
             self._step_ok[bool(use_held)] = False
             return None
@@ -463,14 +470,12 @@ class LayerArena:
         self._launched("step", stream)
         self._dirty = False
         self.launches += 1
-        ev, tot, capped = self._step_plan()
+        ev, tot, capped, _, n_after = plan
         self.last_ev = (tot, capped)
+        self.n_hot[:] = n_after
         if tot:
-            self.n_hot += 1 - ev
             self.cold_pushed += ev
             np.minimum(self.cold_count + ev, self._ccaps_arr(), out=self.cold_count)
-        else:
-            self.n_hot += 1
         return o, ev
 
     def append_rotated(self, k_post, k_pre, v, pos):

@@ -42,6 +42,10 @@ DBG_KEYS = (
 )
 
 
+def _no_hook(name, phase):
+    return None
+
+
 class _RingView:
     """Read-only view of one cold ring in age order (the reference's cpu_*_ring deques)."""
 
@@ -612,7 +616,7 @@ class KVController:
         a = self.arena(li, q_pre.shape[1], k_pre.dtype, k_pre.device)
         self._wait_search(li)
         self._seen[li] += 1
-        hook = self.op_hook or (lambda name, phase: None)
+        hook = self.op_hook or _no_hook
         if self.fused_step:
             res = self._decode_fused(li, a, hook, q_pre, k_pre, v, cos, sin, pos, out)
             if res is not None:
