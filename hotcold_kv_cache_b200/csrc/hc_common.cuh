@@ -217,6 +217,14 @@ __device__ __forceinline__ void bulk_s2cluster(void* buf, uint32_t bytes, uint64
                "r"(smem_u32(buf)), "r"(bytes), "r"(rbar)
                : "memory");
 }
+// 32-bit load from the same-offset shared memory word of cluster CTA `rank`.
+__device__ __forceinline__ int ld_cluster_s32(const int* p, uint32_t rank) {
+  uint32_t addr;
+  int v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(addr) : "r"(smem_u32(p)), "r"(rank));
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

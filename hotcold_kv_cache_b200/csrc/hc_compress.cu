@@ -17,6 +17,10 @@
 //   select_kernel  (one CTA per sequence): exact top-k of the prefix (ties to the lower
 //                  index), order-preserving compaction of the logical order, free-slot
 //                  push, ring plan; small evictions are copied inline.
+//   select_cluster_kernel  (prompts; a cluster of up to 16 CTAs per sequence): the same top-k
+//                  and keep / evict lists, the histograms of the radix passes summed through
+//                  distributed shared memory; up to 16k tokens it also computes the token
+//                  scores (no token_kernel).
 //   evict_kernel   (large evictions / prompt): payload copies into the cold ring with the
 //                  index vector (mean over KV heads of the pre-RoPE key, pad/crop,
 //                  L2-normalise; controller.py:178-182) and, for a prompt, the kept
@@ -1040,6 +1044,224 @@ __global__ void __launch_bounds__(1024) select_kernel(CompressArgs a, int small)
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// select for a prompt: the same keep / evict lists as select_kernel, from a cluster of C CTAs
+// per sequence (grid (C, n_seq), cluster (C, 1, 1), 1024 threads; C * 1024 * kSelPer >= S)
+// ------------------------------------------------------------------------------------------
+constexpr int kSelPer = 8;     // most tokens per thread of the prompt selection (keys in registers)
+constexpr int kSelTarget = 2;  // tokens per thread the cluster is sized for, up to 16 CTAs
+
+// Warp 0 finds the radix digit holding the kk-th largest key of a 256-bin histogram (bins in
+// ascending key order): misc[0] = digit, misc[1] = rank of the k-th largest inside the bin.
+__device__ __forceinline__ void radix_digit(const int* hist, int kk, int* misc) {
+  const int lane = threadIdx.x & 31;
+  int tot = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) tot += hist[255 - 8 * lane - j];
+  int inc = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  const int excl = inc - tot;
+  const unsigned hit = __ballot_sync(0xffffffffu, inc >= kk && excl < kk);
+  if (lane == __ffs(hit) - 1) {
+    int cum = excl, digit = 0;
+    for (int j = 0; j < 8; ++j) {
+      const int b = 255 - 8 * lane - j;
+      if (cum + hist[b] >= kk) {
+        digit = b;
+        break;
+      }
+      cum += hist[b];
+    }
+    misc[0] = digit;
+    misc[1] = kk - cum;
+  }
+}
+
+// Thread g = rank * 1024 + tid owns tokens [g * per, (g + 1) * per), per = ceil(S / (C * 1024)).
+// The top-n_top of the prefix is an exact MSB radix select over the order-preserving keys
+// (four 8-bit passes): each CTA builds its histogram with warp-aggregated shared atomics, and
+// after one cluster barrier every CTA sums the C histograms through distributed shared memory
+// and finds the same digit (histograms double-buffered, so a pass needs one cluster barrier).
+// The threshold key T and the number kk of tokens equal to T that are kept then fix every
+// position: with gt(p) / eq(p) the prefix tokens before p above / equal to T, the kept tokens
+// before p number gt(p) + min(kk, eq(p)) + (tail tokens before p) — ties go to the lower index
+// as in block_topk_flags — and the evicted ones min(p, prefix) - gt(p) - min(kk, eq(p)). One
+// block scan of (gt | eq << 16) per thread and one exchange of the CTA totals give them.
+// With `fused`, the token scores (token_score: pooled importance averaged over KV heads) are
+// computed here, CTA c scoring its own tokens [c * 1024 * per, (c + 1) * 1024 * per) with
+// coalesced loads into shared memory, from which each thread takes its range; otherwise they
+// come from token_kernel.
+__global__ void __launch_bounds__(1024) select_cluster_kernel(CompressArgs a, int fused) {
+  const hc_layer& L = a.L;
+  const int s = blockIdx.y, tid = threadIdx.x, C = gridDim.x, rank = blockIdx.x;
+  __shared__ int hist[2][256];
+  __shared__ int tot[256];
+  __shared__ int misc[2];
+  __shared__ int scan_sh[40];
+  __shared__ int pub;       // this CTA's packed (gt | eq << 16) count, read by the cluster
+  __shared__ int ctot[16];  // the C CTAs' packed counts
+  __shared__ float sTok[1024 * kSelPer];
+  pdl_wait();
+  const hc_seq_desc d = L.desc[s];
+  hc_seq_state* st = d.st;
+  const Plan pl = make_plan(L, d.budget, min(a.S_dense, a.S_max));
+  int* hdr = a.hdr + (size_t)s * 16;
+  const int g = rank * (int)blockDim.x + tid, nthr = C * (int)blockDim.x;
+  if (!pl.active) {
+    // a prompt within the budget is stored whole, in order (every CTA of the cluster returns
+    // here, before any cluster barrier)
+    const int S = min(pl.S, d.cap);
+    for (int t = g; t < S; t += nthr) a.keep_src[(size_t)s * a.S_max + t] = t;
+    for (int i = g; i < d.cap - S; i += nthr) d.hot_free[i] = d.cap - 1 - i;
+    if (g == 0) {
+      if (pl.S > d.cap) set_status(st, HC_DEV_CAPACITY);
+      hdr[4] = 1;
+      hdr[5] = S;
+      hdr[6] = 0;
+      st->n_hot = S;
+      st->n_free = d.cap - S;
+      st->n_evict = 0;
+    }
+    return;
+  }
+  const int S = pl.S, P = pl.prefix, K = pl.ntop;
+  const int per = (S + nthr - 1) / nthr;
+  const int r0 = min(S, g * per), r1 = min(S, r0 + per), npre = max(0, min(r1, P) - r0);
+  // ring state, read by every thread before the CTA of rank 0 updates it (after the count
+  // exchange's cluster barrier)
+  const int ccap = d.ccap, cold_head = st->cold_head, cold_count = st->cold_count;
+  uint32_t key[kSelPer];
+  if (fused) {
+    const int tqu = min(pl.nobs, a.tq);
+    const int c0 = min(S, rank * (int)blockDim.x * per), c1 = min(S, c0 + (int)blockDim.x * per);
+    for (int i = c0 + tid; i < c1; i += blockDim.x) sTok[i - c0] = token_score(a, s, tqu, S, i);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kSelPer; ++j) key[j] = j < npre ? fkey(sTok[tid * per + j]) : 0u;
+  } else {
+    const float* tok = a.tok + (size_t)s * a.S_max;
+#pragma unroll
+    for (int j = 0; j < kSelPer; ++j) key[j] = j < npre ? fkey(tok[r0 + j]) : 0u;
+  }
+  const bool all = K >= P, none = K <= 0;
+  uint32_t T = 0;
+  int kk = 0;
+  if (!all && !none) {
+    uint32_t pre = 0, mask = 0;
+    kk = K;
+    if (tid < 256) hist[0][tid] = 0;
+    __syncthreads();
+#pragma unroll 1
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      int* hb = hist[pass & 1];
+#pragma unroll
+      for (int j = 0; j < kSelPer; ++j) {
+        const bool live = j < npre && (key[j] & mask) == pre;
+        const unsigned act = __ballot_sync(0xffffffffu, live);
+        if (live) {
+          const uint32_t bin = (key[j] >> shift) & 255u;
+          const unsigned same = __match_any_sync(act, bin);
+          if ((tid & 31) == __ffs(same) - 1) atomicAdd(&hb[bin], __popc(same));
+        }
+      }
+      __syncthreads();
+      cluster_arrive();
+      cluster_wait();
+      // the other buffer was last read by the cluster in the previous pass, before every CTA
+      // arrived at the barrier just passed
+      if (tid < 256) {
+        hist[(pass + 1) & 1][tid] = 0;
+        int acc = 0;
+        for (int r = 0; r < C; ++r) acc += ld_cluster_s32(&hb[tid], (uint32_t)r);
+        tot[tid] = acc;
+      }
+      __syncthreads();
+      if (tid < 32) radix_digit(tot, kk, misc);
+      __syncthreads();
+      pre |= (uint32_t)misc[0] << shift;
+      mask |= 255u << shift;
+      kk = misc[1];
+    }
+    T = pre;
+  }
+  int ngt = 0, neq = 0;
+#pragma unroll
+  for (int j = 0; j < kSelPer; ++j) {
+    if (j < npre) {
+      ngt += all || (!none && key[j] > T);
+      neq += !all && !none && key[j] == T;
+    }
+  }
+  int ctotal;
+  const int before = block_exclusive_scan(ngt | (neq << 16), scan_sh, ctotal);
+  if (tid == 0) pub = ctotal;
+  cluster_arrive();
+  cluster_wait();
+  if (tid < C) ctot[tid] = ld_cluster_s32(&pub, (uint32_t)tid);
+  __syncthreads();
+  // every read of the cluster's shared memory is done: arrive now, wait before exiting
+  cluster_arrive_relaxed();
+  int gt_p = before & 0xffff, eq_p = before >> 16, gt_all = 0, eq_all = 0;
+  for (int r = 0; r < C; ++r) {
+    const int v = ctot[r];
+    if (r < rank) {
+      gt_p += v & 0xffff;
+      eq_p += v >> 16;
+    }
+    gt_all += v & 0xffff;
+    eq_all += v >> 16;
+  }
+  const int taken_all = gt_all + min(kk, eq_all);
+  const int n_evict_total = P - taken_all, kept = S - n_evict_total;
+  int kb = gt_p + min(kk, eq_p) + max(0, r0 - P);
+  int eb = min(r0, P) - gt_p - min(kk, eq_p);
+  int eqr = eq_p;
+#pragma unroll
+  for (int j = 0; j < kSelPer; ++j) {
+    const int i = r0 + j;
+    if (i < r1) {
+      bool keep = true;
+      if (j < npre) {
+        keep = all || (!none && key[j] > T);
+        if (!all && !none && key[j] == T) keep = eqr++ < kk;
+      }
+      if (keep) {
+        a.keep_src[(size_t)s * a.S_max + kb++] = i;
+      } else {
+        const int e = eb++;
+        a.ev_src[(size_t)s * a.S_max + e] = i;
+        // ring slot of the e-th evicted token; a batch larger than the ring keeps its last ccap
+        a.ev_dst[(size_t)s * a.S_max + e] =
+            (e >= n_evict_total - ccap) ? (int)(((long)cold_head + cold_count + e) % ccap) : -1;
+      }
+    }
+  }
+  for (int i = g; i < d.cap - kept; i += nthr) d.hot_free[i] = d.cap - 1 - i;
+  if (g == 0) {
+    const long total = (long)cold_count + n_evict_total;
+    int nh = cold_head, nc = (int)total;
+    if (total > ccap) {
+      nh = (int)(((long)cold_head + total - ccap) % ccap);
+      nc = ccap;
+    }
+    st->cold_head = nh;
+    st->cold_count = nc;
+    st->n_evict = n_evict_total;
+    st->n_hot = kept;
+    st->n_free = d.cap - kept;
+    hdr[0] = S;
+    hdr[4] = 1;
+    hdr[5] = kept;
+    hdr[6] = n_evict_total;
+  }
+  cluster_wait();
+}
+
 // Large evictions and the prompt store: kept tokens -> slab slots 0..n_keep-1 (prompt),
 // evicted tokens -> cold ring. Grid (blocks, n_seq), 8 warps per block, a warp per token.
 template <int DT, int D, bool DENSE>
@@ -1215,6 +1437,50 @@ CompressLayout compress_layout(const hc_layer& L, int S_max, int tq) {
   return c;
 }
 
+// Launch configuration of the prompt selection: a cluster of C CTAs per sequence.
+static cudaLaunchConfig_t select_cluster_config(cudaLaunchAttribute* attr, int C, int n_seq, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, n_seq);
+  cfg.blockDim = dim3(1024);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cfg;
+}
+
+// Whether the device holds a cluster of C CTAs of the prompt selection (clusters above 8 CTAs
+// are non-portable; checked once per device).
+static cudaError_t select_cluster_fits(int C, bool& fits) {
+  fits = true;
+  if (C <= 8) return cudaSuccess;
+  static std::mutex mu;
+  static int ok_dev[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  const int di = dev & 63;
+  if (ok_dev[di] == 0) {
+    e = cudaFuncSetAttribute(select_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    cudaLaunchAttribute attr[2];
+    const cudaLaunchConfig_t cfg = select_cluster_config(attr, C, 1, nullptr);
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, select_cluster_kernel, &cfg);
+    if (e != cudaSuccess) return e;
+    ok_dev[di] = clusters >= 1 ? 1 : -1;
+  }
+  fits = ok_dev[di] > 0;
+  return cudaSuccess;
+}
+
 template <int DT, int D, bool DENSE>
 static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cudaStream_t stream) {
   using T = typename Elem<DT>::T;
@@ -1260,6 +1526,31 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
     e = launch_pdl(sk, dim3(chunks, L.Hk, L.n_seq), dim3(128), smem, stream, a);
     if (e != cudaSuccess) return e;
   }
+  // A long prompt's selection runs on a cluster: up to 16k tokens one token per thread, the
+  // token scores computed by the cluster itself (their pooled loads are bound by each SM's L2
+  // bandwidth, so they gain only when spread that thin); longer prompts on up to 16 CTAs sized
+  // for kSelTarget tokens per thread, after token_kernel. Short prompts (scored in shared
+  // memory) and decode steps select on one CTA.
+  int C = 0, fused = 0;
+  if (DENSE && !small) {
+    C = 1;
+    if (S_grid <= 16 * 1024) {
+      while (C * 1024 < S_grid) C <<= 1;
+      fused = 1;
+    } else {
+      while (C < 16 && (long)C * 1024 * kSelTarget < S_grid) C <<= 1;
+    }
+    if (C > 8) {
+      bool fits = true;
+      e = select_cluster_fits(C, fits);
+      if (e != cudaSuccess) return e;
+      if (!fits) {
+        C = 8;
+        fused = 0;
+      }
+    }
+    if ((long)C * 1024 * kSelPer < S_grid) C = fused = 0;
+  }
   if (!small) {
     const int blocks = (int)((S_grid + 255) / 256) < 592 ? (S_grid + 255) / 256 : 592;
     if (snap && !tc) {
@@ -1269,14 +1560,23 @@ static cudaError_t compress_t(CompressArgs a, int S_grid, int n_evict_hint, cuda
       e = launch_pdl(imp_kernel<DENSE>, dim3(ib, L.n_seq), dim3(256), 0, stream, a);
       if (e != cudaSuccess) return e;
     }
-    e = launch_pdl(token_kernel<DENSE>, dim3(blocks > 0 ? blocks : 1, L.n_seq), dim3(256), 0, stream, a);
+    if (!fused) {
+      e = launch_pdl(token_kernel<DENSE>, dim3(blocks > 0 ? blocks : 1, L.n_seq), dim3(256), 0, stream, a);
+      if (e != cudaSuccess) return e;
+    }
+  }
+  if (C > 0) {
+    cudaLaunchAttribute attr[2];
+    const cudaLaunchConfig_t cfg = select_cluster_config(attr, C, L.n_seq, stream);
+    e = cudaLaunchKernelEx(&cfg, select_cluster_kernel, a, fused);
+    if (e != cudaSuccess) return e;
+  } else {
+    auto selk = select_kernel<DT, D, DENSE>;
+    e = ensure_smem(selk, kSelectSmemMax);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(selk, dim3(L.n_seq), dim3(1024), small ? sel_smem : 0, stream, a, small);
     if (e != cudaSuccess) return e;
   }
-  auto selk = select_kernel<DT, D, DENSE>;
-  e = ensure_smem(selk, kSelectSmemMax);
-  if (e != cudaSuccess) return e;
-  e = launch_pdl(selk, dim3(L.n_seq), dim3(1024), small ? sel_smem : 0, stream, a, small);
-  if (e != cudaSuccess) return e;
   if (DENSE || n_evict_hint > kInlineEvict) {
     const int items = DENSE ? S_grid : n_evict_hint;
     int blocks = (items + 7) / 8;
