@@ -27,7 +27,8 @@ def controller_kwargs(case):
                 cpu_buffer_size=c["ccap"], faiss_dim=c["faiss_dim"], normalize_for_ip=True,
                 window_size=c["window_size"], query_pool_size=c["pool"], lookahead_k=c["R"],
                 hold_retrieved=c["hold"], retrieve_after_prefill=c["rap"], policy=c["policy"],
-                pool_kernel=c.get("pool_kernel", 7), async_retrieval=c.get("async", False))
+                pool_kernel=c.get("pool_kernel", 7), pooling=c.get("pooling", "maxpool"),
+                async_retrieval=c.get("async", False))
 
 
 def run_cuda_layer(case, inputs, n_steps, device="cuda:0", model_cos=True, fused=True, chunks=None, searcher=None):

@@ -27,7 +27,8 @@ def oracle_kwargs(case):
     return dict(Hq=c["Hq"], Hk=c["Hk"], D=c["D"], dtype=c["dtype"],
                 inv_freq=synth.rope_inv_freq(c["D"], c["theta"]), attention_scaling=1.0,
                 policy=Policy(policy=c["policy"], cap=c["cap"], recent=c["recent"],
-                              topk_ratio=c["topk_ratio"], pool_kernel=c["pool_kernel"]),
+                              topk_ratio=c["topk_ratio"], pool_kernel=c["pool_kernel"],
+                              pooling=c.get("pooling", "maxpool")),
                 cpu_buffer_size=c["ccap"], faiss_dim=c["faiss_dim"], normalize_for_ip=True,
                 window_size=c["window_size"], query_pool_size=c["pool"], lookahead_k=c["R"],
                 hold_retrieved=c["hold"], retrieve_after_prefill=c["rap"],

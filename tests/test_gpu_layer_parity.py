@@ -259,21 +259,23 @@ def test_snapkv_prompt_scoring_tensor_cores(dtype, D, recent, T):
     assert res["ctrl"].device_status() == 0
 
 
-@pytest.mark.parametrize("T,ccap,ties", [(9000, 4096, False), (20000, 20000, True), (40000, 40000, False),
-                                         (70000, 70000, True)])
-def test_prompt_selection_cluster_sizes(T, ccap, ties):
+@pytest.mark.parametrize("T,ccap,ties,pooling", [(9000, 4096, False, "maxpool"), (9000, 9000, False, "avgpool"),
+                                                 (20000, 20000, True, "maxpool"), (40000, 40000, False, "maxpool"),
+                                                 (70000, 70000, True, "maxpool")])
+def test_prompt_selection_cluster_sizes(T, ccap, ties, pooling):
     """Long prompts, whose keep / evict lists come from a cluster of 16 CTAs: 9000 tokens, one
     per thread, the token scores computed by the cluster; 20000, 40000 and 70000 tokens, 2, 3
     and 5 per thread, after token_kernel (shorter prompts, on clusters of 1 to 8 CTAs, are the
     other tests' cases). Hot set, cold ring (9000 tokens into a ring of 4096: only the last 4096
-    evicted are stored) and one decode step against the oracle. With `ties`, every prefix key
-    but 64 is zero, so the top-k boundary falls inside one group of exactly equal scores that
-    spans every CTA of the cluster, and the lower positions are the ones kept."""
+    evicted are stored; once with average pooling) and one decode step against the oracle.
+    With `ties`, every prefix key but 64 is zero, so the top-k boundary falls inside one group
+    of exactly equal scores that spans every CTA of the cluster, and the lower positions are
+    the ones kept."""
     from hotcold_kv_cache_b200 import synth
     from cuda_runner import cold_positions, run_cuda_layer
     c = dict(B=1, Hq=8, Hk=2, D=128, T=T, steps=1, dtype="float16", policy="snapkv", cap=512, recent=32,
              topk_ratio=0.0, pool_kernel=7, ccap=ccap, faiss_dim=128, window_size=1 << 20, pool=4, R=16,
-             hold=True, rap=not ties, theta=500000.0, seed=5 + T)
+             hold=True, rap=not ties, theta=500000.0, seed=5 + T, pooling=pooling)
     inp = synth.layer_inputs(c["seed"], 1, 8, 2, 128, T, 1, "float16")
     if ties:
         live = np.zeros(T, bool)
