@@ -70,3 +70,54 @@ def test_oracle_chunked_prefill_one_chunk_is_prefill():
     assert a.dbg == b.dbg
     d, od, hd = O.run_layer(inp, 3, chunks=[0, 50, 120, 200], **oracle_kwargs(c))
     assert d.P.shape[1] == a.P.shape[1]  # the same budget is kept either way
+
+
+def test_token_ranges_partition_the_index():
+    """The ranks' token ranges of a cold index of n entries are contiguous, disjoint and cover
+    [0, n) in rank order, for every world size the benchmark runs."""
+    from hotcold_kv_cache_b200.shard import token_range
+    for n in (0, 1, 7, 256, 129033):
+        for world in range(1, 9):
+            spans = [token_range(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert all(lo <= hi for lo, hi in spans)
+
+
+def test_age_runs_map_ages_to_ring_slots():
+    """A range of ages on a ring (age 0 at slot `head`) split into runs of contiguous slots:
+    every age lands on slot (head + age) % ccap, in age order, in one run or two (the second
+    from slot 0 when the range crosses the ring's end)."""
+    from hotcold_kv_cache_b200.shard import age_runs
+    rng = np.random.default_rng(3)
+    for _ in range(500):
+        ccap = int(rng.integers(1, 64))
+        head = int(rng.integers(0, ccap))
+        lo = int(rng.integers(0, ccap + 1))
+        hi = int(rng.integers(lo, ccap + 1))
+        runs = age_runs(head, ccap, lo, hi)
+        ages = [a0 + i for _, c, a0 in runs for i in range(c)]
+        slots = [s0 + i for s0, c, _ in runs for i in range(c)]
+        assert ages == list(range(lo, hi))
+        assert slots == [(head + a) % ccap for a in ages]
+        assert len(runs) <= 2 and all(c > 0 for _, c, _ in runs)
+        if len(runs) == 2:
+            assert runs[1][0] == 0
+
+
+def test_sharded_search_refuses_lookahead_beyond_kernel_limits():
+    """hc_cold_topk keeps at most 256 per rank and hc_shard_merge at most 4096 candidates: the
+    sharded search refuses such a lookahead when it is attached, not at the first search."""
+    from hotcold_kv_cache_b200.shard import ShardedColdSearch
+    ShardedColdSearch(rank=0, world=8).check_k(256)
+    ShardedColdSearch(rank=0, world=16).check_k(256)
+    for world, k in ((1, 0), (1, 257), (17, 256), (32, 200)):
+        with pytest.raises(ValueError):
+            ShardedColdSearch(rank=0, world=world).check_k(k)
+    from hotcold_kv_cache_b200 import KVController
+    ctrl = KVController(lookahead_k=300)
+    with pytest.raises(ValueError):
+        ctrl.cold_search = ShardedColdSearch(rank=0, world=1)
+    ctrl = KVController(lookahead_k=256)
+    ctrl.cold_search = ShardedColdSearch(rank=0, world=16)
+    assert ctrl.cold_search is not None
