@@ -121,3 +121,26 @@ def test_sharded_search_refuses_lookahead_beyond_kernel_limits():
     ctrl = KVController(lookahead_k=256)
     ctrl.cold_search = ShardedColdSearch(rank=0, world=16)
     assert ctrl.cold_search is not None
+
+
+def test_oracle_retrieval_lag_attends_one_step_later():
+    """The oracle's schedule for async_retrieval (retrieval_lag=1): every decode-step search is
+    attended one step later than in the deterministic schedule (a search at the last step is
+    never attended), the same number of searches runs, and the steps before the first attended
+    search are identical in both."""
+    from golden_cases import oracle_kwargs
+    from oracle import hotcold_oracle as O
+    n = 30
+    c = dict(B=2, Hq=8, Hk=2, D=64, T=300, steps=n, dtype="float32", policy="snapkv", cap=64, recent=16,
+             topk_ratio=0.0, pool_kernel=7, ccap=1024, faiss_dim=64, window_size=8, pool=4, R=16, hold=True,
+             rap=False, theta=500000.0, seed=11)
+    inp = synth.layer_inputs(c["seed"], 2, 8, 2, 64, 300, n, "float32")
+    l0, o0, _ = O.run_layer(inp, n, **oracle_kwargs(c))
+    l1, o1, _ = O.run_layer(inp, n, **oracle_kwargs(dict(c, **{"async": True})))
+    s0 = [e["step"] for e in l0.events]
+    s1 = [e["step"] for e in l1.events]
+    assert len(s0) >= 3
+    assert s1 == [s + 1 for s in s0 if s + 1 <= n]
+    assert l0.dbg["retrieval_launched"] == l1.dbg["retrieval_launched"]
+    np.testing.assert_array_equal(o0[:s0[0] - 1], o1[:s0[0] - 1])
+    assert not np.array_equal(o0[s0[0] - 1], o1[s0[0] - 1])
