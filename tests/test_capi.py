@@ -1,14 +1,17 @@
 """CPU checks of the C ABI: the library loads without a GPU, exports every
 entry point include/hotcold_b200.h declares, the ctypes prototypes cover them,
-and the struct sizes agree with the header."""
+and the struct sizes agree with the header; nothing falls back to the host."""
 
 import ctypes
 import os
 import re
 
+import pytest
+
 from hotcold_kv_cache_b200 import _lib
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "hotcold_b200.h")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "hotcold_b200.h")
 
 
 def declared():
@@ -66,3 +69,29 @@ def test_argument_errors_are_reported_not_launched():
     assert rc == 3 and b"head_dim" in lib.hc_last_error()
     rc = lib.hc_shard_merge(None, None, 8, 1024, None, None, None)
     assert rc != 0
+
+
+def test_no_fallback_when_the_library_is_missing():
+    """The product path has no CPU or eager fallback: loading a library that is not there
+    raises, naming the build command."""
+    import subprocess
+    import sys
+    code = ("from hotcold_kv_cache_b200 import _lib\n"
+            "try:\n"
+            "    _lib.load('/nonexistent/libhotcold_b200.so')\n"
+            "except RuntimeError as e:\n"
+            "    print('raised:', e)\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "raised:" in r.stdout and "hotcold_kv_cache_b200.build" in r.stdout
+
+
+def test_drop_in_attention_refuses_cpu_tensors():
+    """triton_evict_attention_forward runs on CUDA tensors only, as the reference's asserts
+    require (kernels.py:87): CPU inputs are refused, never computed on the host."""
+    import torch
+    from hotcold_kv_cache_b200 import triton_evict_attention_forward
+    q = torch.zeros(1, 8, 1, 64, dtype=torch.float16)
+    k = torch.zeros(1, 2, 16, 64, dtype=torch.float16)
+    m = torch.ones(1, 16, dtype=torch.bool)
+    with pytest.raises(AssertionError):
+        triton_evict_attention_forward(q, k, k, m, 4, 0.125)
