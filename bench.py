@@ -166,11 +166,11 @@ def source_sha(name: str) -> str:
 
 
 def profiled_traffic(kernel: str, source: str):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu summary (profiles/traffic.md),
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary (profiles/traffic.txt),
     with where it comes from. DRAM counters cannot be read inside this run, so the figure is
     the one ncu measured; it is withheld (None) when the kernel's source file changed since
     that capture (the summary records the file's SHA-1)."""
-    path = os.path.join(ROOT, "profiles", "traffic.md")
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
     val = sha = None
     try:
         for line in open(path):
@@ -185,7 +185,7 @@ def profiled_traffic(kernel: str, source: str):
         return None, "no ncu figure for this kernel"
     if sha != now:
         return None, f"stale: {source} changed since the ncu capture (sha {sha} vs {now})"
-    return val, f"ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, profiles/traffic.md ({source} sha {now})"
+    return val, f"ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, profiles/traffic.txt ({source} sha {now})"
 
 
 # ------------------------------------------------------------------------------------------

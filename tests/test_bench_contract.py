@@ -41,3 +41,18 @@ def test_reference_arm_runs_on_rank_zero_only():
     rc, lines = _bench(["--impl", "reference", "--steps", "1", "--warmup", "1"],
                        env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert rc == 0 and lines == []
+
+
+def test_roofline_traffic_is_withheld_when_the_kernel_changed():
+    """roofline.traffic comes from the committed ncu figure only while the kernel's source still
+    has the SHA-1 recorded beside it; against another source it is reported stale (None)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    val, src = bench.profiled_traffic("step", "hc_step.cu")
+    assert val is not None and val > 0 and "hc_step.cu sha" in src
+    val, src = bench.profiled_traffic("step", "hc_attention.cu")
+    assert val is None and src.startswith("stale")
+    val, src = bench.profiled_traffic("no_such_kernel", "hc_step.cu")
+    assert val is None
